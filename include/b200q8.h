@@ -1,0 +1,196 @@
+/*
+ * b200q8.h -- C ABI of the B200 (sm_100a) Q8_0 hot path of synthesize.cpp.
+ *
+ * The reference reaches this arithmetic only through ggml's op set; each entry
+ * point below replaces one call that synthesize.cpp makes into ggml (the ggml
+ * submodule itself, pinned at 707321c4cf6d21cb4bc831aa8b687dbf01a521ce, is not
+ * vendored in the reference tree):
+ *
+ *   b200q8_mul_mat        ggml_mul_mat(Q8_0 W, F32 x) as executed by a backend:
+ *                         src/arch/qwen3-tts/operations.cpp:39-41,90-92,142,
+ *                         talker.cpp:45,48,184, code-predictor.cpp:56,79
+ *   b200q8_get_rows       ggml_get_rows(Q8_0 table, I32 ids): talker.cpp:44,86,
+ *                         code-predictor.cpp:31, model.cpp:1347,1449
+ *   b200q8_quantize_rows  quantize_row_q8_0_ref / ggml-cpu from_float for Q8_0
+ *   b200q8_quantize_chunk ggml_quantize_chunk(GGML_TYPE_Q8_0, ...):
+ *                         tools/synthesize-quantize/quantize.cpp:300-301
+ *   b200q8_dequantize_rows  type_traits(Q8_0)->to_float: quantize.cpp:67-83,
+ *                         tests/synthesize_quantize_test.cpp:273-276
+ *   b200q8_chain_*        the per-frame talker step that builds and computes
+ *                         those ops: talker.cpp:135-185 via model.cpp:101-126
+ *                         (GraphRun::run), operations.cpp:44-148
+ *
+ * Conventions (the same as ggml's for these ops):
+ *   - Q8_0 data are rows of K/32 blocks, each block an fp16 scale d followed by
+ *     32 int8 codes (34 bytes); K % 32 == 0 (quantize.cpp:239-242).
+ *   - A MUL_MAT weight W has ne = [K, N]: N rows of K/32 blocks, row n at
+ *     w + n*w_row_bytes.  Activations x have ne = [K, M]: token m at
+ *     x + m*x_col_stride bytes.  The result y has ne = [N, M].
+ *   - Every pointer passed to a compute entry point is a device pointer; work
+ *     is enqueued on the caller's CUDA stream and is asynchronous.  No compute
+ *     entry point allocates memory; the caller owns every buffer.
+ *   - Return values are synth_status_t codes (include/synthesize.h:34-55 in the
+ *     reference): B200Q8_OK on success, never an exception or abort across the
+ *     ABI.  b200q8_last_error() gives the message of the calling thread's last
+ *     failure.  Errors that only a kernel can see (an out-of-range row id, a
+ *     wait that ran out) are recorded in a per-device status word that
+ *     b200q8_device_status() reads.
+ */
+#ifndef B200Q8_H
+#define B200Q8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t b200q8_status_t;
+#define B200Q8_OK                ((b200q8_status_t) 0)  /* SYNTH_OK                    */
+#define B200Q8_ERR_INVALID_ARG   ((b200q8_status_t) 1)  /* SYNTH_ERR_INVALID_ARG       */
+#define B200Q8_ERR_UNSUPPORTED   ((b200q8_status_t) 8)  /* SYNTH_ERR_UNSUPPORTED_INPUT */
+#define B200Q8_ERR_OOM           ((b200q8_status_t) 16) /* SYNTH_ERR_OOM               */
+#define B200Q8_ERR_BACKEND       ((b200q8_status_t) 17) /* SYNTH_ERR_BACKEND           */
+#define B200Q8_ERR_INTERNAL      ((b200q8_status_t) 20) /* SYNTH_ERR_INTERNAL          */
+/* Recorded in the device status word by a kernel whose bounded wait ran out. */
+#define B200Q8_ERR_DEVICE_TIMEOUT ((b200q8_status_t) 21)
+
+/* Activation quantizer variants.  REF is quantize_row_q8_0_ref (what the
+ * packing tool uses, and ggml-cpu's portable path); CPU_X86 and CPU_ARM are
+ * the two SIMD forms of ggml-cpu's quantize_row_q8_0 (id = 127/amax with
+ * round-half-even, and id = 1/d with round-half-even). */
+#define B200Q8_QUANT_REF     0
+#define B200Q8_QUANT_CPU_X86 1
+#define B200Q8_QUANT_CPU_ARM 2
+
+#define B200Q8_QK8_0       32
+#define B200Q8_BLOCK_BYTES 34
+
+/* cudaStream_t without requiring the CUDA headers. NULL = legacy stream. */
+typedef struct CUstream_st * b200q8_stream_t;
+
+/* Library version, major*10000 + minor*100 + patch. */
+int32_t b200q8_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated
+ * to len) and returns its status code. */
+b200q8_status_t b200q8_last_error(char * buf, size_t len);
+
+/* Synchronises `device` and returns the status word its kernels recorded
+ * (B200Q8_OK if none); clear != 0 resets it.  Replaces ggml's GGML_ASSERT
+ * aborts for conditions only the device can check. */
+b200q8_status_t b200q8_device_status(int32_t device, int32_t clear);
+
+/* ---- packing and activation quantization (ggml_quantize_chunk,
+ *      quantize_row_q8_0_ref, ggml-cpu from_float) ------------------------- */
+
+/* rows x K floats (row r at x + r*x_row_stride bytes) -> rows of K/32 Q8_0
+ * blocks (row r at dst + r*dst_row_stride bytes).  mode: B200Q8_QUANT_*.
+ * Bit-exact with the reference for every input; for non-finite inputs the
+ * codes follow the reference on x86 (a non-finite x*id stores 0) and a NaN
+ * scale is stored as 0x7e00. */
+b200q8_status_t b200q8_quantize_rows(const float * x, int64_t rows, int64_t K, size_t x_row_stride, void * dst,
+                                     size_t dst_row_stride, int32_t mode, b200q8_stream_t stream);
+
+/* ggml_quantize_chunk(GGML_TYPE_Q8_0, src, dst, start, nrows, n_per_row, NULL)
+ * on device memory: quantizes nrows rows starting at element `start` (a
+ * multiple of n_per_row) of a dense src into the matching rows of a dense
+ * dst.  *written receives nrows * n_per_row/32 * 34, the value ggml returns. */
+b200q8_status_t b200q8_quantize_chunk(const float * src, void * dst, int64_t start, int64_t nrows,
+                                      int64_t n_per_row, size_t * written, b200q8_stream_t stream);
+
+/* Q8_0 rows -> F32 rows: out = q * fp32(d) (exact). */
+b200q8_status_t b200q8_dequantize_rows(const void * src, int64_t rows, int64_t K, size_t src_row_stride, float * dst,
+                                       size_t dst_row_stride, b200q8_stream_t stream);
+
+/* ---- GET_ROWS ----------------------------------------------------------- */
+
+/* out[i] = dequantize(table row ids[i]) for i < n_ids; K floats per output
+ * row at out + i*out_row_stride bytes.  An id outside [0, rows) zero-fills
+ * its output row and records B200Q8_ERR_INVALID_ARG in the device status
+ * word (ggml-cpu asserts instead). */
+b200q8_status_t b200q8_get_rows(const void * table, int64_t K, int64_t rows, size_t table_row_stride,
+                                const int32_t * ids, int64_t n_ids, float * out, size_t out_row_stride,
+                                b200q8_stream_t stream);
+
+/* ---- MUL_MAT ------------------------------------------------------------ */
+
+/* Bytes of caller-provided scratch b200q8_mul_mat needs for these sizes
+ * (0 when the fused decode path needs none). */
+size_t b200q8_mul_mat_workspace_size(int64_t K, int64_t N, int64_t M);
+
+/* y = W * quantize(x): y[m][n] = sum_b fp32(dw[n,b]) * fp32(dx[m,b]) * sum_i qw*qx,
+ * the arithmetic of ggml-cpu's vec_dot_q8_0_q8_0 after from_float.  Codes and
+ * scales of x are bit-exact with the reference quantizer `mode`; y agrees
+ * with the reference within 1e-5 * sum_b |dw*dx*isum_b| per element (only
+ * the fp32 summation order differs).  workspace may be NULL when
+ * b200q8_mul_mat_workspace_size() returns 0. */
+b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_row_bytes, const float * x, int64_t M,
+                               size_t x_col_stride, float * y, size_t y_col_stride, int32_t mode, void * workspace,
+                               size_t workspace_bytes, b200q8_stream_t stream);
+
+/* ---- the talker-shaped decode step -------------------------------------- */
+
+/* One decoder layer of the Qwen3 talker as the step chain sees it (ggml
+ * layouts, device pointers).  wq..wd are Q8_0 matrices with ne = [in, out];
+ * norm_in / norm_post are F32 [hidden] (input_layernorm, post_attn_norm). */
+typedef struct b200q8_layer {
+    const void *  wq;
+    const void *  wk;
+    const void *  wv;
+    const void *  wo;
+    const void *  wgate;
+    const void *  wup;
+    const void *  wdown;
+    const float * norm_in;
+    const float * norm_post;
+} b200q8_layer;
+
+typedef struct b200q8_chain_desc {
+    int32_t              n_layers;
+    int64_t              hidden;   /* 1024 for the 0.6B talker          */
+    int64_t              n_head;   /* 16                                */
+    int64_t              n_kv;     /* 8                                 */
+    int64_t              head_dim; /* 128                               */
+    int64_t              inter;    /* 3072                              */
+    float                eps;      /* rms_norm_eps                      */
+    int64_t              max_m;    /* largest token batch run() accepts */
+    int32_t              mode;     /* B200Q8_QUANT_*                    */
+    const b200q8_layer * layers;   /* n_layers entries, copied          */
+    const void *         table;    /* Q8_0 embedding [hidden, table_rows] */
+    int64_t              table_rows;
+} b200q8_chain_desc;
+
+typedef struct b200q8_chain b200q8_chain;
+
+/* Builds a step plan: packs each layer's q|k|v and gate|up weights into
+ * contiguous device copies (one allocation, at plan time), allocates the
+ * per-layer activation buffers, and prepares the launch sequence.  The only
+ * entry points that allocate are b200q8_chain_create and nothing else. */
+b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t device, b200q8_chain ** out);
+
+/* One decode step for M tokens (M <= max_m):
+ *   h = x_in + get_rows(table, ids); then per layer
+ *   h1 = h + Wo*Q(attend(Wq,Wk,Wv * Q(rms_norm(h)*norm_in)))
+ *   h  = h1 + Wd*Q(silu(Wg*Q(n)) * (Wu*Q(n))),  n = rms_norm(h1)*norm_post
+ * where attend is attention over a single cached position (query head j
+ * reads kv head j/(n_head/n_kv)).  ids [M] I32, x_in and h_out [M][hidden]
+ * F32, all device pointers. */
+b200q8_status_t b200q8_chain_run(b200q8_chain * chain, const int32_t * ids, const float * x_in, float * h_out,
+                                 int64_t M, b200q8_stream_t stream);
+
+/* Device pointer to one of layer l's activation buffers of the last run
+ * (which: 0 = normalised input, 1 = q|k|v, 2 = attention output, 3 = o,
+ * 4 = h1, 5 = normalised h1, 6 = gate|up, 7 = silu(gate)*up, 8 = down,
+ * 9 = h after the layer); row stride in floats via *stride. */
+b200q8_status_t b200q8_chain_buffer(b200q8_chain * chain, int32_t layer, int32_t which, float ** ptr,
+                                    int64_t * stride);
+
+void b200q8_chain_destroy(b200q8_chain * chain);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200Q8_H */

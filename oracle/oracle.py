@@ -1,0 +1,269 @@
+"""CPU oracle for the Q8_0 hot path -- TEST INFRASTRUCTURE ONLY.
+
+Two restatements of ggml's Q8_0 arithmetic as synthesize.cpp reaches it:
+
+* ``q8_oracle.c`` (loaded here through ctypes): packing
+  (``quantize_row_q8_0_ref``, reached from
+  tools/synthesize-quantize/quantize.cpp:300-301), the three activation
+  quantizer variants ggml-cpu's ``from_float`` may use, ``vec_dot_q8_0_q8_0``
+  / MUL_MAT (operations.cpp:39-41,90-92,142), GET_ROWS (talker.cpp:44,86,
+  code-predictor.cpp:31), the seeded normal stream (src/random-stream.cpp:10-48)
+  and the decode-step chain.
+* numpy / pure-Python versions of the packing and of the random stream,
+  used to cross-check the C code and small cases.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg import
+this module.  The product library never links or calls it.
+
+Pinning: packing is checked byte-for-byte against gguf-py 0.19.0
+(gguf/quants.py:378-394, rounding helper :43-47) through the fixtures in
+tests/golden/; the random stream and thread policy are checked against the
+reference's own sources compiled into oracle/_ref/ when that library exists.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "build", "libq8oracle.so")
+REF_LIB_PATH = os.path.join(HERE, "_ref", "libsynth_ref.so")
+
+QK = 32
+BLOCK_BYTES = 34
+QUANT_REF = 0
+QUANT_CPU_X86 = 1
+QUANT_CPU_ARM = 2
+
+_lib = None
+_ref = None
+
+
+def build(reference_root: str | None = None) -> None:
+    """Compile the oracle (and, when the reference tree exists, oracle/_ref)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    ref = reference_root or "/root/reference"
+    if os.path.isdir(os.path.join(ref, "src")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        c_void_p, c_int64, c_size_t, c_int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_size_t, ctypes.c_int
+        L.oracle_fp32_to_fp16.argtypes = [ctypes.c_float]
+        L.oracle_fp32_to_fp16.restype = ctypes.c_uint16
+        L.oracle_fp16_to_fp32.argtypes = [ctypes.c_uint16]
+        L.oracle_fp16_to_fp32.restype = ctypes.c_float
+        L.oracle_quantize_row_q8_0.argtypes = [c_void_p, c_void_p, c_int64, c_int]
+        L.oracle_quantize_chunk_q8_0.argtypes = [c_void_p, c_void_p, c_int64, c_int64, c_int64]
+        L.oracle_quantize_chunk_q8_0.restype = c_size_t
+        L.oracle_dequantize_row_q8_0.argtypes = [c_void_p, c_void_p, c_int64]
+        L.oracle_vec_dot_q8_0_q8_0.argtypes = [c_int64, c_void_p, c_void_p, c_void_p]
+        L.oracle_vec_dot_q8_0_q8_0.restype = ctypes.c_float
+        L.oracle_mul_mat_q8_0_f32.argtypes = [c_void_p, c_int64, c_int64, c_size_t, c_void_p, c_int64, c_size_t,
+                                              c_void_p, c_size_t, c_int, c_void_p, c_int]
+        L.oracle_mul_mat_q8_0_q8_0.argtypes = [c_void_p, c_int64, c_int64, c_size_t, c_void_p, c_int64,
+                                               c_void_p, c_size_t, c_void_p, c_int]
+        L.oracle_get_rows_q8_0.argtypes = [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p]
+        L.oracle_get_rows_q8_0.restype = c_int
+        L.oracle_normal_fill.argtypes = [ctypes.c_uint64, c_void_p, c_size_t]
+        L.oracle_uniform_fill.argtypes = [ctypes.c_uint64, c_void_p, c_size_t]
+        L.oracle_normal_fill_scaled.argtypes = [ctypes.c_uint64, ctypes.c_float, c_void_p, c_size_t]
+        L.oracle_default_synthesis_threads.argtypes = [c_int]
+        L.oracle_default_synthesis_threads.restype = c_int
+        L.oracle_max_threads.restype = c_int
+        L.oracle_decoder_chain.argtypes = [c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
+                                           ctypes.c_float, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
+                                           c_int, c_int]
+        _lib = L
+    return _lib
+
+
+def ref_lib() -> ctypes.CDLL | None:
+    """The reference's own random stream / thread policy, if oracle/_ref was built."""
+    global _ref
+    if _ref is None and os.path.exists(REF_LIB_PATH):
+        R = ctypes.CDLL(REF_LIB_PATH)
+        R.ref_normal_fill.argtypes = [ctypes.c_uint64, ctypes.c_void_p, ctypes.c_size_t]
+        R.ref_uniform_fill.argtypes = [ctypes.c_uint64, ctypes.c_void_p, ctypes.c_size_t]
+        R.ref_default_synthesis_threads.restype = ctypes.c_int
+        R.ref_available_cpu_parallelism.restype = ctypes.c_int
+        _ref = R
+    return _ref
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def row_bytes(k: int) -> int:
+    return k // QK * BLOCK_BYTES
+
+
+# ------------------------------------------------------------------ C wrappers
+
+def quantize_rows(x: np.ndarray, mode: int = QUANT_REF) -> np.ndarray:
+    """x: float32 [rows, K] -> uint8 [rows, K/32*34] (ggml block_q8_0 rows)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, k = x.reshape(-1, x.shape[-1]).shape
+    out = np.empty((rows, row_bytes(k)), dtype=np.uint8)
+    L = lib()
+    xr = x.reshape(rows, k)
+    for r in range(rows):
+        L.oracle_quantize_row_q8_0(_ptr(xr[r]), _ptr(out[r]), k, mode)
+    return out
+
+
+def quantize_chunk(src: np.ndarray, start: int, nrows: int, n_per_row: int) -> tuple[np.ndarray, int]:
+    """ggml_quantize_chunk(Q8_0, ...) on a flat float32 buffer; returns (dst, bytes written)."""
+    src = np.ascontiguousarray(src, dtype=np.float32).ravel()
+    total_rows = src.size // n_per_row
+    dst = np.zeros(total_rows * row_bytes(n_per_row), dtype=np.uint8)
+    n = lib().oracle_quantize_chunk_q8_0(_ptr(src), _ptr(dst), start, nrows, n_per_row)
+    return dst, n
+
+
+def dequantize_rows(q: np.ndarray, k: int) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.uint8).reshape(-1, row_bytes(k))
+    out = np.empty((q.shape[0], k), dtype=np.float32)
+    L = lib()
+    for r in range(q.shape[0]):
+        L.oracle_dequantize_row_q8_0(_ptr(q[r]), _ptr(out[r]), k)
+    return out
+
+
+def mul_mat(w_q: np.ndarray, k: int, x: np.ndarray, mode: int = QUANT_REF, threads: int = 0,
+            want_bound: bool = True):
+    """ggml_mul_mat(W Q8_0 [N rows], x F32 [M, K]) -> (y [M, N], bound [M, N])."""
+    w_q = np.ascontiguousarray(w_q, dtype=np.uint8)
+    n = w_q.shape[0]
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
+    m = x.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    bound = np.empty((m, n), dtype=np.float64) if want_bound else None
+    lib().oracle_mul_mat_q8_0_f32(_ptr(w_q), k, n, w_q.shape[1], _ptr(x), m, k * 4, _ptr(y), n * 4, mode,
+                                  _ptr(bound) if bound is not None else None, threads)
+    return y, bound
+
+
+def mul_mat_q8(w_q: np.ndarray, k: int, xq: np.ndarray, threads: int = 0):
+    """MUL_MAT with already-quantized activations xq [M, K/32*34]."""
+    w_q = np.ascontiguousarray(w_q, dtype=np.uint8)
+    xq = np.ascontiguousarray(xq, dtype=np.uint8).reshape(-1, row_bytes(k))
+    n, m = w_q.shape[0], xq.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    bound = np.empty((m, n), dtype=np.float64)
+    lib().oracle_mul_mat_q8_0_q8_0(_ptr(w_q), k, n, w_q.shape[1], _ptr(xq), m, _ptr(y), n * 4, _ptr(bound), threads)
+    return y, bound
+
+
+def get_rows(table_q: np.ndarray, k: int, ids: np.ndarray) -> tuple[np.ndarray, int]:
+    table_q = np.ascontiguousarray(table_q, dtype=np.uint8)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    out = np.empty((ids.size, k), dtype=np.float32)
+    st = lib().oracle_get_rows_q8_0(_ptr(table_q), k, table_q.shape[0], _ptr(ids), ids.size, _ptr(out))
+    return out, st
+
+
+def normal(seed: int, count: int, scale: float | None = None) -> np.ndarray:
+    out = np.empty(count, dtype=np.float32)
+    if scale is None:
+        lib().oracle_normal_fill(seed, _ptr(out), count)
+    else:
+        lib().oracle_normal_fill_scaled(seed, scale, _ptr(out), count)
+    return out
+
+
+def uniform(seed: int, count: int) -> np.ndarray:
+    out = np.empty(count, dtype=np.float32)
+    lib().oracle_uniform_fill(seed, _ptr(out), count)
+    return out
+
+
+def default_synthesis_threads(available: int) -> int:
+    return lib().oracle_default_synthesis_threads(available)
+
+
+def decoder_chain(weights_q, norms: np.ndarray, table_q: np.ndarray, ids: np.ndarray, x_in: np.ndarray, *,
+                  hidden: int, n_head: int, n_kv: int, head_dim: int, inter: int, eps: float = 1e-6,
+                  mode: int = QUANT_REF, threads: int = 0) -> np.ndarray:
+    """The decode-step chain; weights_q: list of n_layers*7 uint8 arrays (q,k,v,o,gate,up,down)."""
+    n_layers = len(weights_q) // 7
+    ptrs = (ctypes.c_void_p * len(weights_q))(*[_ptr(np.ascontiguousarray(w)) for w in weights_q])
+    norms = np.ascontiguousarray(norms, dtype=np.float32)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    x_in = np.ascontiguousarray(x_in, dtype=np.float32).reshape(-1, hidden)
+    m = x_in.shape[0]
+    h = np.empty((m, hidden), dtype=np.float32)
+    lib().oracle_decoder_chain(n_layers, ptrs, _ptr(norms), hidden, n_head, n_kv, head_dim, inter, eps,
+                               _ptr(table_q), table_q.shape[0], _ptr(ids), _ptr(x_in), m, _ptr(h), mode, threads)
+    return h
+
+
+# ---------------------------------------------------- numpy / Python restatements
+
+def np_roundf(v: np.ndarray) -> np.ndarray:
+    """Round half away from zero (C roundf), in float32."""
+    a = np.abs(v)
+    f = np.floor(a)
+    r = f + (a - f >= np.float32(0.5)).astype(np.float32)
+    return np.copysign(r, v).astype(np.float32)
+
+
+def quantize_rows_np(x: np.ndarray) -> np.ndarray:
+    """numpy restatement of quantize_row_q8_0_ref for finite inputs."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, k = x.reshape(-1, x.shape[-1]).shape
+    blocks = x.reshape(-1, QK)
+    amax = np.abs(blocks).max(axis=1, keepdims=True)
+    d = (amax / np.float32(127)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        idv = np.where(d == 0, np.float32(0), np.float32(1) / d).astype(np.float32)
+    q = np_roundf((blocks * idv).astype(np.float32)).astype(np.int8)
+    out = np.concatenate([d.astype(np.float16).view(np.uint8), q.view(np.uint8)], axis=1)
+    return out.reshape(rows, row_bytes(k))
+
+
+class PyNormalStream:
+    """Pure-Python restatement of synth::NormalRandomStream (src/random-stream.cpp:10-48)."""
+
+    M64 = (1 << 64) - 1
+
+    def __init__(self, seed: int):
+        self.state = seed & self.M64
+        self.spare = None
+
+    def next_u64(self) -> int:
+        self.state = (self.state + 0x9E3779B97F4A7C15) & self.M64
+        v = self.state
+        v = ((v ^ (v >> 30)) * 0xBF58476D1CE4E5B9) & self.M64
+        v = ((v ^ (v >> 27)) * 0x94D049BB133111EB) & self.M64
+        return v ^ (v >> 31)
+
+    def uniform_open(self) -> float:
+        return ((self.next_u64() >> 11) + 0.5) * (1.0 / 9007199254740992.0)
+
+    def next(self) -> float:
+        if self.spare is not None:
+            s, self.spare = self.spare, None
+            return s
+        while True:
+            first = 2.0 * self.uniform_open() - 1.0
+            second = 2.0 * self.uniform_open() - 1.0
+            radius = first * first + second * second
+            if not (radius >= 1.0 or radius == 0.0):
+                break
+        scale = math.sqrt(-2.0 * math.log(radius) / radius)
+        self.spare = float(np.float32(second * scale))
+        return float(np.float32(first * scale))
+
+    def fill(self, count: int) -> np.ndarray:
+        return np.array([self.next() for _ in range(count)], dtype=np.float32)

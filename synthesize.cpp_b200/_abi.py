@@ -1,0 +1,104 @@
+"""ctypes binding of libb200q8.so (include/b200q8.h).
+
+The product path: every call goes through the C ABI into the sm_100a kernels.
+There is no fallback: if the library is missing or cannot be loaded, calls
+raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+LIB_PATH = os.path.join(PKG, "libb200q8.so")
+HEADER = os.path.join(ROOT, "include", "b200q8.h")
+
+OK = 0
+ERR_INVALID_ARG = 1
+ERR_UNSUPPORTED = 8
+ERR_OOM = 16
+ERR_BACKEND = 17
+ERR_INTERNAL = 20
+ERR_DEVICE_TIMEOUT = 21
+
+QUANT_REF = 0
+QUANT_CPU_X86 = 1
+QUANT_CPU_ARM = 2
+
+_lib: ctypes.CDLL | None = None
+
+
+class B200Q8Error(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"b200q8 status {status}: {message}")
+        self.status = status
+
+
+class Layer(ctypes.Structure):
+    _fields_ = [("wq", ctypes.c_void_p), ("wk", ctypes.c_void_p), ("wv", ctypes.c_void_p),
+                ("wo", ctypes.c_void_p), ("wgate", ctypes.c_void_p), ("wup", ctypes.c_void_p),
+                ("wdown", ctypes.c_void_p), ("norm_in", ctypes.c_void_p), ("norm_post", ctypes.c_void_p)]
+
+
+class ChainDesc(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int32), ("hidden", ctypes.c_int64), ("n_head", ctypes.c_int64),
+                ("n_kv", ctypes.c_int64), ("head_dim", ctypes.c_int64), ("inter", ctypes.c_int64),
+                ("eps", ctypes.c_float), ("max_m", ctypes.c_int64), ("mode", ctypes.c_int32),
+                ("layers", ctypes.POINTER(Layer)), ("table", ctypes.c_void_p), ("table_rows", ctypes.c_int64)]
+
+
+def header_symbols() -> list[str]:
+    """Every function the public header declares."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\S[^\n;]*?\b(b200q8_\w+)\s*\(", text, flags=re.M)))
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is not built: run __graft_entry__.build() (no CPU fallback exists)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+    L.b200q8_version.restype = i32
+    L.b200q8_last_error.argtypes = [ctypes.c_char_p, sz]
+    L.b200q8_last_error.restype = i32
+    L.b200q8_device_status.argtypes = [i32, i32]
+    L.b200q8_device_status.restype = i32
+    L.b200q8_quantize_rows.argtypes = [vp, i64, i64, sz, vp, sz, i32, vp]
+    L.b200q8_quantize_rows.restype = i32
+    L.b200q8_quantize_chunk.argtypes = [vp, vp, i64, i64, i64, ctypes.POINTER(sz), vp]
+    L.b200q8_quantize_chunk.restype = i32
+    L.b200q8_dequantize_rows.argtypes = [vp, i64, i64, sz, vp, sz, vp]
+    L.b200q8_dequantize_rows.restype = i32
+    L.b200q8_get_rows.argtypes = [vp, i64, i64, sz, vp, i64, vp, sz, vp]
+    L.b200q8_get_rows.restype = i32
+    L.b200q8_mul_mat_workspace_size.argtypes = [i64, i64, i64]
+    L.b200q8_mul_mat_workspace_size.restype = sz
+    L.b200q8_mul_mat.argtypes = [vp, i64, i64, sz, vp, i64, sz, vp, sz, i32, vp, sz, vp]
+    L.b200q8_mul_mat.restype = i32
+    L.b200q8_chain_create.argtypes = [ctypes.POINTER(ChainDesc), i32, ctypes.POINTER(vp)]
+    L.b200q8_chain_create.restype = i32
+    L.b200q8_chain_run.argtypes = [vp, vp, vp, vp, i64, vp]
+    L.b200q8_chain_run.restype = i32
+    L.b200q8_chain_buffer.argtypes = [vp, i32, i32, ctypes.POINTER(vp), ctypes.POINTER(i64)]
+    L.b200q8_chain_buffer.restype = i32
+    L.b200q8_chain_destroy.argtypes = [vp]
+    L.b200q8_chain_destroy.restype = None
+    _lib = L
+    return L
+
+
+def last_error() -> tuple[int, str]:
+    buf = ctypes.create_string_buffer(1024)
+    code = lib().b200q8_last_error(buf, len(buf))
+    return code, buf.value.decode(errors="replace")
+
+
+def check(status: int) -> None:
+    if status != OK:
+        _, msg = last_error()
+        raise B200Q8Error(status, msg)

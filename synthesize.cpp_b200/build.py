@@ -1,0 +1,70 @@
+"""Build recipe for the in-tree native libraries of the Q8_0 hot path.
+
+    libb200q8.so       the CUDA kernels + C ABI (include/b200q8.h), sm_100a only
+    libb200q8_host.so  host C++: seeded input streams, thread policy and the
+                       ggml-seam shim over that ABI (host/*.cpp)
+
+Both are written next to this file so they travel with the source tree.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+HOST = os.path.join(PKG, "host")
+LIB = os.path.join(PKG, "libb200q8.so")
+HOST_LIB = os.path.join(PKG, "libb200q8_host.so")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo", "-O3", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-shared",
+]
+
+
+def _nvcc() -> str:
+    for cand in (shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found: the B200 library cannot be built")
+
+
+def _sources(d: str, exts: tuple[str, ...]) -> list[str]:
+    return sorted(os.path.join(d, f) for f in os.listdir(d) if f.endswith(exts))
+
+
+def _stale(target: str, deps: list[str]) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> list[str]:
+    """Compile what is out of date; returns the built library paths."""
+    include = os.path.join(ROOT, "include")
+    deps = _sources(CSRC, (".cu", ".cuh", ".h")) + _sources(include, (".h",))
+    if force or _stale(LIB, deps):
+        cmd = [_nvcc(), *NVCC_FLAGS, "-o", LIB, os.path.join(CSRC, "libb200q8.cu")]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+        subprocess.run(cmd, check=True)
+    out = [LIB]
+    host_srcs = _sources(HOST, (".cpp",))
+    if host_srcs:
+        host_deps = host_srcs + _sources(HOST, (".h",)) + _sources(include, (".h",)) + [LIB]
+        if force or _stale(HOST_LIB, host_deps):
+            cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-pthread", f"-I{include}", "-o", HOST_LIB,
+                   *host_srcs, f"-L{PKG}", "-lb200q8", "-Wl,-rpath,$ORIGIN"]
+            subprocess.run(cmd, check=True)
+        out.append(HOST_LIB)
+    return out
+
+
+if __name__ == "__main__":
+    for p in build(force=True, verbose=True):
+        print(p)

@@ -1,0 +1,67 @@
+"""The talker-shaped decode step (b200q8_chain_*) from Python.
+
+Mirrors the caller side of the reference's per-frame talker step
+(src/arch/qwen3-tts/talker.cpp:135-185 build_talker_step, computed through
+model.cpp:101-126 GraphRun::run): weights stay resident on the device, each
+run() is one step for M tokens.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._abi import ChainDesc, Layer, check, lib
+from .q8 import QUANT_REF, stream_ptr
+
+BUFFERS = {"n1": 0, "qkv": 1, "attn": 2, "o": 3, "h1": 4, "n2": 5, "gu": 6, "s": 7, "down": 8, "h": 9}
+
+
+class DecodeChain:
+    """layers: list of dicts with torch CUDA tensors wq, wk, wv, wo, wgate, wup, wdown (uint8 Q8_0 rows) and
+    norm_in, norm_post (float32 [hidden]); table: uint8 Q8_0 [table_rows, hidden/32*34]."""
+
+    def __init__(self, layers, table: torch.Tensor, *, hidden: int, n_head: int, n_kv: int, head_dim: int,
+                 inter: int, eps: float = 1e-6, max_m: int = 8, mode: int = QUANT_REF):
+        self._keep = (layers, table)
+        arr = (Layer * len(layers))()
+        for i, L in enumerate(layers):
+            arr[i] = Layer(*[L[k].data_ptr() for k in ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown",
+                                                       "norm_in", "norm_post")])
+        self._arr = arr
+        desc = ChainDesc(len(layers), hidden, n_head, n_kv, head_dim, inter, eps, max_m, mode,
+                         ctypes.cast(arr, ctypes.POINTER(Layer)), table.data_ptr(), table.shape[0])
+        handle = ctypes.c_void_p()
+        check(lib().b200q8_chain_create(ctypes.byref(desc), table.device.index or 0, ctypes.byref(handle)))
+        self._h = handle
+        self.hidden = hidden
+        self.n_layers = len(layers)
+        self.device = table.device
+
+    def run(self, ids: torch.Tensor, x_in: torch.Tensor, h_out: torch.Tensor) -> torch.Tensor:
+        m = ids.numel()
+        check(lib().b200q8_chain_run(self._h, ids.data_ptr(), x_in.data_ptr(), h_out.data_ptr(), m, stream_ptr()))
+        return h_out
+
+    def buffer(self, layer: int, name: str, m: int) -> torch.Tensor:
+        """A copy of one activation buffer of the last run, [m, width] float32 on the device."""
+        ptr = ctypes.c_void_p()
+        stride = ctypes.c_int64()
+        check(lib().b200q8_chain_buffer(self._h, layer, BUFFERS[name], ctypes.byref(ptr), ctypes.byref(stride)))
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (m, stride.value), "typestr": "<f4", "data": (ptr.value, False),
+                                        "version": 3, "strides": None}
+
+        return torch.as_tensor(_View(), device=self.device).clone()
+
+    def close(self) -> None:
+        if self._h:
+            lib().b200q8_chain_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,366 @@
+// chain.cu -- the talker-shaped decode step as one replayable launch sequence.
+//
+// The reference rebuilds and computes a ggml graph per frame on the CPU
+// (src/arch/qwen3-tts/model.cpp:101-126 GraphRun::run, talker.cpp:135-185,
+// operations.cpp:44-148).  Here the step is a fixed sequence of kernels:
+//
+//   embed: h = x_in + get_rows(table, ids)
+//   per layer:  qkv  = W_qkv * Q(rms_norm(h) * norm_in)      (one GEMV, 4096 rows)
+//               h1   = h + W_o * Q(attend(v))                (GEMV + residual)
+//               gu   = W_gu * Q(rms_norm(h1) * norm_post)    (one GEMV, 6144 rows)
+//               h    = h1 + W_d * Q(silu(g) * u)             (GEMV + residual)
+//
+// where attend is attention over a single cached position: the softmax of
+// one score is 1, so query head j reads kv head j / (n_head / n_kv).  The
+// norms, the GQA expansion and SwiGLU are folded into the prologue of the
+// GEMV that consumes them, the residual adds into its epilogue, so the step
+// is 1 + 4 * n_layers kernels.  They are launched with programmatic
+// dependent launch (each GEMV streams its weights into shared memory before
+// waiting on its predecessor) and captured once per (M, pointer set) into a
+// CUDA graph that run() replays.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <algorithm>
+#include <new>
+#include <vector>
+
+namespace b200q8 {
+b200q8_status_t set_error(b200q8_status_t code, const char * fmt, ...);
+b200q8_status_t cuda_error(cudaError_t e, const char * what);
+int             current_sm_count();
+
+namespace {
+
+__global__ void embed_add_kernel(const uint8_t * __restrict__ table, size_t table_stride, int64_t table_rows,
+                                 const int32_t * __restrict__ ids, const float * __restrict__ x_in,
+                                 float * __restrict__ h, int64_t M, int64_t H) {
+    const int64_t total = M * H;
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t) gridDim.x * blockDim.x) {
+        const int64_t m = i / H;
+        const int64_t k = i % H;
+        const int64_t r = ids[m];
+        float         e = 0.0f;
+        if (r < 0 || r >= table_rows) {
+            if (k == 0) {
+                record_device_error((unsigned) B200Q8_ERR_INVALID_ARG);
+            }
+        } else {
+            const uint8_t * blk = table + r * table_stride + (k / kQK) * kBlockBytes;
+            const float     d   = __half2float(__ushort_as_half((unsigned short) (blk[0] | (blk[1] << 8))));
+            e                   = __fmul_rn((float) (int8_t) blk[2 + k % kQK], d);
+        }
+        h[i] = __fadd_rn(x_in[i], e);
+    }
+}
+
+enum Buf : int {
+    kN1 = 0, kQkv, kAttn, kO, kH1, kN2, kGu, kS, kDown, kHout, kNumBufs
+};
+
+}  // namespace
+}  // namespace b200q8
+
+using namespace b200q8;
+
+struct b200q8_chain {
+    int                          device = 0;
+    b200q8_chain_desc            d      = {};
+    std::vector<b200q8_layer>    layers;
+    std::vector<void *>          owned;  // device allocations to free
+    std::vector<const uint8_t *> w_qkv, w_o, w_gu, w_d;
+    size_t                       rb_h = 0, rb_q = 0, rb_i = 0;
+    int64_t                      qkv_dim = 0;
+    float *                      act     = nullptr;  // per-layer activation buffers
+    size_t                       buf_off[kNumBufs] = {};
+    size_t                       buf_stride[kNumBufs] = {};
+    size_t                       layer_floats = 0;
+    float *                      h0           = nullptr;
+    cudaStream_t                 cap_stream   = nullptr;
+    int                          sms          = 148;
+
+    struct Graph {
+        int64_t         M;
+        const void *    ids;
+        const void *    x;
+        void *          h;
+        cudaGraphExec_t exec;
+    };
+    std::vector<Graph> graphs;
+
+    float * buf(int layer, int which) { return act + (size_t) layer * layer_floats + buf_off[which]; }
+};
+
+namespace {
+
+void chain_free(b200q8_chain * c) {
+    if (c == nullptr) {
+        return;
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(c->device);
+    for (auto & g : c->graphs) {
+        cudaGraphExecDestroy(g.exec);
+    }
+    for (void * p : c->owned) {
+        cudaFree(p);
+    }
+    if (c->cap_stream) {
+        cudaStreamDestroy(c->cap_stream);
+    }
+    cudaSetDevice(prev);
+    delete c;
+}
+
+// Returns a contiguous copy base for [a | b | c] row blocks, or a if they are
+// already contiguous (no copy).
+const uint8_t * contiguous(b200q8_chain * c, const void * a, size_t a_bytes, const void * b, size_t b_bytes,
+                           const void * e, size_t e_bytes, cudaError_t & err) {
+    const uint8_t * pa = static_cast<const uint8_t *>(a);
+    if (pa + a_bytes == b && (e == nullptr || static_cast<const uint8_t *>(b) + b_bytes == e)) {
+        return pa;
+    }
+    void * dst = nullptr;
+    err        = cudaMalloc(&dst, a_bytes + b_bytes + e_bytes);
+    if (err != cudaSuccess) {
+        return nullptr;
+    }
+    c->owned.push_back(dst);
+    uint8_t * o = static_cast<uint8_t *>(dst);
+    err         = cudaMemcpy(o, a, a_bytes, cudaMemcpyDeviceToDevice);
+    if (err == cudaSuccess) {
+        err = cudaMemcpy(o + a_bytes, b, b_bytes, cudaMemcpyDeviceToDevice);
+    }
+    if (err == cudaSuccess && e != nullptr) {
+        err = cudaMemcpy(o + a_bytes + b_bytes, e, e_bytes, cudaMemcpyDeviceToDevice);
+    }
+    return o;
+}
+
+cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, int64_t M, const int32_t * ids, const float * x_in,
+                         float * h_out) {
+    const b200q8_chain_desc & d = c->d;
+    const int64_t H = d.hidden, Q = d.n_head * d.head_dim, KV = d.n_kv * d.head_dim, I = d.inter;
+    {
+        const int64_t total = M * H;
+        const int     grid  = (int) std::min<int64_t>((total + 255) / 256, (int64_t) c->sms * 4);
+        embed_add_kernel<<<grid, 256, 0, st>>>(static_cast<const uint8_t *>(d.table), (size_t) c->rb_h,
+                                                d.table_rows, ids, x_in, c->h0, M, H);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            return e;
+        }
+    }
+    for (int64_t m0 = 0; m0 < M; m0 += 8) {
+        const int   mc = (int) std::min<int64_t>(M - m0, 8);
+        const float * h = c->h0 + m0 * H;
+        for (int l = 0; l < d.n_layers; ++l) {
+            const bool last = l == d.n_layers - 1;
+            auto       B    = [&](int which) { return c->buf(l, which) + m0 * c->buf_stride[which]; };
+            GemvParams p    = {};
+            p.M             = mc;
+            p.mode          = d.mode;
+            p.eps           = d.eps;
+            // qkv = W_qkv * Q(rms_norm(h) * norm_in)
+            p.w = c->w_qkv[l]; p.row_bytes = c->rb_h; p.K = (int) H; p.N = (int) c->qkv_dim;
+            p.pro = kProRmsNorm; p.x = h; p.x_stride = (size_t) H; p.norm_w = c->layers[l].norm_in;
+            p.pro_out = B(kN1); p.pro_out_stride = (size_t) H;
+            p.y = B(kQkv); p.y_stride = (size_t) c->qkv_dim; p.res = nullptr; p.y_res = nullptr;
+            cudaError_t e = launch_gemv(p, st, c->sms, true);
+            if (e != cudaSuccess) return e;
+            // h1 = h + W_o * Q(attend(v))
+            p.w = c->w_o[l]; p.row_bytes = c->rb_q; p.K = (int) Q; p.N = (int) H;
+            p.pro = kProGqa; p.x = B(kQkv) + Q + KV; p.x_stride = (size_t) c->qkv_dim;
+            p.head_dim = (int) d.head_dim; p.group = (int) (d.n_head / d.n_kv);
+            p.pro_out = B(kAttn); p.pro_out_stride = (size_t) Q;
+            p.y = B(kO); p.y_stride = (size_t) H; p.res = h; p.y_res = B(kH1); p.res_stride = (size_t) H;
+            e = launch_gemv(p, st, c->sms, true);
+            if (e != cudaSuccess) return e;
+            // gu = W_gu * Q(rms_norm(h1) * norm_post)
+            p.w = c->w_gu[l]; p.row_bytes = c->rb_h; p.K = (int) H; p.N = (int) (2 * I);
+            p.pro = kProRmsNorm; p.x = B(kH1); p.x_stride = (size_t) H; p.norm_w = c->layers[l].norm_post;
+            p.pro_out = B(kN2); p.pro_out_stride = (size_t) H;
+            p.y = B(kGu); p.y_stride = (size_t) (2 * I); p.res = nullptr; p.y_res = nullptr;
+            e = launch_gemv(p, st, c->sms, true);
+            if (e != cudaSuccess) return e;
+            // h = h1 + W_d * Q(silu(g) * u)
+            p.w = c->w_d[l]; p.row_bytes = c->rb_i; p.K = (int) I; p.N = (int) H;
+            p.pro = kProSwiGlu; p.x = B(kGu); p.x2 = B(kGu) + I; p.x_stride = (size_t) (2 * I);
+            p.pro_out = B(kS); p.pro_out_stride = (size_t) I;
+            p.y = B(kDown); p.y_stride = (size_t) H; p.res = B(kH1); p.res_stride = (size_t) H;
+            p.y_res = last ? h_out + m0 * H : B(kHout);
+            e = launch_gemv(p, st, c->sms, true);
+            if (e != cudaSuccess) return e;
+            h = p.y_res;
+        }
+    }
+    return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" {
+
+b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t device, b200q8_chain ** out) {
+    if (out == nullptr || desc == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_create: null argument");
+    }
+    *out                = nullptr;
+    const b200q8_chain_desc & d = *desc;
+    if (d.n_layers < 1 || d.layers == nullptr || d.table == nullptr || d.hidden <= 0 || d.hidden % 256 != 0 ||
+        d.inter % 256 != 0 || d.n_head <= 0 || d.n_kv <= 0 || d.n_head % d.n_kv != 0 || d.head_dim <= 0 ||
+        (d.n_head * d.head_dim) % 256 != 0 || d.max_m < 1 || d.table_rows < 1 ||
+        (d.mode != B200Q8_QUANT_REF && d.mode != B200Q8_QUANT_CPU_X86 && d.mode != B200Q8_QUANT_CPU_ARM)) {
+        return set_error(B200Q8_ERR_INVALID_ARG,
+                         "chain_create: bad shape (hidden, inter and n_head*head_dim must be multiples of 256)");
+    }
+    for (int l = 0; l < d.n_layers; ++l) {
+        const b200q8_layer & L = d.layers[l];
+        if (!L.wq || !L.wk || !L.wv || !L.wo || !L.wgate || !L.wup || !L.wdown || !L.norm_in || !L.norm_post) {
+            return set_error(B200Q8_ERR_INVALID_ARG, "chain_create: layer %d has a null pointer", l);
+        }
+    }
+    b200q8_chain * c = new (std::nothrow) b200q8_chain();
+    if (c == nullptr) {
+        return set_error(B200Q8_ERR_OOM, "chain_create: out of host memory");
+    }
+    c->device = device;
+    c->d      = d;
+    c->layers.assign(d.layers, d.layers + d.n_layers);
+    c->d.layers = nullptr;
+    int prev    = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_error(e, "chain_create: cudaSetDevice");
+    }
+    c->sms           = current_sm_count();
+    const int64_t H  = d.hidden, Q = d.n_head * d.head_dim, KV = d.n_kv * d.head_dim, I = d.inter;
+    c->rb_h          = (size_t) (H / kQK) * kBlockBytes;
+    c->rb_q          = (size_t) (Q / kQK) * kBlockBytes;
+    c->rb_i          = (size_t) (I / kQK) * kBlockBytes;
+    c->qkv_dim       = Q + 2 * KV;
+    for (int l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
+        const b200q8_layer & L = c->layers[l];
+        const uint8_t * qkv = contiguous(c, L.wq, (size_t) Q * c->rb_h, L.wk, (size_t) KV * c->rb_h, L.wv,
+                                         (size_t) KV * c->rb_h, e);
+        const uint8_t * gu  = e == cudaSuccess ? contiguous(c, L.wgate, (size_t) I * c->rb_h, L.wup,
+                                                            (size_t) I * c->rb_h, nullptr, 0, e)
+                                               : nullptr;
+        c->w_qkv.push_back(qkv);
+        c->w_gu.push_back(gu);
+        c->w_o.push_back(static_cast<const uint8_t *>(L.wo));
+        c->w_d.push_back(static_cast<const uint8_t *>(L.wdown));
+    }
+    // per-layer activation buffers, each [max_m][width]
+    const int64_t widths[kNumBufs] = { H, c->qkv_dim, Q, H, H, H, 2 * I, I, H, H };
+    size_t        off              = 0;
+    for (int i = 0; i < kNumBufs; ++i) {
+        c->buf_off[i]    = off;
+        c->buf_stride[i] = (size_t) widths[i];
+        off += (size_t) (widths[i] * d.max_m + 63) / 64 * 64;
+    }
+    c->layer_floats = off;
+    if (e == cudaSuccess) {
+        void * p = nullptr;
+        e        = cudaMalloc(&p, (off * d.n_layers + (size_t) (H * d.max_m + 63) / 64 * 64) * sizeof(float));
+        if (e == cudaSuccess) {
+            c->owned.push_back(p);
+            c->act = static_cast<float *>(p);
+            c->h0  = c->act + off * d.n_layers;
+            e      = cudaMemset(p, 0, (off * d.n_layers + (size_t) H * d.max_m) * sizeof(float));
+        }
+    }
+    if (e == cudaSuccess) {
+        e = cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking);
+    }
+    for (int l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
+        GemvParams p = {};
+        p.w = c->w_qkv[l]; p.row_bytes = c->rb_h; p.K = (int) H; p.N = (int) c->qkv_dim; p.M = 8;
+        bool ok = gemv_supported(p);
+        p.w = c->w_gu[l]; p.N = (int) (2 * I); ok = ok && gemv_supported(p);
+        p.w = c->w_o[l]; p.row_bytes = c->rb_q; p.K = (int) Q; p.N = (int) H; ok = ok && gemv_supported(p);
+        p.w = c->w_d[l]; p.row_bytes = c->rb_i; p.K = (int) I; ok = ok && gemv_supported(p);
+        if (!ok) {
+            cudaSetDevice(prev);
+            chain_free(c);
+            return set_error(B200Q8_ERR_UNSUPPORTED, "chain_create: layer %d weights are not 16-byte aligned "
+                                                     "or too wide for the streaming GEMV", l);
+        }
+    }
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        chain_free(c);
+        return cuda_error(e, "chain_create");
+    }
+    *out = c;
+    return B200Q8_OK;
+}
+
+b200q8_status_t b200q8_chain_run(b200q8_chain * c, const int32_t * ids, const float * x_in, float * h_out, int64_t M,
+                                 b200q8_stream_t stream) {
+    if (c == nullptr || ids == nullptr || x_in == nullptr || h_out == nullptr || M < 1 || M > c->d.max_m) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_run: bad argument (M must be in [1, max_m])");
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) {
+        return cuda_error(e, "chain_run: cudaSetDevice");
+    }
+    cudaGraphExec_t exec = nullptr;
+    for (auto & g : c->graphs) {
+        if (g.M == M && g.ids == ids && g.x == x_in && g.h == h_out) {
+            exec = g.exec;
+            break;
+        }
+    }
+    if (exec == nullptr) {
+        cudaGraph_t graph = nullptr;
+        e                 = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal);
+        if (e == cudaSuccess) {
+            cudaError_t e2 = enqueue_step(c, c->cap_stream, M, ids, x_in, h_out);
+            e              = cudaStreamEndCapture(c->cap_stream, &graph);
+            if (e2 != cudaSuccess) {
+                e = e2;
+            }
+        }
+        if (e == cudaSuccess) {
+            e = cudaGraphInstantiate(&exec, graph, 0);
+        }
+        if (graph) {
+            cudaGraphDestroy(graph);
+        }
+        if (e != cudaSuccess) {
+            cudaSetDevice(prev);
+            return cuda_error(e, "chain_run: graph capture");
+        }
+        if (c->graphs.size() >= 8) {
+            cudaGraphExecDestroy(c->graphs.front().exec);
+            c->graphs.erase(c->graphs.begin());
+        }
+        c->graphs.push_back({ M, ids, x_in, h_out, exec });
+    }
+    e = cudaGraphLaunch(exec, reinterpret_cast<cudaStream_t>(stream));
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_run: graph launch");
+}
+
+b200q8_status_t b200q8_chain_buffer(b200q8_chain * c, int32_t layer, int32_t which, float ** ptr, int64_t * stride) {
+    if (c == nullptr || ptr == nullptr || layer < 0 || layer >= c->d.n_layers || which < 0 || which >= kNumBufs) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_buffer: bad layer or buffer index");
+    }
+    *ptr = c->buf(layer, which);
+    if (stride) {
+        *stride = (int64_t) c->buf_stride[which];
+    }
+    return B200Q8_OK;
+}
+
+void b200q8_chain_destroy(b200q8_chain * c) {
+    chain_free(c);
+}
+
+}  // extern "C"

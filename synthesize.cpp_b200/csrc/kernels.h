@@ -1,0 +1,66 @@
+// kernels.h -- host-side launchers of the sm_100a kernels (internal).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace b200q8 {
+
+cudaError_t launch_quantize(const float * x, int64_t rows, int64_t K, size_t x_stride, void * dst, size_t dst_stride,
+                            int mode, cudaStream_t stream, int sm_count);
+
+cudaError_t launch_dequant_rows(const void * src, size_t src_stride, int64_t src_rows, const int32_t * ids,
+                                int64_t n_out, int64_t K, float * out, size_t out_stride, cudaStream_t stream,
+                                int sm_count);
+
+// How the GEMV derives its fp32 input from the buffers it is given.
+enum Prologue : int {
+    kProPlain   = 0,  // x_eff = x
+    kProRmsNorm = 1,  // x_eff = (x * 1/sqrtf(mean(x^2)+eps)) * norm_w
+    kProGqa     = 2,  // x_eff[j] = x[(j/head_dim/group)*head_dim + j%head_dim]
+    kProSwiGlu  = 3,  // x_eff[i] = silu(x[i]) * x2[i]
+};
+
+struct GemvParams {
+    // weights: N rows of K/32 Q8_0 blocks, row n at w + n*row_bytes
+    const uint8_t * w;
+    size_t          row_bytes;
+    int             K;
+    int             N;
+    int             M;  // tokens
+    // input
+    int             pro;
+    const float *   x;
+    const float *   x2;
+    size_t          x_stride;  // floats between tokens
+    const float *   norm_w;
+    float           eps;
+    int             head_dim;
+    int             group;
+    float *         pro_out;  // optional: x_eff written by CTA 0
+    size_t          pro_out_stride;
+    // output
+    float *         y;
+    size_t          y_stride;  // floats between tokens
+    const float *   res;       // optional residual: y_res = res + y
+    float *         y_res;
+    size_t          res_stride;
+    int             mode;
+};
+
+// True when the streaming GEMV supports this shape (K % 256 == 0, 16-byte
+// aligned weight rows, M <= 8, activation tile fits in shared memory).
+bool gemv_supported(const GemvParams & p);
+
+// pdl: launch with programmatic stream serialization (weights are prefetched
+// before the wait on the previous kernel; only for chains whose weights no
+// kernel in the stream writes).
+cudaError_t launch_gemv(const GemvParams & p, cudaStream_t stream, int sm_count, bool pdl);
+
+// Fallback for any K % 32 == 0 / alignment: x already quantized into xq
+// (M rows of K/32 standard blocks).
+cudaError_t launch_gemv_generic(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const uint8_t * xq,
+                                int64_t M, float * y, size_t y_stride_bytes, cudaStream_t stream);
+
+}  // namespace b200q8

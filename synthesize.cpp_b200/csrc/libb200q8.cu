@@ -1,0 +1,6 @@
+// libb200q8.cu -- the whole library as one translation unit, so the per-device
+// status word and the kernels share one module without relocatable device code.
+#include "quantize.cu"
+#include "gemv.cu"
+#include "abi.cu"
+#include "chain.cu"

@@ -1,0 +1,109 @@
+"""Packing and activation quantization on the GPU, through the C ABI, against
+the CPU oracle and the gguf-py golden bytes: bit-exact in every case."""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.filterwarnings("ignore:overflow encountered in cast")]
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+PACK = json.load(open(os.path.join(GOLDEN, "q8_pack_fixtures.json")))
+
+
+def to_dev(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+@pytest.mark.parametrize("name", sorted(PACK["cases"]))
+def test_golden_packing(q8, dev, name):
+    case = PACK["cases"][name]
+    x = np.frombuffer(bytes.fromhex(case["x_f32_hex"]), np.float32).reshape(1, -1)
+    got = q8.quantize_rows(to_dev(x, dev), q8.QUANT_REF).cpu().numpy().tobytes()
+    assert got == bytes.fromhex(case["q8_0_hex"])
+
+
+def random_rows(rows, k, seed, outliers=True):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, k)).astype(np.float32)
+    x *= np.exp(rng.uniform(-8, 8, (rows, 1))).astype(np.float32)
+    if outliers:
+        mask = rng.random((rows, k)) < 0.01
+        x[mask] *= 20
+    # exact ties: blocks whose amax is 127*2^e and values at half-steps
+    t = rows // 3
+    if t:
+        x[:t, ::32] = 127.0
+        x[:t, 1::32] = 2.5
+        x[:t, 2::32] = -0.5
+    return x
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("rows,k", [(1, 32), (3, 160), (7, 256), (64, 1024), (5, 3072), (33, 2048)])
+def test_modes_match_oracle(q8, O, dev, mode, rows, k):
+    x = random_rows(rows, k, seed=rows * 1000 + k + mode)
+    got = q8.quantize_rows(to_dev(x, dev), mode).cpu().numpy()
+    assert np.array_equal(got, O.quantize_rows(x, mode))
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_strided_and_unaligned_rows(q8, O, dev, mode):
+    x = random_rows(9, 352, seed=11)
+    big = torch.zeros((9, 400), dtype=torch.float32, device=dev)
+    big[:, 1:353] = to_dev(x, dev)
+    view = big[:, 1:353]  # row stride 1600 B, base not 16-byte aligned
+    got = q8.quantize_rows(view, mode).cpu().numpy()
+    assert np.array_equal(got, O.quantize_rows(x, mode))
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_non_finite_inputs(q8, O, dev, mode):
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((16, 64)).astype(np.float32)
+    x[0, 3] = np.nan
+    x[1, 31] = np.nan
+    x[2, 0] = np.inf
+    x[3, 5] = -np.inf
+    x[4, :32] = np.nan
+    x[5, 40] = np.nan
+    x[5, 50] = np.nan
+    x[6, :] = 1e-42  # fp32 subnormals: 1/d overflows to inf
+    x[7, 7] = 3e38
+    got = q8.quantize_rows(to_dev(x, dev), mode).cpu().numpy()
+    assert np.array_equal(got, O.quantize_rows(x, mode))
+
+
+def test_ragged_tail_and_chunk(q8, O, dev):
+    x = random_rows(3, 160, seed=4)  # 15 blocks: one 8-block run + a 7-block tail
+    assert np.array_equal(q8.quantize_rows(to_dev(x, dev)).cpu().numpy(), O.quantize_rows(x))
+    src = random_rows(6, 256, seed=6).ravel()
+    dst = torch.zeros(6 * 272, dtype=torch.uint8, device=dev)
+    n = q8.quantize_chunk(to_dev(src, dev), dst, 2 * 256, 3, 256)
+    ref, nref = O.quantize_chunk(src, 2 * 256, 3, 256)
+    assert n == nref == 3 * 272
+    assert np.array_equal(dst.cpu().numpy(), ref)
+
+
+def test_large_packing_and_round_trip(q8, O, dev):
+    # a 1.7B-shaped gate matrix (6144 x 2048): bit-exact, and dequant(quant(x))
+    # lands within half a step of x everywhere
+    w = O.normal(77, 6144 * 2048, 0.02).reshape(6144, 2048)
+    wq = q8.quantize_rows(to_dev(w, dev))
+    assert np.array_equal(wq.cpu().numpy(), O.quantize_rows(w))
+    back = q8.dequantize_rows(wq, 2048).cpu().numpy()
+    d = wq.cpu().numpy().reshape(-1, 34)[:, :2].copy().view(np.float16).astype(np.float32).reshape(6144, 64, 1)
+    err = np.abs(back.reshape(6144, 64, 32) - w.reshape(6144, 64, 32))
+    # half a step plus the fp16 rounding of d (127 * 2^-11 * d)
+    assert np.all(err <= 0.57 * d + 1e-12)
+
+
+def test_bad_arguments_raise(q8, dev):
+    x = torch.zeros((2, 33), dtype=torch.float32, device=dev)
+    with pytest.raises(q8.B200Q8Error) as e:
+        q8.quantize_rows(x)
+    assert e.value.status == 1
