@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b"])
     ap.add_argument("--batch", type=int, default=1, help="tokens (streams) per step per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chain", default="auto", choices=["auto", "per-op"],
+                    help="auto: single-launch persistent step for M <= 2; per-op: CUDA graph of per-op kernels")
     return ap.parse_args()
 
 
@@ -248,6 +250,7 @@ def main():
     shape = TALKER_17B if args.workload == "talker-1.7b" else TALKER_06B
     m = args.batch
     dm = build_model(shape, dev)
+    os.environ["B200Q8_CHAIN_PER_OP"] = "1" if args.chain == "per-op" else "0"
     ch = chain_mod.DecodeChain(dm.layers, dm.table, hidden=shape.hidden, n_head=shape.n_head, n_kv=shape.n_kv,
                                head_dim=shape.head_dim, inter=shape.inter, eps=shape.eps, max_m=max(8, m))
     x_np, ids_np = stream_inputs(m, shape.hidden, shape.table_rows, first_stream=rank * m)
@@ -300,7 +303,10 @@ def main():
     peaks, peak_kind = measured_peaks()
     step_bytes = shape.step_bytes(m)
     achieved = step_bytes / step_s / 1e9
-    launches_per_step = 1 + 4 * shape.n_layers * ((m + 7) // 8)
+    persistent = args.chain == "auto" and m <= 2
+    launches_per_step = 1 if persistent else 1 + 4 * shape.n_layers * ((m + 7) // 8)
+    kernel_name = ("decode_step_kernel (the whole step in one persistent launch)" if persistent
+                   else "gemv_q8_0_kernel (every launch of the step; 1 + 4*layers launches)")
     line = {
         "metric": "talker-shaped Q8_0 decode throughput", "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * step_s, "higher_is_better": True,
@@ -313,7 +319,7 @@ def main():
                    "weight_bytes_per_step": shape.weight_bytes(), "algorithmic_bytes_per_step": step_bytes},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic(f"{shape.name}-m{m}"),
-                     "kernel": "gemv_q8_0_kernel (every launch of the step; 1 + 4*layers launches)",
+                     "kernel": kernel_name,
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
         "e2e": {"value": tokens / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": m * shape.hidden * 4 + m * 4,
                 "d2h_bytes_per_step": m * shape.hidden * 4},

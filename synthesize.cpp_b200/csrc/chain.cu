@@ -22,6 +22,8 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <new>
 #include <vector>
 
@@ -78,6 +80,12 @@ struct b200q8_chain {
     float *                      h0           = nullptr;
     cudaStream_t                 cap_stream   = nullptr;
     int                          sms          = 148;
+    // persistent single-launch step (M <= 2)
+    StepLayerDev *               step_layers  = nullptr;  // device array
+    unsigned long long *         ll           = nullptr;
+    size_t                       ll_layer     = 0;
+    unsigned *                   sync         = nullptr;
+    bool                         persistent   = false;
 
     struct Graph {
         int64_t         M;
@@ -276,6 +284,30 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
     if (e == cudaSuccess) {
         e = cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking);
     }
+    // persistent step: per-layer weight table, LL hand-off words, sync words
+    const char * per_op = getenv("B200Q8_CHAIN_PER_OP");
+    if (e == cudaSuccess && !(per_op && per_op[0] == '1')) {
+        std::vector<StepLayerDev> host_layers(d.n_layers);
+        for (int l = 0; l < d.n_layers; ++l) {
+            host_layers[l] = { c->w_qkv[l], c->w_o[l], c->w_gu[l], c->w_gu[l] + (size_t) I * c->rb_h, c->w_d[l],
+                               c->layers[l].norm_in, c->layers[l].norm_post };
+        }
+        c->ll_layer  = (size_t) 2 * (KV + H + I + H);
+        void * p1 = nullptr, * p2 = nullptr, * p3 = nullptr;
+        e = cudaMalloc(&p1, sizeof(StepLayerDev) * d.n_layers);
+        if (e == cudaSuccess) { c->owned.push_back(p1); e = cudaMalloc(&p2, sizeof(unsigned long long) * c->ll_layer * d.n_layers); }
+        if (e == cudaSuccess) { c->owned.push_back(p2); e = cudaMalloc(&p3, 64); }
+        if (e == cudaSuccess) {
+            c->owned.push_back(p3);
+            c->step_layers = static_cast<StepLayerDev *>(p1);
+            c->ll          = static_cast<unsigned long long *>(p2);
+            c->sync        = static_cast<unsigned *>(p3);
+            e = cudaMemcpy(p1, host_layers.data(), sizeof(StepLayerDev) * d.n_layers, cudaMemcpyHostToDevice);
+        }
+        if (e == cudaSuccess) e = cudaMemset(p2, 0, sizeof(unsigned long long) * c->ll_layer * d.n_layers);
+        if (e == cudaSuccess) e = cudaMemset(p3, 0, 64);
+        c->persistent = e == cudaSuccess;
+    }
     for (int l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
         GemvParams p = {};
         p.w = c->w_qkv[l]; p.row_bytes = c->rb_h; p.K = (int) H; p.N = (int) c->qkv_dim; p.M = 8;
@@ -309,6 +341,25 @@ b200q8_status_t b200q8_chain_run(b200q8_chain * c, const int32_t * ids, const fl
     cudaError_t e = cudaSetDevice(c->device);
     if (e != cudaSuccess) {
         return cuda_error(e, "chain_run: cudaSetDevice");
+    }
+    if (c->persistent && M <= 2) {
+        const b200q8_chain_desc & d = c->d;
+        StepArgs a = {};
+        a.layers = c->step_layers; a.n_layers = d.n_layers;
+        a.H = (int) d.hidden; a.Q = (int) (d.n_head * d.head_dim); a.KV = (int) (d.n_kv * d.head_dim);
+        a.I = (int) d.inter; a.head_dim = (int) d.head_dim; a.group = (int) (d.n_head / d.n_kv); a.eps = d.eps;
+        a.rb_h = c->rb_h; a.rb_q = c->rb_q; a.rb_i = c->rb_i;
+        a.table = static_cast<const uint8_t *>(d.table); a.table_rows = d.table_rows;
+        a.ids = ids; a.x_in = x_in; a.h_out = h_out; a.M = (int) M; a.mode = d.mode;
+        a.ll = c->ll; a.ll_layer = c->ll_layer; a.ll_m = 2;
+        a.trace = c->act; a.trace_layer = c->layer_floats;
+        for (int i = 0; i < kNumBufs; ++i) a.trace_off[i] = c->buf_off[i];
+        a.sync = c->sync;
+        if (decode_step_supported(a, c->sms)) {
+            e = launch_decode_step(a, c->sms, reinterpret_cast<cudaStream_t>(stream));
+            cudaSetDevice(prev);
+            return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_run: persistent step launch");
+        }
     }
     cudaGraphExec_t exec = nullptr;
     for (auto & g : c->graphs) {

@@ -128,6 +128,12 @@ __device__ __forceinline__ int quant_code(float x, float id) {
     return isfinite(r) ? static_cast<int>(r) : 0;
 }
 
+// silu as ggml's scalar form writes it: x / (1 + expf(-x)).  expf is CUDA's
+// (within 2 ulp of the exact value); libm's may differ by an ulp.
+__device__ __forceinline__ float silu_f32(float v) {
+    return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+}
+
 // ------------------------------------------------------------- PTX wrappers
 
 __device__ __forceinline__ uint32_t smem_addr(const void * p) {

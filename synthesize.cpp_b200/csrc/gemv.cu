@@ -28,6 +28,7 @@
 //    previous op finishes.
 #include "common.cuh"
 #include "kernels.h"
+#include "tile_dot.cuh"
 
 #include <algorithm>
 #include <atomic>
@@ -73,10 +74,6 @@ bool make_layout(int K, size_t row_bytes, int rows_per_cta, int mt, Layout & L) 
     L.n_slots    = std::min(std::min(kMaxSlots, tiles), budget / L.slot_bytes);
     L.smem_bytes = L.ring_off + L.n_slots * L.slot_bytes;
     return L.n_slots >= 1;
-}
-
-__device__ __forceinline__ float silu_f32(float v) {
-    return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
 }
 
 template <int M_T, int MODE, int PRO>
@@ -219,19 +216,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_q8_0_kernel(const GemvPa
         for (int c = 0; c < kChunk; ++c) {
             const int blk = base_blk + c * kConsumerWarps;
             if (blk < NBM) {  // warp-uniform
-                const int         m     = blk / NB;
-                const int         b     = blk % NB;
-                float             vv[1] = { v[c] };
-                const float       am    = block_amax<32, 1>(vv, lane);
-                const QuantParams qp    = quant_params<MODE>(am);
-                const int         q     = quant_code<MODE>(v[c], qp.id);
-                const int         pp    = b >> 1;
-                const int         pos   = ((b & 1) << 5) + lane;
-                const int         wi    = pos >> 2;
-                xc[((size_t) (m * 4 + (wi >> 2)) * P + pp) * 16 + (wi & 3) * 4 + (pos & 3)] = (uint8_t) (q & 0xff);
-                if (lane == 0) {
-                    xd[m * NB + b] = qp.d;
-                }
+                const int m = blk / NB;
+                const int b = blk % NB;
+                stage_activation_block<MODE>(v[c], m, b, lane, P, NB, xc, xd);
                 if (p.pro_out != nullptr && blockIdx.x == 0) {
                     p.pro_out[(size_t) m * p.pro_out_stride + b * kQK + lane] = v[c];
                 }
@@ -241,15 +228,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_q8_0_kernel(const GemvPa
     named_barrier_sync(1, kConsumers);
 
     // ------------------------------------------------------ consume tiles
-    int GS = 1;
-    while (GS < P && GS < 32) {
-        GS <<= 1;
-    }
-    const int RPW = 32 / GS;
-    const int sub = lane / GS;
-    const int gl  = lane % GS;
-    const uint4 * xv_base = reinterpret_cast<const uint4 *>(xc);
-
     for (int t = 0; t < n_tiles; ++t) {
         const int s = t % S;
         if (!mbar_wait_bounded(&full[s], (t / S) & 1)) {
@@ -260,82 +238,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_q8_0_kernel(const GemvPa
         const int       tr0  = t * L.slot_rows;
         const int       R    = min(L.slot_rows, nrows - tr0);
         const uint8_t * tile = ring + (size_t) s * L.slot_bytes;
-        for (int rb = warp * RPW; rb < R; rb += kConsumerWarps * RPW) {
-            const int  rr     = rb + sub;
-            const bool active = rr < R;
-            float      acc[M_T];
-#pragma unroll
-            for (int m = 0; m < M_T; ++m) {
-                acc[m] = 0.0f;
-            }
-            if (active) {
-                const uint32_t * wr = reinterpret_cast<const uint32_t *>(tile + (size_t) rr * p.row_bytes);
-                for (int pp = gl; pp < P; pp += GS) {
-                    uint32_t w[17];
-#pragma unroll
-                    for (int k = 0; k < 17; ++k) {
-                        w[k] = wr[17 * pp + k];
-                    }
-                    int qa[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        qa[i] = (int) __byte_perm(w[i], w[i + 1], 0x5432);
-                    }
-                    const float dA = __half2float(__ushort_as_half((unsigned short) (w[0] & 0xffffu)));
-                    const float dB = __half2float(__ushort_as_half((unsigned short) (w[8] >> 16)));
-#pragma unroll
-                    for (int m = 0; m < M_T; ++m) {
-                        if (m < M) {
-                            const uint4 * xv = xv_base + (size_t) (m * 4) * P + pp;
-                            const uint4   x0 = xv[0];
-                            const uint4   x1 = xv[P];
-                            const uint4   x2 = xv[2 * P];
-                            const uint4   x3 = xv[3 * P];
-                            const float2  dx = *reinterpret_cast<const float2 *>(xd + m * NB + 2 * pp);
-                            int           sA = 0;
-                            int           sB = 0;
-                            sA = __dp4a(qa[0], (int) x0.x, sA);
-                            sA = __dp4a(qa[1], (int) x0.y, sA);
-                            sA = __dp4a(qa[2], (int) x0.z, sA);
-                            sA = __dp4a(qa[3], (int) x0.w, sA);
-                            sA = __dp4a(qa[4], (int) x1.x, sA);
-                            sA = __dp4a(qa[5], (int) x1.y, sA);
-                            sA = __dp4a(qa[6], (int) x1.z, sA);
-                            sA = __dp4a(qa[7], (int) x1.w, sA);
-                            sB = __dp4a((int) w[9], (int) x2.x, sB);
-                            sB = __dp4a((int) w[10], (int) x2.y, sB);
-                            sB = __dp4a((int) w[11], (int) x2.z, sB);
-                            sB = __dp4a((int) w[12], (int) x2.w, sB);
-                            sB = __dp4a((int) w[13], (int) x3.x, sB);
-                            sB = __dp4a((int) w[14], (int) x3.y, sB);
-                            sB = __dp4a((int) w[15], (int) x3.z, sB);
-                            sB = __dp4a((int) w[16], (int) x3.w, sB);
-                            acc[m] = __fmaf_rn((float) sA, __fmul_rn(dA, dx.x), acc[m]);
-                            acc[m] = __fmaf_rn((float) sB, __fmul_rn(dB, dx.y), acc[m]);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int m = 0; m < M_T; ++m) {
-                for (int off = GS / 2; off > 0; off >>= 1) {
-                    acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], off);
-                }
-            }
-            if (active && gl == 0) {
-                const int n = r0 + tr0 + rr;
-#pragma unroll
-                for (int m = 0; m < M_T; ++m) {
-                    if (m < M) {
-                        p.y[(size_t) m * p.y_stride + n] = acc[m];
-                        if (p.y_res != nullptr) {
-                            p.y_res[(size_t) m * p.res_stride + n] =
-                                __fadd_rn(p.res[(size_t) m * p.res_stride + n], acc[m]);
-                        }
-                    }
-                }
-            }
-        }
+        dot_tile_rows<M_T>(tile, R, p.row_bytes, P, NB, xc, xd, M, warp, lane, kConsumerWarps,
+                           [&](int rr, int m, float acc) {
+                               const int n                           = r0 + tr0 + rr;
+                               p.y[(size_t) m * p.y_stride + n] = acc;
+                               if (p.y_res != nullptr) {
+                                   p.y_res[(size_t) m * p.res_stride + n] =
+                                       __fadd_rn(p.res[(size_t) m * p.res_stride + n], acc);
+                               }
+                           });
         __syncwarp();
         if (lane == 0) {
             mbar_arrive(&empty[s]);

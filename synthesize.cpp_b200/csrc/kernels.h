@@ -63,4 +63,43 @@ cudaError_t launch_gemv(const GemvParams & p, cudaStream_t stream, int sm_count,
 cudaError_t launch_gemv_generic(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const uint8_t * xq,
                                 int64_t M, float * y, size_t y_stride_bytes, cudaStream_t stream);
 
+// ---- the persistent decode step (decode_step.cu)
+
+struct StepLayerDev {
+    const uint8_t * w_qkv;   // [Q + 2*KV rows] of K = H
+    const uint8_t * w_o;     // [H rows] of K = Q
+    const uint8_t * w_gate;  // [I rows] of K = H
+    const uint8_t * w_up;    // [I rows] of K = H
+    const uint8_t * w_down;  // [H rows] of K = I
+    const float *   norm_in;
+    const float *   norm_post;
+};
+
+struct StepArgs {
+    const StepLayerDev * layers;  // device array [n_layers]
+    int                  n_layers;
+    int                  H, Q, KV, I, head_dim, group;
+    float                eps;
+    size_t               rb_h, rb_q, rb_i;
+    const uint8_t *      table;
+    int64_t              table_rows;
+    const int32_t *      ids;
+    const float *        x_in;
+    float *              h_out;
+    int                  M;
+    int                  mode;
+    unsigned long long * ll;        // LL words, per layer [v | o | s | d], each [ll_m][width]
+    size_t               ll_layer;  // words per layer
+    int                  ll_m;      // token stride of the LL buffers
+    float *              trace;     // optional per-layer activation copies (chain buffer layout)
+    size_t               trace_layer;
+    size_t               trace_off[10];
+    unsigned *           sync;      // [0] launch counter, [1] abort word
+    int                  n_slots;   // set by the launcher
+};
+
+bool        decode_step_supported(const StepArgs & a, int grid);
+size_t      decode_step_smem_bytes(const StepArgs & a, int mt, int & n_slots);
+cudaError_t launch_decode_step(StepArgs a, int grid, cudaStream_t stream);
+
 }  // namespace b200q8

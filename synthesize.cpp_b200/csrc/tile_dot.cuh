@@ -1,0 +1,127 @@
+// tile_dot.cuh -- the inner product of a shared-memory tile of Q8_0 weight
+// rows with shared-memory Q8_0 activations (int8 dp4a per block, fp32 scale),
+// shared by the standalone GEMV and the persistent decode-step kernel.
+//
+// Activation layout in shared memory (written by stage_activation_block):
+//   codes: for token m, block pair p (64 codes) and 16-byte chunk c (0..3),
+//          the chunk lives at ((m*4 + c)*P + p)*16, so lanes reading
+//          consecutive pairs touch consecutive 16-byte words (no bank
+//          conflicts for 128-bit loads);
+//   scales: fp32(fp16(d)) at [m*NB + b].
+// Weight rows in the tile are ggml block_q8_0 rows (34-byte blocks); a lane
+// reads one 68-byte block pair as 17 4-byte words, stride 17 words between
+// lanes, which is conflict-free.
+#pragma once
+
+#include "common.cuh"
+
+namespace b200q8 {
+
+// Quantizes value v (lane = position in the block) of block b of token m
+// and stores the code and scale in the layout above.  All 32 lanes call it.
+template <int MODE>
+__device__ __forceinline__ void stage_activation_block(float v, int m, int b, int lane, int P, int NB, uint8_t * xc,
+                                                       float * xd) {
+    float             vv[1] = { v };
+    const float       am    = block_amax<32, 1>(vv, lane);
+    const QuantParams qp    = quant_params<MODE>(am);
+    const int         q     = quant_code<MODE>(v, qp.id);
+    const int         pp    = b >> 1;
+    const int         pos   = ((b & 1) << 5) + lane;
+    const int         wi    = pos >> 2;
+    xc[((size_t) (m * 4 + (wi >> 2)) * P + pp) * 16 + (wi & 3) * 4 + (pos & 3)] = (uint8_t) (q & 0xff);
+    if (lane == 0) {
+        xd[m * NB + b] = qp.d;
+    }
+}
+
+// Dot products of the R rows of `tile` (row stride row_bytes, K = 64*P) with
+// the M staged tokens.  Warps warp0..warp0+n_warps-1 share the rows; a group
+// of GS lanes (GS = P rounded up to a power of two, at most 32) takes one
+// row.  store(row, m, value) is called once per (row, token) by one lane.
+template <int M_T, typename Store>
+__device__ __forceinline__ void dot_tile_rows(const uint8_t * tile, int R, size_t row_bytes, int P, int NB,
+                                              const uint8_t * xc, const float * xd, int M, int warp, int lane,
+                                              int n_warps, Store && store) {
+    int GS = 1;
+    while (GS < P && GS < 32) {
+        GS <<= 1;
+    }
+    const int     RPW     = 32 / GS;
+    const int     sub     = lane / GS;
+    const int     gl      = lane % GS;
+    const uint4 * xv_base = reinterpret_cast<const uint4 *>(xc);
+    for (int rb = warp * RPW; rb < R; rb += n_warps * RPW) {
+        const int  rr     = rb + sub;
+        const bool active = rr < R;
+        float      acc[M_T];
+#pragma unroll
+        for (int m = 0; m < M_T; ++m) {
+            acc[m] = 0.0f;
+        }
+        if (active) {
+            const uint32_t * wr = reinterpret_cast<const uint32_t *>(tile + (size_t) rr * row_bytes);
+            for (int pp = gl; pp < P; pp += GS) {
+                uint32_t w[17];
+#pragma unroll
+                for (int k = 0; k < 17; ++k) {
+                    w[k] = wr[17 * pp + k];
+                }
+                int qa[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    qa[i] = (int) __byte_perm(w[i], w[i + 1], 0x5432);
+                }
+                const float dA = __half2float(__ushort_as_half((unsigned short) (w[0] & 0xffffu)));
+                const float dB = __half2float(__ushort_as_half((unsigned short) (w[8] >> 16)));
+#pragma unroll
+                for (int m = 0; m < M_T; ++m) {
+                    if (m < M) {
+                        const uint4 * xv = xv_base + (size_t) (m * 4) * P + pp;
+                        const uint4   x0 = xv[0];
+                        const uint4   x1 = xv[P];
+                        const uint4   x2 = xv[2 * P];
+                        const uint4   x3 = xv[3 * P];
+                        const float2  dx = *reinterpret_cast<const float2 *>(xd + m * NB + 2 * pp);
+                        int           sA = 0;
+                        int           sB = 0;
+                        sA = __dp4a(qa[0], (int) x0.x, sA);
+                        sA = __dp4a(qa[1], (int) x0.y, sA);
+                        sA = __dp4a(qa[2], (int) x0.z, sA);
+                        sA = __dp4a(qa[3], (int) x0.w, sA);
+                        sA = __dp4a(qa[4], (int) x1.x, sA);
+                        sA = __dp4a(qa[5], (int) x1.y, sA);
+                        sA = __dp4a(qa[6], (int) x1.z, sA);
+                        sA = __dp4a(qa[7], (int) x1.w, sA);
+                        sB = __dp4a((int) w[9], (int) x2.x, sB);
+                        sB = __dp4a((int) w[10], (int) x2.y, sB);
+                        sB = __dp4a((int) w[11], (int) x2.z, sB);
+                        sB = __dp4a((int) w[12], (int) x2.w, sB);
+                        sB = __dp4a((int) w[13], (int) x3.x, sB);
+                        sB = __dp4a((int) w[14], (int) x3.y, sB);
+                        sB = __dp4a((int) w[15], (int) x3.z, sB);
+                        sB = __dp4a((int) w[16], (int) x3.w, sB);
+                        acc[m] = __fmaf_rn((float) sA, __fmul_rn(dA, dx.x), acc[m]);
+                        acc[m] = __fmaf_rn((float) sB, __fmul_rn(dB, dx.y), acc[m]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M_T; ++m) {
+            for (int off = GS / 2; off > 0; off >>= 1) {
+                acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], off);
+            }
+        }
+        if (active && gl == 0) {
+#pragma unroll
+            for (int m = 0; m < M_T; ++m) {
+                if (m < M) {
+                    store(rr, m, acc[m]);
+                }
+            }
+        }
+    }
+}
+
+}  // namespace b200q8

@@ -1,0 +1,105 @@
+"""The C ABI library loads and exports what include/b200q8.h declares, and its
+argument checks answer with synth_status_t codes -- all without a GPU (no
+compute call is made)."""
+from __future__ import annotations
+
+import ctypes
+import subprocess
+
+import numpy as np
+import pytest
+
+
+def test_every_declared_symbol_is_exported(pkg):
+    from synthesize_cpp_b200 import _abi
+
+    L = _abi.lib()
+    declared = _abi.header_symbols()
+    assert len(declared) >= 13
+    for name in declared:
+        assert hasattr(L, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", _abi.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert set(declared) <= exported
+
+
+def test_version_and_workspace(pkg):
+    from synthesize_cpp_b200 import _abi
+
+    L = _abi.lib()
+    assert L.b200q8_version() == 100
+    assert L.b200q8_mul_mat_workspace_size(1024, 3072, 1) == 256 * ((32 * 34 + 255) // 256)
+    assert L.b200q8_mul_mat_workspace_size(33, 1, 1) == 0
+
+
+def test_invalid_arguments_report_status_and_message(pkg):
+    from synthesize_cpp_b200 import _abi
+
+    L = _abi.lib()
+    st = L.b200q8_mul_mat(None, 33, 4, 34, None, 1, 0, None, 0, 0, None, 0, None)
+    assert st == _abi.ERR_INVALID_ARG
+    code, msg = _abi.last_error()
+    assert code == _abi.ERR_INVALID_ARG and "multiple of 32" in msg
+    assert L.b200q8_mul_mat(None, 64, 4, 68, None, 1, 0, None, 0, 7, None, 0, None) == _abi.ERR_INVALID_ARG
+    assert "mode" in _abi.last_error()[1]
+    assert L.b200q8_quantize_rows(None, 2, 48, 0, None, 0, 0, None) == _abi.ERR_INVALID_ARG
+    assert L.b200q8_quantize_chunk(None, None, 5, 1, 32, None, None) == _abi.ERR_INVALID_ARG
+    assert L.b200q8_get_rows(None, 40, 1, 0, None, 1, None, 0, None) == _abi.ERR_INVALID_ARG
+    assert L.b200q8_dequantize_rows(None, 1, 31, 0, None, 0, None) == _abi.ERR_INVALID_ARG
+    h = ctypes.c_void_p()
+    assert L.b200q8_chain_create(None, 0, ctypes.byref(h)) == _abi.ERR_INVALID_ARG
+    p = ctypes.c_void_p()
+    assert L.b200q8_chain_buffer(None, 0, 0, ctypes.byref(p), None) == _abi.ERR_INVALID_ARG
+    # empty work is a successful no-op
+    assert L.b200q8_mul_mat(None, 64, 0, 68, None, 1, 0, None, 0, 0, None, 0, None) == _abi.OK
+    assert L.b200q8_quantize_rows(None, 0, 64, 0, None, 0, 0, None) == _abi.OK
+
+
+def test_chain_desc_validation(pkg):
+    from synthesize_cpp_b200 import _abi
+
+    L = _abi.lib()
+    layers = (_abi.Layer * 1)()
+    desc = _abi.ChainDesc(1, 1000, 16, 8, 128, 3072, 1e-6, 1, 0, ctypes.cast(layers, ctypes.POINTER(_abi.Layer)),
+                          1, 10)
+    h = ctypes.c_void_p()
+    assert L.b200q8_chain_create(ctypes.byref(desc), 0, ctypes.byref(h)) == _abi.ERR_INVALID_ARG  # hidden % 256
+    desc.hidden = 1024
+    assert L.b200q8_chain_create(ctypes.byref(desc), 0, ctypes.byref(h)) == _abi.ERR_INVALID_ARG  # null weights
+    assert "null" in _abi.last_error()[1]
+
+
+def test_host_stream_matches_oracle_and_reference(pkg, O):
+    from synthesize_cpp_b200 import host
+
+    for seed in (0, 1, 42, 12345):
+        a = host.normal(seed, 1000)
+        assert np.array_equal(a, O.normal(seed, 1000))
+        assert np.array_equal(host.normal(seed, 100, 0.02), O.normal(seed, 100, 0.02))
+    outs = [np.empty(n, np.float32) for n in (5, 1000, 77)]
+    host.normal_many([3, 4, 5], [1.0, 0.5, 2.0], outs, threads=3)
+    for o, s, f in zip(outs, (3, 4, 5), (1.0, 0.5, 2.0)):
+        assert np.array_equal(o, O.normal(s, o.size, f) if f != 1.0 else O.normal(s, o.size))
+    assert [host.default_threads(n) for n in (1, 2, 3, 16)] == [1, 1, 1, 8]
+    ref = O.ref_lib()
+    if ref is not None:
+        r = np.empty(500, np.float32)
+        ref.ref_normal_fill(77, r.ctypes.data, 500)
+        assert np.array_equal(host.normal(77, 500), r)
+
+
+def test_product_library_does_not_link_the_oracle(pkg):
+    from synthesize_cpp_b200 import _abi, host
+
+    for path in (_abi.LIB_PATH, host.HOST_LIB):
+        deps = subprocess.run(["ldd", path], capture_output=True, text=True).stdout
+        assert "q8oracle" not in deps and "synth_ref" not in deps
+        syms = subprocess.run(["nm", "-D", path], capture_output=True, text=True).stdout
+        assert "oracle_" not in syms
+
+
+@pytest.mark.parametrize("name", ["q8", "chain", "workloads", "host"])
+def test_modules_import_without_gpu(pkg, name):
+    import importlib
+
+    importlib.import_module("synthesize_cpp_b200." + name)
