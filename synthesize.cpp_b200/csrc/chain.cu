@@ -86,6 +86,7 @@ struct b200q8_chain {
     size_t                       ll_layer     = 0;
     unsigned *                   sync         = nullptr;
     bool                         persistent   = false;
+    void *                       timeline     = nullptr;  // B200Q8_TIMELINE analysis builds only
 
     struct Graph {
         int64_t         M;
@@ -355,6 +356,14 @@ b200q8_status_t b200q8_chain_run(b200q8_chain * c, const int32_t * ids, const fl
         a.trace = c->act; a.trace_layer = c->layer_floats;
         for (int i = 0; i < kNumBufs; ++i) a.trace_off[i] = c->buf_off[i];
         a.sync = c->sync;
+#ifdef B200Q8_TIMELINE
+        if (c->timeline == nullptr) {
+            cudaMalloc(&c->timeline, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms);
+            cudaMemset(c->timeline, 0, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms);
+            c->owned.push_back(c->timeline);
+        }
+        a.timeline = static_cast<unsigned long long *>(c->timeline);
+#endif
         if (decode_step_supported(a, c->sms)) {
             e = launch_decode_step(a, c->sms, reinterpret_cast<cudaStream_t>(stream));
             cudaSetDevice(prev);
@@ -409,6 +418,22 @@ b200q8_status_t b200q8_chain_buffer(b200q8_chain * c, int32_t layer, int32_t whi
     }
     return B200Q8_OK;
 }
+
+#ifdef B200Q8_TIMELINE
+// Analysis builds only: copies the last persistent step's stamps
+// [cta][op][8] (events 0-4 consumer, 5 producer first issue) to the host.
+b200q8_status_t b200q8_chain_timeline(b200q8_chain * c, unsigned long long * host, size_t n) {
+    if (c == nullptr || c->timeline == nullptr) {
+        return B200Q8_ERR_INVALID_ARG;
+    }
+    const size_t have = (size_t) 8 * 4 * c->d.n_layers * c->sms;
+    cudaDeviceSynchronize();
+    return cudaMemcpy(host, c->timeline, sizeof(unsigned long long) * std::min(n, have), cudaMemcpyDeviceToHost) ==
+                   cudaSuccess
+               ? B200Q8_OK
+               : B200Q8_ERR_BACKEND;
+}
+#endif
 
 void b200q8_chain_destroy(b200q8_chain * c) {
     chain_free(c);

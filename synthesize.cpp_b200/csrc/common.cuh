@@ -174,6 +174,48 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
 // the limit ran out; the caller records B200Q8_ERR_DEVICE_TIMEOUT.
 constexpr long long kWaitLimitCycles = 2000000000LL;
 
+// try_wait with a suspend-time hint (ns): for waiters off the critical path,
+// so they do not compete for issue slots while they wait.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t * bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(20000u)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t * bar, uint32_t parity) {
+    const long long start = clock64();
+    while (!mbar_try_wait_sleep(bar, parity)) {
+        if (clock64() - start > kWaitLimitCycles) {
+            return false;
+        }
+    }
+    return true;
+}
+
+// Shared-memory loads by shared-window address (explicit .shared space).
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ float2 lds_f2(uint32_t addr) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+    return v;
+}
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t * bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) {
         return true;

@@ -75,6 +75,28 @@ __device__ __forceinline__ bool consumers_any(bool pred) {
     return r != 0;
 }
 
+#ifdef B200Q8_TIMELINE
+// Analysis builds only: per (CTA, op, event) globaltimer stamps.
+__device__ __forceinline__ void tl_stamp(const StepArgs & a, int op, int ev) {
+    if (threadIdx.x == 0 && a.timeline != nullptr) {
+        unsigned long long g;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g));
+        a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + op) * 8 + ev] = g;
+    }
+}
+#define TL(op, ev) tl_stamp(a, (op), (ev))
+#define TL_CYC(op)                                                                                      \
+    do {                                                                                                \
+        if (threadIdx.x == 0 && a.timeline != nullptr) {                                                \
+            a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + (op)) * 8 + 6] = tl_wait_cycles;        \
+            a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + (op)) * 8 + 7] = tl_dot_cycles;         \
+        }                                                                                               \
+    } while (0)
+#else
+#define TL(op, ev) ((void) 0)
+#define TL_CYC(op) ((void) 0)
+#endif
+
 struct Part {
     int r0;
     int n;
@@ -106,6 +128,7 @@ struct Smem {
     float *    rms_scale;  // [2]
     float *    hbuf;       // [M_T][H]
     float *    h1buf;      // [M_T][H]
+    float *    normbuf;    // [H] the RMS-norm weight of the current norm op
     float *    ybuf;       // [M_T][2*kStepYMax]
     uint8_t *  xc;         // codes [M_T][Kmax]
     float *    xd;         // scales [M_T][Kmax/32]
@@ -147,7 +170,7 @@ template <int N>
 __device__ __forceinline__ bool ll_settle(const StepArgs & a, const Smem & s, const unsigned long long * const (&src)[N],
                                           unsigned long long (&w)[N], int n, unsigned epoch) {
     long long start = -1;
-    for (;;) {
+    for (unsigned iter = 0;; ++iter) {
         bool done = true;
 #pragma unroll
         for (int i = 0; i < N; ++i) {
@@ -163,7 +186,8 @@ __device__ __forceinline__ bool ll_settle(const StepArgs & a, const Smem & s, co
             start = clock64();
         } else if (clock64() - start > kWaitLimitCycles) {
             return false;
-        } else if (aborted(a, s)) {
+        } else if ((iter & 255u) == 255u && aborted(a, s)) {
+            // the global abort word costs an L2 round trip: look rarely
             return false;
         }
     }
@@ -176,9 +200,14 @@ __device__ __forceinline__ bool ll_settle(const StepArgs & a, const Smem & s, co
 template <int M_T>
 __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsigned long long * delta,
                                  const float * h_src, float * h_dst, int M, unsigned epoch, float * trace_h,
-                                 bool & fail) {
+                                 const float * norm, bool & fail) {
     const int H = a.H;
     const int t = threadIdx.x;
+    // The norm weight goes to shared memory now, its L2 latency hidden under
+    // the wait for the previous op's outputs.
+    for (int i = t; i < H; i += kStepConsumers) {
+        s.normbuf[i] = norm[i];
+    }
     double    ss[M_T];
 #pragma unroll
     for (int m = 0; m < M_T; ++m) {
@@ -353,6 +382,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     off += (size_t) M_T * H * 4;
     s.h1buf = reinterpret_cast<float *>(smem + off);
     off += (size_t) M_T * H * 4;
+    s.normbuf = reinterpret_cast<float *>(smem + off);
+    off += (size_t) H * 4;
     s.ybuf = reinterpret_cast<float *>(smem + off);
     off += (size_t) M_T * 2 * kStepYMax * 4;
     s.xc = smem + off;
@@ -389,14 +420,21 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                 layer_segs(a, l, c, G, segs);
                 for (int g = 0; g < 5 && !stop; ++g) {
                     const int nt = seg_tiles(segs[g]);
+#ifdef B200Q8_TIMELINE
+                    if (a.timeline != nullptr && g != 3) {
+                        unsigned long long gt;
+                        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
+                        a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + 4 * l + (g < 3 ? g : 3)) * 8 + 5] = gt;
+                    }
+#endif
                     for (int k = 0; k < nt; ++k, ++t) {
                         const int sl = t % S;
-                        if (t >= S && !mbar_wait_bounded(&s.empty[sl], ((t / S) - 1) & 1)) {
+                        if (t >= S && !mbar_wait_bounded_sleep(&s.empty[sl], ((t / S) - 1) & 1)) {
                             raise_abort(a, s);
                             stop = true;
                             break;
                         }
-                        if (aborted(a, s)) {
+                        if (*(volatile int *) s.abort_local != 0) {
                             stop = true;
                             break;
                         }
@@ -440,6 +478,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     const int qkv_dim = a.Q + 2 * a.KV;
     int       t       = 0;      // tile counter, mirrors the producer
     bool      fail    = false;  // this thread saw a timeout or an abort
+#ifdef B200Q8_TIMELINE
+    long long tl_wait_cycles = 0, tl_dot_cycles = 0;
+#endif
     // Consumes the tiles of one weight segment.  A warp whose wait runs out
     // stops consuming (and stops arriving) but still reaches every barrier.
     auto consume = [&](const Seg & sg, int K, int yoff) {
@@ -451,11 +492,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                 continue;
             }
             const int sl = t % S;
+#ifdef B200Q8_TIMELINE
+            const long long c0 = clock64();
+#endif
             if (!mbar_wait_bounded(&s.full[sl], (t / S) & 1)) {
                 raise_abort(a, s);
                 fail = true;
                 continue;
             }
+#ifdef B200Q8_TIMELINE
+            const long long c1 = clock64();
+#endif
             const int r = k * sg.sr;
             const int R = min(sg.sr, sg.n - r);
             dot_tile_rows<M_T>(s.ring + (size_t) sl * kStepSlotBytes, R, sg.rb, P, NB, s.xc, s.xd, M, warp, lane,
@@ -463,6 +510,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                                    s.ybuf[m * 2 * kStepYMax + yoff + r + rr] = acc;
                                });
             __syncwarp();
+#ifdef B200Q8_TIMELINE
+            const long long c2 = clock64();
+            tl_wait_cycles += c1 - c0;
+            tl_dot_cycles += c2 - c1;
+#endif
             if (lane == 0) {
                 mbar_arrive(&s.empty[sl]);
             }
@@ -486,16 +538,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         const Part pg = part(a.I, G, c);
 
         // ---- qkv = W_qkv * Q(rms_norm(h) * norm_in), h = h1 + d(l-1)
+        TL(4 * l + 0, 0);
         const unsigned long long * prev_d = l > 0 ? a.ll + (size_t) (l - 1) * a.ll_layer + llm * (a.KV + a.H + a.I)
                                                   : nullptr;
         residual_and_rms<M_T>(a, s, prev_d, s.h1buf, s.hbuf, M, epoch, (l > 0 && c == 0) ? trace(l - 1, 9) : nullptr,
-                              fail);
-        stage_activations<M_T, MODE>(a, s, H, M, 0, s.hbuf, L.norm_in, nullptr, 0, false, epoch,
+                              L.norm_in, fail);
+        TL(4 * l + 0, 1);
+        stage_activations<M_T, MODE>(a, s, H, M, 0, s.hbuf, s.normbuf, nullptr, 0, false, epoch,
                                      c == 0 ? trace(l, 0) : nullptr, (size_t) H, fail);
+        TL(4 * l + 0, 2);
         consume(segs[0], H, 0);
+        TL(4 * l + 0, 3);
+        TL_CYC(4 * l + 0);
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
+        TL(4 * l + 0, 4);
         {
             float * tq = trace(l, 1);
             for (int e = t_id; e < M * pq.n; e += kStepConsumers) {
@@ -512,12 +570,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             }
         }
         // ---- o = W_o * Q(attend(v)); attention over one cached position
+        TL(4 * l + 1, 0);
         stage_activations<M_T, MODE>(a, s, a.Q, M, 1, nullptr, nullptr, ll_v, (size_t) a.KV, true, epoch,
                                      c == 0 ? trace(l, 2) : nullptr, (size_t) a.Q, fail);
+        TL(4 * l + 1, 2);
         consume(segs[1], a.Q, 0);
+        TL(4 * l + 1, 3);
+        TL_CYC(4 * l + 1);
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
+        TL(4 * l + 1, 4);
         {
             float * to = trace(l, 3);
             for (int e = t_id; e < M * po.n; e += kStepConsumers) {
@@ -531,14 +594,21 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             }
         }
         // ---- g|u = W_gate|W_up * Q(rms_norm(h1) * norm_post), h1 = h + o
-        residual_and_rms<M_T>(a, s, ll_o, s.hbuf, s.h1buf, M, epoch, c == 0 ? trace(l, 4) : nullptr, fail);
-        stage_activations<M_T, MODE>(a, s, H, M, 0, s.h1buf, L.norm_post, nullptr, 0, false, epoch,
+        TL(4 * l + 2, 0);
+        residual_and_rms<M_T>(a, s, ll_o, s.hbuf, s.h1buf, M, epoch, c == 0 ? trace(l, 4) : nullptr, L.norm_post,
+                              fail);
+        TL(4 * l + 2, 1);
+        stage_activations<M_T, MODE>(a, s, H, M, 0, s.h1buf, s.normbuf, nullptr, 0, false, epoch,
                                      c == 0 ? trace(l, 5) : nullptr, (size_t) H, fail);
+        TL(4 * l + 2, 2);
         consume(segs[2], H, 0);
         consume(segs[3], H, kStepYMax);
+        TL(4 * l + 2, 3);
+        TL_CYC(4 * l + 2);
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
+        TL(4 * l + 2, 4);
         {
             float * tgu = trace(l, 6);
             float * ts  = trace(l, 7);
@@ -559,12 +629,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             }
         }
         // ---- d = W_down * Q(s)
+        TL(4 * l + 3, 0);
         stage_activations<M_T, MODE>(a, s, a.I, M, 1, nullptr, nullptr, ll_s, (size_t) a.I, false, epoch, nullptr,
                                      0, fail);
+        TL(4 * l + 3, 2);
         consume(segs[4], a.I, 0);
+        TL(4 * l + 3, 3);
+        TL_CYC(4 * l + 3);
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
+        TL(4 * l + 3, 4);
         {
             float *    td   = trace(l, 8);
             const bool last = l == a.n_layers - 1;
@@ -592,6 +667,7 @@ size_t decode_step_smem_bytes(const StepArgs & a, int mt, int & n_slots) {
     const int Kmax = std::max(std::max(a.H, a.Q), a.I);
     size_t    off  = kStepHeader;
     off += (size_t) mt * a.H * 4 * 2;
+    off += (size_t) a.H * 4;
     off += (size_t) mt * 2 * kStepYMax * 4;
     off += (size_t) mt * Kmax;
     off += (size_t) mt * (Kmax / kQK) * 4;

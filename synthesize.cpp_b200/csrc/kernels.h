@@ -96,6 +96,7 @@ struct StepArgs {
     size_t               trace_off[10];
     unsigned *           sync;      // [0] launch counter, [1] abort word
     int                  n_slots;   // set by the launcher
+    unsigned long long * timeline;  // analysis builds (B200Q8_TIMELINE) only: stamps, else unused
 };
 
 bool        decode_step_supported(const StepArgs & a, int grid);

@@ -47,10 +47,12 @@ __device__ __forceinline__ void dot_tile_rows(const uint8_t * tile, int R, size_
     while (GS < P && GS < 32) {
         GS <<= 1;
     }
-    const int     RPW     = 32 / GS;
-    const int     sub     = lane / GS;
-    const int     gl      = lane % GS;
-    const uint4 * xv_base = reinterpret_cast<const uint4 *>(xc);
+    const int      RPW    = 32 / GS;
+    const int      sub    = lane / GS;
+    const int      gl     = lane % GS;
+    const uint32_t xc_s   = smem_addr(xc);
+    const uint32_t xd_s   = smem_addr(xd);
+    const uint32_t tile_s = smem_addr(tile);
     for (int rb = warp * RPW; rb < R; rb += n_warps * RPW) {
         const int  rr     = rb + sub;
         const bool active = rr < R;
@@ -60,12 +62,12 @@ __device__ __forceinline__ void dot_tile_rows(const uint8_t * tile, int R, size_
             acc[m] = 0.0f;
         }
         if (active) {
-            const uint32_t * wr = reinterpret_cast<const uint32_t *>(tile + (size_t) rr * row_bytes);
+            const uint32_t wr = tile_s + (uint32_t) ((size_t) rr * row_bytes);
             for (int pp = gl; pp < P; pp += GS) {
                 uint32_t w[17];
 #pragma unroll
                 for (int k = 0; k < 17; ++k) {
-                    w[k] = wr[17 * pp + k];
+                    w[k] = lds_u32(wr + (uint32_t) (68 * pp + 4 * k));
                 }
                 int qa[8];
 #pragma unroll
@@ -77,32 +79,35 @@ __device__ __forceinline__ void dot_tile_rows(const uint8_t * tile, int R, size_
 #pragma unroll
                 for (int m = 0; m < M_T; ++m) {
                     if (m < M) {
-                        const uint4 * xv = xv_base + (size_t) (m * 4) * P + pp;
-                        const uint4   x0 = xv[0];
-                        const uint4   x1 = xv[P];
-                        const uint4   x2 = xv[2 * P];
-                        const uint4   x3 = xv[3 * P];
-                        const float2  dx = *reinterpret_cast<const float2 *>(xd + m * NB + 2 * pp);
-                        int           sA = 0;
-                        int           sB = 0;
+                        const uint32_t xv = xc_s + (uint32_t) (((m * 4) * P + pp) * 16);
+                        const uint4    x0 = lds_v4(xv);
+                        const uint4    x1 = lds_v4(xv + (uint32_t) (P * 16));
+                        const uint4    x2 = lds_v4(xv + (uint32_t) (2 * P * 16));
+                        const uint4    x3 = lds_v4(xv + (uint32_t) (3 * P * 16));
+                        const float2   dx = lds_f2(xd_s + (uint32_t) ((m * NB + 2 * pp) * 4));
+                        int            sA = 0;
+                        int            sB = 0;
+                        int            tA = 0;
+                        int            tB = 0;
+                        // two independent chains per block halve the dp4a latency
                         sA = __dp4a(qa[0], (int) x0.x, sA);
-                        sA = __dp4a(qa[1], (int) x0.y, sA);
+                        tA = __dp4a(qa[1], (int) x0.y, tA);
                         sA = __dp4a(qa[2], (int) x0.z, sA);
-                        sA = __dp4a(qa[3], (int) x0.w, sA);
+                        tA = __dp4a(qa[3], (int) x0.w, tA);
                         sA = __dp4a(qa[4], (int) x1.x, sA);
-                        sA = __dp4a(qa[5], (int) x1.y, sA);
+                        tA = __dp4a(qa[5], (int) x1.y, tA);
                         sA = __dp4a(qa[6], (int) x1.z, sA);
-                        sA = __dp4a(qa[7], (int) x1.w, sA);
+                        tA = __dp4a(qa[7], (int) x1.w, tA);
                         sB = __dp4a((int) w[9], (int) x2.x, sB);
-                        sB = __dp4a((int) w[10], (int) x2.y, sB);
+                        tB = __dp4a((int) w[10], (int) x2.y, tB);
                         sB = __dp4a((int) w[11], (int) x2.z, sB);
-                        sB = __dp4a((int) w[12], (int) x2.w, sB);
+                        tB = __dp4a((int) w[12], (int) x2.w, tB);
                         sB = __dp4a((int) w[13], (int) x3.x, sB);
-                        sB = __dp4a((int) w[14], (int) x3.y, sB);
+                        tB = __dp4a((int) w[14], (int) x3.y, tB);
                         sB = __dp4a((int) w[15], (int) x3.z, sB);
-                        sB = __dp4a((int) w[16], (int) x3.w, sB);
-                        acc[m] = __fmaf_rn((float) sA, __fmul_rn(dA, dx.x), acc[m]);
-                        acc[m] = __fmaf_rn((float) sB, __fmul_rn(dB, dx.y), acc[m]);
+                        tB = __dp4a((int) w[16], (int) x3.w, tB);
+                        acc[m] = __fmaf_rn((float) (sA + tA), __fmul_rn(dA, dx.x), acc[m]);
+                        acc[m] = __fmaf_rn((float) (sB + tB), __fmul_rn(dB, dx.y), acc[m]);
                     }
                 }
             }
