@@ -130,6 +130,23 @@ b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_ro
                                size_t x_col_stride, float * y, size_t y_col_stride, int32_t mode, void * workspace,
                                size_t workspace_bytes, b200q8_stream_t stream);
 
+/* The same MUL_MAT for callers that cannot allocate device memory at the
+ * point of the call -- a ggml backend computing a graph whose buffers were all
+ * placed before the graph ran, a real-time streaming callback that must not
+ * block on cudaMalloc's device-wide synchronisation, code inside a CUDA stream
+ * capture.  No counterpart in the reference (its CPU path allocates nothing
+ * on the device).  It allocates nothing: the quantized activations go to a
+ * fixed 1 MiB array in the library's own device memory, held by every GPU
+ * that loads the library until the process exits.  Requires
+ * M * (K/32) * 34 <= 1048576 bytes (else B200Q8_ERR_INVALID_ARG).  Every call
+ * on a device shares that array, so calls whose kernels overlap on the GPU
+ * race; order them on one stream.  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  Results as b200q8_mul_mat. */
+b200q8_status_t b200q8_mul_mat_noalloc(const void * w, int64_t K, int64_t N, size_t w_row_bytes, const float * x,
+                                       int64_t M, size_t x_col_stride, float * y, size_t y_col_stride, int32_t mode,
+                                       b200q8_stream_t stream);
+
 /* ---- the talker-shaped decode step -------------------------------------- */
 
 /* One decoder layer of the Qwen3 talker as the step chain sees it (ggml

@@ -80,6 +80,8 @@ def lib() -> ctypes.CDLL:
     L.b200q8_mul_mat_workspace_size.restype = sz
     L.b200q8_mul_mat.argtypes = [vp, i64, i64, sz, vp, i64, sz, vp, sz, i32, vp, sz, vp]
     L.b200q8_mul_mat.restype = i32
+    L.b200q8_mul_mat_noalloc.argtypes = [vp, i64, i64, sz, vp, i64, sz, vp, sz, i32, vp]
+    L.b200q8_mul_mat_noalloc.restype = i32
     L.b200q8_chain_create.argtypes = [ctypes.POINTER(ChainDesc), i32, ctypes.POINTER(vp)]
     L.b200q8_chain_create.restype = i32
     L.b200q8_chain_run.argtypes = [vp, vp, vp, vp, i64, vp]

@@ -5,3 +5,4 @@
 #include "decode_step.cu"
 #include "abi.cu"
 #include "chain.cu"
+#include "noalloc.cu"
