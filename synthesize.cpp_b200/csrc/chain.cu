@@ -307,7 +307,10 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
         }
         if (e == cudaSuccess) e = cudaMemset(p2, 0, sizeof(unsigned long long) * c->ll_layer * d.n_layers);
         if (e == cudaSuccess) e = cudaMemset(p3, 0, 64);
-        c->persistent = e == cudaSuccess;
+        StepArgs probe = {};
+        probe.H = (int) H; probe.Q = (int) (d.n_head * d.head_dim); probe.KV = (int) KV; probe.I = (int) I;
+        probe.mode = d.mode;
+        c->persistent = e == cudaSuccess && decode_step_fits(probe);
     }
     for (int l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
         GemvParams p = {};
@@ -349,6 +352,8 @@ b200q8_status_t b200q8_chain_run(b200q8_chain * c, const int32_t * ids, const fl
         a.layers = c->step_layers; a.n_layers = d.n_layers;
         a.H = (int) d.hidden; a.Q = (int) (d.n_head * d.head_dim); a.KV = (int) (d.n_kv * d.head_dim);
         a.I = (int) d.inter; a.head_dim = (int) d.head_dim; a.group = (int) (d.n_head / d.n_kv); a.eps = d.eps;
+        while ((1 << a.lg_head_dim) < a.head_dim) ++a.lg_head_dim;
+        while ((1 << a.lg_group) < a.group) ++a.lg_group;
         a.rb_h = c->rb_h; a.rb_q = c->rb_q; a.rb_i = c->rb_i;
         a.table = static_cast<const uint8_t *>(d.table); a.table_rows = d.table_rows;
         a.ids = ids; a.x_in = x_in; a.h_out = h_out; a.M = (int) M; a.mode = d.mode;

@@ -101,14 +101,32 @@ struct QuantParams {
     unsigned short dbits;  // stored fp16 bits of d
 };
 
+// amax / 127 rounded to nearest (IEEE single division), for amax >= 0.
+// For finite amax: q = RN(amax * r) with r = RN(1/127), then one FMA
+// correction with the exact residual amax - 127*q (the division-by-a-constant
+// scheme of P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", 1990).  It was checked against IEEE division
+// for all 2^31 non-negative finite floats; it uses only correctly rounded
+// multiply and FMA, so it gives the same bits on any IEEE machine.
+// Infinity and NaN take the plain division.
+__device__ __forceinline__ float div127_rn(float amax) {
+    if (!(amax <= 3.40282347e38f)) {
+        return __fdiv_rn(amax, 127.0f);
+    }
+    const float r = 0.00787401574803149606f;  // RN(1/127)
+    const float q = __fmul_rn(amax, r);
+    const float e = __fmaf_rn(-q, 127.0f, amax);
+    return __fmaf_rn(e, r, q);
+}
+
 template <int MODE>
 __device__ __forceinline__ QuantParams quant_params(float amax) {
     QuantParams p;
-    const float d = __fdiv_rn(amax, 127.0f);
+    const float d = div127_rn(amax);
     if (MODE == B200Q8_QUANT_CPU_X86) {
         p.id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
     } else {
-        p.id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+        p.id = (d != 0.0f) ? __frcp_rn(d) : 0.0f;  // IEEE reciprocal == 1.0f/d
     }
     if (isnan(d)) {
         p.dbits = 0x7e00u;
@@ -216,8 +234,19 @@ __device__ __forceinline__ float2 lds_f2(uint32_t addr) {
     return v;
 }
 
+// Non-blocking probe of a phase (no suspension, unlike try_wait).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t * bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t * bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) {
+    if (mbar_test_wait(bar, parity)) {
         return true;
     }
     const long long start = clock64();

@@ -43,7 +43,7 @@ namespace b200q8 {
 
 namespace {
 
-constexpr int kStepConsumerWarps = 16;
+constexpr int kStepConsumerWarps = 12;
 constexpr int kStepConsumers     = kStepConsumerWarps * 32;
 constexpr int kStepThreads       = kStepConsumers + 32;
 constexpr int kStepSlotBytes     = 16384;
@@ -85,16 +85,8 @@ __device__ __forceinline__ void tl_stamp(const StepArgs & a, int op, int ev) {
     }
 }
 #define TL(op, ev) tl_stamp(a, (op), (ev))
-#define TL_CYC(op)                                                                                      \
-    do {                                                                                                \
-        if (threadIdx.x == 0 && a.timeline != nullptr) {                                                \
-            a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + (op)) * 8 + 6] = tl_wait_cycles;        \
-            a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + (op)) * 8 + 7] = tl_dot_cycles;         \
-        }                                                                                               \
-    } while (0)
 #else
 #define TL(op, ev) ((void) 0)
-#define TL_CYC(op) ((void) 0)
 #endif
 
 struct Part {
@@ -116,7 +108,11 @@ struct Seg {
 };
 
 __device__ __forceinline__ int seg_tiles(const Seg & s) {
-    return s.n > 0 ? (s.n + s.sr - 1) / s.sr : 0;
+    int t = 0;
+    for (int r = 0; r < s.n; r += s.sr) {
+        ++t;
+    }
+    return t;
 }
 
 struct Smem {
@@ -124,7 +120,7 @@ struct Smem {
     uint64_t * empty;
     unsigned * epoch;
     int *      abort_local;
-    double *   rms_part;   // [kStepConsumerWarps][2]
+    double *   rms_part;   // [kStepConsumerWarps][2] (header room for 16 warps)
     float *    rms_scale;  // [2]
     float *    hbuf;       // [M_T][H]
     float *    h1buf;      // [M_T][H]
@@ -135,23 +131,33 @@ struct Smem {
     uint8_t *  ring;
 };
 
-// The 5 weight segments of layer l for CTA c, in streaming order:
+// This CTA's row slices and tile sizes, the same for every layer; computed
+// once per launch (each holds runtime divisions).
+struct Plan {
+    Part pq, ph, pi;       // rows of q|k|v, of H (o and down), of I (gate and up)
+    int  sr_h, sr_q, sr_i;  // rows per 16 KiB slot for K = H, Q, I
+};
+
+__device__ __forceinline__ Plan make_plan(const StepArgs & a, int c, int G) {
+    Plan p;
+    p.pq   = part(a.Q + 2 * a.KV, G, c);
+    p.ph   = part(a.H, G, c);
+    p.pi   = part(a.I, G, c);
+    p.sr_h = max(1, (int) (kStepSlotBytes / a.rb_h));
+    p.sr_q = max(1, (int) (kStepSlotBytes / a.rb_q));
+    p.sr_i = max(1, (int) (kStepSlotBytes / a.rb_i));
+    return p;
+}
+
+// The 5 weight segments of layer l for this CTA, in streaming order:
 // qkv, o, gate, up, down.
-__device__ __forceinline__ void layer_segs(const StepArgs & a, int l, int c, int G, Seg (&segs)[5]) {
-    const StepLayerDev & L   = a.layers[l];
-    const int            qkv = a.Q + 2 * a.KV;
-    const Part           pq  = part(qkv, G, c);
-    const Part           po  = part(a.H, G, c);
-    const Part           pg  = part(a.I, G, c);
-    const Part           pd  = part(a.H, G, c);
-    const int            sr_h = max(1, (int) (kStepSlotBytes / a.rb_h));
-    const int            sr_q = max(1, (int) (kStepSlotBytes / a.rb_q));
-    const int            sr_i = max(1, (int) (kStepSlotBytes / a.rb_i));
-    segs[0] = { L.w_qkv + (size_t) pq.r0 * a.rb_h, a.rb_h, pq.n, sr_h };
-    segs[1] = { L.w_o + (size_t) po.r0 * a.rb_q, a.rb_q, po.n, sr_q };
-    segs[2] = { L.w_gate + (size_t) pg.r0 * a.rb_h, a.rb_h, pg.n, sr_h };
-    segs[3] = { L.w_up + (size_t) pg.r0 * a.rb_h, a.rb_h, pg.n, sr_h };
-    segs[4] = { L.w_down + (size_t) pd.r0 * a.rb_i, a.rb_i, pd.n, sr_i };
+__device__ __forceinline__ void layer_segs(const StepArgs & a, const Plan & p, int l, Seg (&segs)[5]) {
+    const StepLayerDev & L = a.layers[l];
+    segs[0] = { L.w_qkv + (size_t) p.pq.r0 * a.rb_h, a.rb_h, p.pq.n, p.sr_h };
+    segs[1] = { L.w_o + (size_t) p.ph.r0 * a.rb_q, a.rb_q, p.ph.n, p.sr_q };
+    segs[2] = { L.w_gate + (size_t) p.pi.r0 * a.rb_h, a.rb_h, p.pi.n, p.sr_h };
+    segs[3] = { L.w_up + (size_t) p.pi.r0 * a.rb_h, a.rb_h, p.pi.n, p.sr_h };
+    segs[4] = { L.w_down + (size_t) p.ph.r0 * a.rb_i, a.rb_i, p.ph.n, p.sr_i };
 }
 
 __device__ __forceinline__ bool aborted(const StepArgs & a, const Smem & s) {
@@ -213,57 +219,60 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
     for (int m = 0; m < M_T; ++m) {
         ss[m] = 0.0;
     }
-    constexpr int kPer = 4;  // elements per thread per pass (H <= 4 * 512 * passes)
-    for (int base = 0; base < M * H; base += kStepConsumers * kPer) {
-        const unsigned long long * src[kPer];
-        unsigned long long         w[kPer];
-        int                        n = 0;
+    constexpr int kPer = 4;  // elements in flight per thread per pass
 #pragma unroll
-        for (int i = 0; i < kPer; ++i) {
-            const int e = base + i * kStepConsumers + t;
-            src[i]      = delta != nullptr ? delta + (e < M * H ? e : 0) : nullptr;
-            w[i]        = 0;
-            if (e < M * H) {
-                n = i + 1;
-            }
+    for (int m = 0; m < M_T; ++m) {
+        if (m >= M) {
+            break;
         }
-        if (delta != nullptr) {
+        const unsigned long long * dm  = delta != nullptr ? delta + (size_t) m * H : nullptr;
+        float *                    hd  = h_dst + (size_t) m * H;
+        const float *              hs  = h_src + (size_t) m * H;
+        for (int base = 0; base < H; base += kStepConsumers * kPer) {
+            const unsigned long long * src[kPer];
+            unsigned long long         w[kPer];
+            int                        n = 0;
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
-                if (i < n) {
-                    w[i] = ld_ll(src[i]);
+                const int e = base + i * kStepConsumers + t;
+                src[i]      = dm != nullptr ? dm + (e < H ? e : 0) : nullptr;
+                w[i]        = 0;
+                if (e < H) {
+                    n = i + 1;
                 }
             }
-            if (!fail && !ll_settle<kPer>(a, s, src, w, n, epoch)) {
-                fail = true;
-            }
-        }
+            if (dm != nullptr) {
 #pragma unroll
-        for (int i = 0; i < kPer; ++i) {
-            const int e = base + i * kStepConsumers + t;
-            if (e < M * H) {
-                const int m = e / H;
-                float     v;
-                if (delta != nullptr) {
-                    v = __fadd_rn(h_src[e], __uint_as_float((unsigned) (w[i] & 0xffffffffu)));
-                    h_dst[e] = v;
-                    if (trace_h != nullptr) {
-                        trace_h[e] = v;
+                for (int i = 0; i < kPer; ++i) {
+                    if (i < n) {
+                        w[i] = ld_ll(src[i]);
                     }
-                } else {
-                    v = h_dst[e];
                 }
+                if (!fail && !ll_settle<kPer>(a, s, src, w, n, epoch)) {
+                    fail = true;
+                }
+            }
 #pragma unroll
-                for (int mm = 0; mm < M_T; ++mm) {
-                    if (mm == m) {
-                        ss[mm] += (double) __fmul_rn(v, v);
+            for (int i = 0; i < kPer; ++i) {
+                const int e = base + i * kStepConsumers + t;
+                if (e < H) {
+                    float v;
+                    if (dm != nullptr) {
+                        v     = __fadd_rn(hs[e], __uint_as_float((unsigned) (w[i] & 0xffffffffu)));
+                        hd[e] = v;
+                        if (trace_h != nullptr) {
+                            trace_h[(size_t) m * H + e] = v;
+                        }
+                    } else {
+                        v = hd[e];
                     }
+                    ss[m] += (double) __fmul_rn(v, v);
                 }
             }
         }
     }
-    const int warp = t / 32;
-    const int lane = t % 32;
+    const int warp = t >> 5;
+    const int lane = t & 31;
 #pragma unroll
     for (int m = 0; m < M_T; ++m) {
 #pragma unroll
@@ -294,18 +303,16 @@ template <int M_T, int MODE>
 __device__ void stage_activations(const StepArgs & a, const Smem & s, int K, int M, int src_kind,
                                   const float * hsrc, const float * norm, const unsigned long long * ll, size_t ll_stride,
                                   bool map_gqa, unsigned epoch, float * trace_x, size_t trace_stride, bool & fail) {
-    const int warp = threadIdx.x / 32;
-    const int lane = threadIdx.x % 32;
-    const int NB   = K / kQK;
-    const int P    = K / 64;
-    const int g4   = lane / 4;
-    const int e4   = lane % 4;
-    for (int base = warp * 8; base < M * NB; base += kStepConsumerWarps * 8) {
-        const int  blk   = base + g4;
-        const bool valid = blk < M * NB;
-        const int  m     = valid ? blk / NB : 0;
-        const int  b     = valid ? blk % NB : 0;
-        const int  i0    = b * kQK + e4 * 8;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int NB   = K >> 5;
+    const int g4   = lane >> 2;
+    const int e4   = lane & 3;
+    for (int m = 0; m < M; ++m)
+    for (int base = warp * 8; base < NB; base += kStepConsumerWarps * 8) {
+        const int  b     = base + g4;
+        const bool valid = b < NB;
+        const int  i0    = (valid ? b : 0) * kQK + e4 * 8;
         float      v[8];
         if (src_kind == 0) {
 #pragma unroll
@@ -319,8 +326,8 @@ __device__ void stage_activations(const StepArgs & a, const Smem & s, int K, int
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 int j = i0 + k;
-                if (map_gqa) {
-                    j = ((j / a.head_dim) / a.group) * a.head_dim + j % a.head_dim;
+                if (map_gqa) {  // query head j >> lg_hd reads kv head (j >> lg_hd) >> lg_group
+                    j = (((j >> a.lg_head_dim) >> a.lg_group) << a.lg_head_dim) | (j & ((1 << a.lg_head_dim) - 1));
                 }
                 src[k] = ll + (size_t) m * ll_stride + j;
                 w[k]   = valid ? ld_ll(src[k]) : ((unsigned long long) epoch << 32);
@@ -342,10 +349,9 @@ __device__ void stage_activations(const StepArgs & a, const Smem & s, int K, int
             hi |= (uint32_t) (quant_code<MODE>(v[4 + k], qp.id) & 0xff) << (8 * k);
         }
         if (valid) {
-            const int pp  = b >> 1;
-            const int pos = ((b & 1) << 5) + e4 * 8;
-            const int wi  = pos >> 2;  // even
-            uint2 *   dst = reinterpret_cast<uint2 *>(s.xc + ((size_t) (m * 4 + (wi >> 2)) * P + pp) * 16 + (wi & 3) * 4);
+            // chunk-major layout of tile_dot.cuh's superblock path
+            const int pos = ((b & 7) << 5) + e4 * 8;
+            uint2 *   dst = reinterpret_cast<uint2 *>(s.xc + sb_code_offset(m, K, K >> 8, b >> 3, pos));
             *dst          = make_uint2(lo, hi);
             if (e4 == 0) {
                 s.xd[m * NB + b] = qp.d;
@@ -359,6 +365,119 @@ __device__ void stage_activations(const StepArgs & a, const Smem & s, int K, int
         }
     }
     named_barrier_sync(1, kStepConsumers);
+}
+
+// Consumes all tiles of one op in a single pass over all consumer warps.
+// The op's rows come from segs[0..nseg) in streaming order; with pair_units
+// the op has two segments of equal length (gate, up) and unit u is the row
+// pair (seg0 row u, seg1 row u), computed by one lane group so that SwiGLU
+// can be applied before publishing.  Otherwise nseg == 1 and unit u is row u.
+// publish(u, acc0, acc1) is called by lane 0 of the unit's group.
+template <int M_T, typename Pub>
+__device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, int S, int & sl, uint32_t & ph,
+                                           const Seg * segs, int nseg, bool pair_units, int K, int M, int warp,
+                                           int lane, bool & fail, int op, Pub && publish) {
+    constexpr int kMaxOpTiles = 16;
+    int           t_sl[kMaxOpTiles];
+    uint32_t      t_ph[kMaxOpTiles];
+    int           seg_first[2] = { 0, 0 };
+    int           nt           = 0;
+    for (int g = 0; g < nseg; ++g) {
+        seg_first[g] = nt;
+        for (int r = 0; r < segs[g].n; r += segs[g].sr) {
+            if (nt < kMaxOpTiles) {
+                t_sl[nt] = sl;
+                t_ph[nt] = ph;
+            }
+            ++nt;
+            if (++sl == S) {
+                sl = 0;
+                ph ^= 1u;
+            }
+        }
+    }
+#ifdef B200Q8_TIMELINE
+    const long long tc0 = clock64();
+#endif
+    bool bad = fail || nt > kMaxOpTiles;
+    for (int i = 0; i < nt && !bad; ++i) {
+        if (!mbar_wait_bounded(&s.full[t_sl[i]], t_ph[i])) {
+            raise_abort(a, s);
+            bad = true;
+        }
+    }
+    bad  = __any_sync(0xffffffffu, bad);
+    fail = fail || bad;
+#ifdef B200Q8_TIMELINE
+    const long long tc1 = clock64();
+    long long       tc_pub = 0;
+#endif
+    if (!bad) {
+        const int      NSB    = K >> 8;  // superblocks per row
+        const int      NB     = K >> 5;
+        const int      lgs    = NSB <= 1 ? 0 : min(5, 32 - __clz(NSB - 1));  // ~1 superblock per lane
+        const int      GS     = 1 << lgs;
+        const int      gpw    = 32 >> lgs;  // groups per warp
+        const int      ngroup = kStepConsumerWarps * gpw;
+        const int      gl     = lane & (GS - 1);
+        const uint32_t xc_s   = smem_addr(s.xc);
+        const uint32_t xd_s   = smem_addr(s.xd);
+        const uint32_t ring_s = smem_addr(s.ring);
+        const int      nunit  = segs[0].n;
+        auto row_addr = [&](int g, int r) -> uint32_t {
+            int ti = 0;
+            while (r >= segs[g].sr) {
+                r -= segs[g].sr;
+                ++ti;
+            }
+            return ring_s + (uint32_t) (t_sl[seg_first[g] + ti] * kStepSlotBytes) + (uint32_t) (r * segs[g].rb);
+        };
+        for (int ub = warp * gpw; ub < nunit; ub += ngroup) {  // warp-uniform
+            const int  u      = ub + (lane >> lgs);
+            const bool active = u < nunit;
+            float      acc0[M_T], acc1[M_T];
+#pragma unroll
+            for (int m = 0; m < M_T; ++m) {
+                acc0[m] = 0.0f;
+                acc1[m] = 0.0f;
+            }
+            if (active) {
+                dot_row_sb<M_T>(row_addr(0, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc0);
+                if (pair_units) {
+                    dot_row_sb<M_T>(row_addr(1, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc1);
+                }
+            }
+            group_reduce<M_T>(acc0, GS);
+            if (pair_units) {
+                group_reduce<M_T>(acc1, GS);
+            }
+#ifdef B200Q8_TIMELINE
+            const long long tp0 = clock64();
+#endif
+            if (active && gl == 0) {
+                publish(u, acc0, acc1);
+            }
+#ifdef B200Q8_TIMELINE
+            __syncwarp();
+            tc_pub += clock64() - tp0;
+#endif
+        }
+    }
+    __syncwarp();
+#ifdef B200Q8_TIMELINE
+    if (threadIdx.x == 0 && a.timeline != nullptr) {
+        const long long tc2 = clock64();
+        // [6] = tile waits, [7] = dot + reduce, packed with publish in the high half
+        a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + op) * 8 + 6] = (unsigned long long) (tc1 - tc0);
+        a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + op) * 8 + 7] =
+            (unsigned long long) (tc2 - tc1 - tc_pub) | ((unsigned long long) tc_pub << 32);
+    }
+#endif
+    if (lane == 0 && nt <= kMaxOpTiles) {
+        for (int i = 0; i < nt; ++i) {
+            mbar_arrive(&s.empty[t_sl[i]]);
+        }
+    }
 }
 
 template <int M_T, int MODE>
@@ -406,20 +525,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     }
     __syncthreads();
     const unsigned epoch = *s.epoch;
-    const int      warp  = threadIdx.x / 32;
-    const int      lane  = threadIdx.x % 32;
+    const int      warp  = threadIdx.x >> 5;
+    const int      lane  = threadIdx.x & 31;
+    const Plan     plan  = make_plan(a, c, G);
 
     if (warp == kStepConsumerWarps) {
         // ------------------------------------------------------- producer
         if (lane == 0) {
-            const uint64_t pol    = l2_evict_first_policy();
-            int            t      = 0;
-            bool           stop   = false;
+            const uint64_t pol     = l2_evict_first_policy();
+            int            t       = 0;  // tiles issued
+            int            sl      = 0;  // slot of tile t
+            uint32_t       ph      = 0;  // fill round of slot sl, mod 2
+            bool           stop    = false;
             for (int l = 0; l < a.n_layers && !stop; ++l) {
                 Seg segs[5];
-                layer_segs(a, l, c, G, segs);
+                layer_segs(a, plan, l, segs);
                 for (int g = 0; g < 5 && !stop; ++g) {
-                    const int nt = seg_tiles(segs[g]);
 #ifdef B200Q8_TIMELINE
                     if (a.timeline != nullptr && g != 3) {
                         unsigned long long gt;
@@ -427,9 +548,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                         a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + 4 * l + (g < 3 ? g : 3)) * 8 + 5] = gt;
                     }
 #endif
-                    for (int k = 0; k < nt; ++k, ++t) {
-                        const int sl = t % S;
-                        if (t >= S && !mbar_wait_bounded_sleep(&s.empty[sl], ((t / S) - 1) & 1)) {
+                    for (int r = 0; r < segs[g].n; r += segs[g].sr) {
+                        // slot sl was last filled in round ph^1: wait until it was released
+                        if (t >= S && !mbar_wait_bounded_sleep(&s.empty[sl], ph ^ 1u)) {
                             raise_abort(a, s);
                             stop = true;
                             break;
@@ -438,15 +559,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                             stop = true;
                             break;
                         }
-                        const int      r     = k * segs[g].sr;
                         const int      R     = min(segs[g].sr, segs[g].n - r);
                         const uint32_t bytes = (uint32_t) ((size_t) R * segs[g].rb);
                         mbar_arrive_expect_tx(&s.full[sl], bytes);
                         bulk_copy_g2s(s.ring + (size_t) sl * kStepSlotBytes, segs[g].base + (size_t) r * segs[g].rb,
                                       bytes, &s.full[sl], pol);
+                        ++t;
+                        if (++sl == S) {
+                            sl = 0;
+                            ph ^= 1u;
+                        }
                     }
                 }
             }
+            // never leave with a copy in flight into this CTA's shared memory
             for (int u = max(0, t - S); u < t; ++u) {
                 if (!mbar_wait_bounded(&s.full[u % S], (u / S) & 1)) {
                     record_device_error((unsigned) B200Q8_ERR_DEVICE_TIMEOUT);
@@ -459,71 +585,35 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     // ----------------------------------------------------------- consumers
     const int t_id = threadIdx.x;
     // step input: h = x_in + get_rows(table, ids), every CTA for itself
-    for (int e = t_id; e < M * H; e += kStepConsumers) {
-        const int     m  = e / H;
-        const int     k  = e % H;
-        const int64_t r  = a.ids[m];
-        float         ev = 0.0f;
-        if (r >= 0 && r < a.table_rows) {
-            const uint8_t * blk = a.table + r * a.rb_h + (k / kQK) * kBlockBytes;
-            const float     d   = __half2float(__ushort_as_half((unsigned short) (blk[0] | (blk[1] << 8))));
-            ev                  = __fmul_rn((float) (int8_t) blk[2 + k % kQK], d);
-        } else if (c == 0 && k == 0) {
+    for (int m = 0; m < M; ++m) {
+        const int64_t r     = a.ids[m];
+        const bool    in_tb = r >= 0 && r < a.table_rows;
+        if (!in_tb && c == 0 && t_id == 0) {
             record_device_error((unsigned) B200Q8_ERR_INVALID_ARG);
         }
-        s.hbuf[e] = __fadd_rn(a.x_in[e], ev);
+        for (int k = t_id; k < H; k += kStepConsumers) {
+            float ev = 0.0f;
+            if (in_tb) {
+                const uint8_t * blk = a.table + r * a.rb_h + (k >> 5) * kBlockBytes;
+                const float     d   = __half2float(__ushort_as_half((unsigned short) (blk[0] | (blk[1] << 8))));
+                ev                  = __fmul_rn((float) (int8_t) blk[2 + (k & 31)], d);
+            }
+            s.hbuf[m * H + k] = __fadd_rn(a.x_in[(size_t) m * H + k], ev);
+        }
     }
     named_barrier_sync(1, kStepConsumers);
 
     const int qkv_dim = a.Q + 2 * a.KV;
-    int       t       = 0;      // tile counter, mirrors the producer
+    int       sl      = 0;      // slot of the next tile, mirrors the producer
+    uint32_t  ph      = 0;      // its fill round mod 2
     bool      fail    = false;  // this thread saw a timeout or an abort
-#ifdef B200Q8_TIMELINE
-    long long tl_wait_cycles = 0, tl_dot_cycles = 0;
-#endif
-    // Consumes the tiles of one weight segment.  A warp whose wait runs out
-    // stops consuming (and stops arriving) but still reaches every barrier.
-    auto consume = [&](const Seg & sg, int K, int yoff) {
-        const int NB = K / kQK;
-        const int P  = K / 64;
-        const int nt = seg_tiles(sg);
-        for (int k = 0; k < nt; ++k, ++t) {
-            if (fail) {
-                continue;
-            }
-            const int sl = t % S;
-#ifdef B200Q8_TIMELINE
-            const long long c0 = clock64();
-#endif
-            if (!mbar_wait_bounded(&s.full[sl], (t / S) & 1)) {
-                raise_abort(a, s);
-                fail = true;
-                continue;
-            }
-#ifdef B200Q8_TIMELINE
-            const long long c1 = clock64();
-#endif
-            const int r = k * sg.sr;
-            const int R = min(sg.sr, sg.n - r);
-            dot_tile_rows<M_T>(s.ring + (size_t) sl * kStepSlotBytes, R, sg.rb, P, NB, s.xc, s.xd, M, warp, lane,
-                               kStepConsumerWarps, [&](int rr, int m, float acc) {
-                                   s.ybuf[m * 2 * kStepYMax + yoff + r + rr] = acc;
-                               });
-            __syncwarp();
-#ifdef B200Q8_TIMELINE
-            const long long c2 = clock64();
-            tl_wait_cycles += c1 - c0;
-            tl_dot_cycles += c2 - c1;
-#endif
-            if (lane == 0) {
-                mbar_arrive(&s.empty[sl]);
-            }
-        }
-    };
     auto trace = [&](int l, int which) -> float * {
         return a.trace ? a.trace + (size_t) l * a.trace_layer + a.trace_off[which] : nullptr;
     };
     const size_t llm = (size_t) a.ll_m;  // token stride of the LL buffers
+    const Part   pq  = plan.pq;
+    const Part   po  = plan.ph;
+    const Part   pg  = plan.pi;
 
     for (int l = 0; l < a.n_layers; ++l) {
         const StepLayerDev &       L    = a.layers[l];
@@ -532,12 +622,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         unsigned long long * const ll_s = ll_o + llm * a.H;
         unsigned long long * const ll_d = ll_s + llm * a.I;
         Seg                        segs[5];
-        layer_segs(a, l, c, G, segs);
-        const Part pq = part(qkv_dim, G, c);
-        const Part po = part(a.H, G, c);
-        const Part pg = part(a.I, G, c);
+        layer_segs(a, plan, l, segs);
 
-        // ---- qkv = W_qkv * Q(rms_norm(h) * norm_in), h = h1 + d(l-1)
+        // ---- qkv = W_qkv * Q(rms_norm(h) * norm_in), h = h1 + d(l-1); v published
         TL(4 * l + 0, 0);
         const unsigned long long * prev_d = l > 0 ? a.ll + (size_t) (l - 1) * a.ll_layer + llm * (a.KV + a.H + a.I)
                                                   : nullptr;
@@ -547,53 +634,55 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         stage_activations<M_T, MODE>(a, s, H, M, 0, s.hbuf, s.normbuf, nullptr, 0, false, epoch,
                                      c == 0 ? trace(l, 0) : nullptr, (size_t) H, fail);
         TL(4 * l + 0, 2);
-        consume(segs[0], H, 0);
+        {
+            float * tq = trace(l, 1);
+            consume_op<M_T>(a, s, S, sl, ph, &segs[0], 1, false, H, M, warp, lane, fail, 4 * l + 0,
+                            [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
+                                const int row = pq.r0 + u;
+#pragma unroll
+                                for (int m = 0; m < M_T; ++m) {
+                                    if (m < M) {
+                                        if (row >= a.Q + a.KV) {
+                                            st_ll(ll_v + (size_t) m * a.KV + (row - a.Q - a.KV), y[m], epoch);
+                                        }
+                                        if (tq) {
+                                            tq[(size_t) m * qkv_dim + row] = y[m];
+                                        }
+                                    }
+                                }
+                            });
+        }
         TL(4 * l + 0, 3);
-        TL_CYC(4 * l + 0);
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
         TL(4 * l + 0, 4);
-        {
-            float * tq = trace(l, 1);
-            for (int e = t_id; e < M * pq.n; e += kStepConsumers) {
-                const int   m   = e / pq.n;
-                const int   i   = e % pq.n;
-                const int   row = pq.r0 + i;
-                const float v   = s.ybuf[m * 2 * kStepYMax + i];
-                if (row >= a.Q + a.KV) {
-                    st_ll(ll_v + (size_t) m * a.KV + (row - a.Q - a.KV), v, epoch);
-                }
-                if (tq) {
-                    tq[(size_t) m * qkv_dim + row] = v;
-                }
-            }
-        }
-        // ---- o = W_o * Q(attend(v)); attention over one cached position
+        // ---- o = W_o * Q(attend(v)); attention over one cached position; o published
         TL(4 * l + 1, 0);
         stage_activations<M_T, MODE>(a, s, a.Q, M, 1, nullptr, nullptr, ll_v, (size_t) a.KV, true, epoch,
                                      c == 0 ? trace(l, 2) : nullptr, (size_t) a.Q, fail);
         TL(4 * l + 1, 2);
-        consume(segs[1], a.Q, 0);
+        {
+            float * to = trace(l, 3);
+            consume_op<M_T>(a, s, S, sl, ph, &segs[1], 1, false, a.Q, M, warp, lane, fail, 4 * l + 1,
+                            [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
+#pragma unroll
+                                for (int m = 0; m < M_T; ++m) {
+                                    if (m < M) {
+                                        st_ll(ll_o + (size_t) m * a.H + po.r0 + u, y[m], epoch);
+                                        if (to) {
+                                            to[(size_t) m * a.H + po.r0 + u] = y[m];
+                                        }
+                                    }
+                                }
+                            });
+        }
         TL(4 * l + 1, 3);
-        TL_CYC(4 * l + 1);
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
         TL(4 * l + 1, 4);
-        {
-            float * to = trace(l, 3);
-            for (int e = t_id; e < M * po.n; e += kStepConsumers) {
-                const int   m = e / po.n;
-                const int   i = e % po.n;
-                const float v = s.ybuf[m * 2 * kStepYMax + i];
-                st_ll(ll_o + (size_t) m * a.H + po.r0 + i, v, epoch);
-                if (to) {
-                    to[(size_t) m * a.H + po.r0 + i] = v;
-                }
-            }
-        }
-        // ---- g|u = W_gate|W_up * Q(rms_norm(h1) * norm_post), h1 = h + o
+        // ---- g|u = W_gate|W_up * Q(rms_norm(h1) * norm_post), h1 = h + o; s = silu(g)*u published
         TL(4 * l + 2, 0);
         residual_and_rms<M_T>(a, s, ll_o, s.hbuf, s.h1buf, M, epoch, c == 0 ? trace(l, 4) : nullptr, L.norm_post,
                               fail);
@@ -601,63 +690,63 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         stage_activations<M_T, MODE>(a, s, H, M, 0, s.h1buf, s.normbuf, nullptr, 0, false, epoch,
                                      c == 0 ? trace(l, 5) : nullptr, (size_t) H, fail);
         TL(4 * l + 2, 2);
-        consume(segs[2], H, 0);
-        consume(segs[3], H, kStepYMax);
+        {
+            float * tgu = trace(l, 6);
+            float * ts  = trace(l, 7);
+            consume_op<M_T>(a, s, S, sl, ph, &segs[2], 2, true, H, M, warp, lane, fail, 4 * l + 2,
+                            [&](int u, const float (&g)[M_T], const float (&up)[M_T]) {
+#pragma unroll
+                                for (int m = 0; m < M_T; ++m) {
+                                    if (m < M) {
+                                        const float sv = __fmul_rn(silu_f32(g[m]), up[m]);
+                                        st_ll(ll_s + (size_t) m * a.I + pg.r0 + u, sv, epoch);
+                                        if (tgu) {
+                                            tgu[(size_t) m * 2 * a.I + pg.r0 + u]       = g[m];
+                                            tgu[(size_t) m * 2 * a.I + a.I + pg.r0 + u] = up[m];
+                                        }
+                                        if (ts) {
+                                            ts[(size_t) m * a.I + pg.r0 + u] = sv;
+                                        }
+                                    }
+                                }
+                            });
+        }
         TL(4 * l + 2, 3);
-        TL_CYC(4 * l + 2);
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
         TL(4 * l + 2, 4);
-        {
-            float * tgu = trace(l, 6);
-            float * ts  = trace(l, 7);
-            for (int e = t_id; e < M * pg.n; e += kStepConsumers) {
-                const int   m  = e / pg.n;
-                const int   i  = e % pg.n;
-                const float gv = s.ybuf[m * 2 * kStepYMax + i];
-                const float uv = s.ybuf[m * 2 * kStepYMax + kStepYMax + i];
-                const float sv = __fmul_rn(silu_f32(gv), uv);
-                st_ll(ll_s + (size_t) m * a.I + pg.r0 + i, sv, epoch);
-                if (tgu) {
-                    tgu[(size_t) m * 2 * a.I + pg.r0 + i]       = gv;
-                    tgu[(size_t) m * 2 * a.I + a.I + pg.r0 + i] = uv;
-                }
-                if (ts) {
-                    ts[(size_t) m * a.I + pg.r0 + i] = sv;
-                }
-            }
-        }
-        // ---- d = W_down * Q(s)
+        // ---- d = W_down * Q(s); d published (the last layer writes h_out = h1 + d)
         TL(4 * l + 3, 0);
         stage_activations<M_T, MODE>(a, s, a.I, M, 1, nullptr, nullptr, ll_s, (size_t) a.I, false, epoch, nullptr,
                                      0, fail);
         TL(4 * l + 3, 2);
-        consume(segs[4], a.I, 0);
+        {
+            float *    td   = trace(l, 8);
+            const bool last = l == a.n_layers - 1;
+            consume_op<M_T>(a, s, S, sl, ph, &segs[4], 1, false, a.I, M, warp, lane, fail, 4 * l + 3,
+                            [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
+                                const int row = po.r0 + u;
+#pragma unroll
+                                for (int m = 0; m < M_T; ++m) {
+                                    if (m < M) {
+                                        if (last) {
+                                            a.h_out[(size_t) m * H + row] = __fadd_rn(s.h1buf[m * H + row], y[m]);
+                                        } else {
+                                            st_ll(ll_d + (size_t) m * a.H + row, y[m], epoch);
+                                        }
+                                        if (td) {
+                                            td[(size_t) m * a.H + row] = y[m];
+                                        }
+                                    }
+                                }
+                            });
+        }
         TL(4 * l + 3, 3);
-        TL_CYC(4 * l + 3);
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
         TL(4 * l + 3, 4);
-        {
-            float *    td   = trace(l, 8);
-            const bool last = l == a.n_layers - 1;
-            for (int e = t_id; e < M * po.n; e += kStepConsumers) {
-                const int   m   = e / po.n;
-                const int   i   = e % po.n;
-                const int   row = po.r0 + i;
-                const float v   = s.ybuf[m * 2 * kStepYMax + i];
-                if (last) {
-                    a.h_out[(size_t) m * H + row] = __fadd_rn(s.h1buf[m * H + row], v);
-                } else {
-                    st_ll(ll_d + (size_t) m * a.H + row, v, epoch);
-                }
-                if (td) {
-                    td[(size_t) m * a.H + row] = v;
-                }
-            }
-        }
     }
 }
 
@@ -685,6 +774,9 @@ bool decode_step_supported(const StepArgs & a, int G) {
     if (a.M < 1 || a.M > 2 || a.H % 256 || a.Q % 256 || a.I % 256 || a.KV % 32) {
         return false;
     }
+    if ((1 << a.lg_head_dim) != a.head_dim || (1 << a.lg_group) != a.group) {
+        return false;  // the GQA expansion uses shifts
+    }
     // every CTA's slice of one op must fit the output staging buffer
     const int qkv = a.Q + 2 * a.KV;
     if ((qkv + G - 1) / G > 2 * kStepYMax || (a.I + G - 1) / G > kStepYMax || (a.H + G - 1) / G > kStepYMax) {
@@ -694,7 +786,53 @@ bool decode_step_supported(const StepArgs & a, int G) {
         return false;
     }
     int slots = 0;
-    return decode_step_smem_bytes(a, a.M <= 1 ? 1 : 2, slots) > 0 && slots >= 2;
+    if (decode_step_smem_bytes(a, a.M <= 1 ? 1 : 2, slots) == 0 || slots < 2) {
+        return false;
+    }
+    // consume_op holds all tiles of one op at once: they must fit the ring
+    auto tiles = [&](int rows_total, size_t rb) {
+        const int rows = (rows_total + G - 1) / G;
+        const int sr   = std::max(1, (int) (kStepSlotBytes / rb));
+        return (rows + sr - 1) / sr;
+    };
+    const int worst = std::max(std::max(tiles(qkv, a.rb_h), tiles(a.H, a.rb_q)),
+                               std::max(2 * tiles(a.I, a.rb_h), tiles(a.H, a.rb_i)));
+    return worst <= std::min(slots, 16);
+}
+
+namespace {
+using StepFn = void (*)(const StepArgs);
+
+StepFn pick_step_kernel(int mode, int mt) {
+    switch (mode) {
+        case B200Q8_QUANT_CPU_X86:
+            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_X86> : decode_step_kernel<2, B200Q8_QUANT_CPU_X86>;
+        case B200Q8_QUANT_CPU_ARM:
+            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_ARM> : decode_step_kernel<2, B200Q8_QUANT_CPU_ARM>;
+        default:
+            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_REF> : decode_step_kernel<2, B200Q8_QUANT_REF>;
+    }
+}
+}  // namespace
+
+// True when one CTA of the step kernel fits on an SM with its shared memory
+// (the cooperative launch needs every CTA resident at once).
+bool decode_step_fits(const StepArgs & a) {
+    for (int mt = 1; mt <= 2; ++mt) {
+        int          slots = 0;
+        const size_t smem  = decode_step_smem_bytes(a, mt, slots);
+        StepFn       fn    = pick_step_kernel(a.mode, mt);
+        if (smem == 0 || cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        int blocks = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, kStepThreads, smem) != cudaSuccess || blocks < 1) {
+            cudaGetLastError();
+            return false;
+        }
+    }
+    return true;
 }
 
 cudaError_t launch_decode_step(StepArgs a, int G, cudaStream_t stream) {
@@ -702,12 +840,7 @@ cudaError_t launch_decode_step(StepArgs a, int G, cudaStream_t stream) {
     int       slots = 0;
     const size_t smem = decode_step_smem_bytes(a, mt, slots);
     a.n_slots         = slots;
-    void (*fn)(const StepArgs) = nullptr;
-    switch (a.mode) {
-        case B200Q8_QUANT_CPU_X86: fn = mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_X86> : decode_step_kernel<2, B200Q8_QUANT_CPU_X86>; break;
-        case B200Q8_QUANT_CPU_ARM: fn = mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_ARM> : decode_step_kernel<2, B200Q8_QUANT_CPU_ARM>; break;
-        default: fn = mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_REF> : decode_step_kernel<2, B200Q8_QUANT_REF>; break;
-    }
+    StepFn fn = pick_step_kernel(a.mode, mt);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     if (e != cudaSuccess) {
         return e;
@@ -722,7 +855,11 @@ cudaError_t launch_decode_step(StepArgs a, int G, cudaStream_t stream) {
     attr[0].val.cooperative = 1;
     cfg.attrs              = attr;
     cfg.numAttrs           = 1;
-    return cudaLaunchKernelEx(&cfg, fn, a);
+    e                      = cudaLaunchKernelEx(&cfg, fn, a);
+    if (e != cudaSuccess) {
+        cudaGetLastError();  // a failed launch must not surface in the caller's next check
+    }
+    return e;
 }
 
 }  // namespace b200q8

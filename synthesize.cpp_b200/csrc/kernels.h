@@ -79,6 +79,7 @@ struct StepArgs {
     const StepLayerDev * layers;  // device array [n_layers]
     int                  n_layers;
     int                  H, Q, KV, I, head_dim, group;
+    int                  lg_head_dim, lg_group;  // log2 of head_dim and group (both powers of two)
     float                eps;
     size_t               rb_h, rb_q, rb_i;
     const uint8_t *      table;
@@ -100,6 +101,7 @@ struct StepArgs {
 };
 
 bool        decode_step_supported(const StepArgs & a, int grid);
+bool        decode_step_fits(const StepArgs & a);
 size_t      decode_step_smem_bytes(const StepArgs & a, int mt, int & n_slots);
 cudaError_t launch_decode_step(StepArgs a, int grid, cudaStream_t stream);
 
