@@ -9,6 +9,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -200,8 +201,11 @@ size_t b200q8_mul_mat_workspace_size(int64_t K, int64_t N, int64_t M) {
     if (K <= 0 || M <= 0 || K % kQK != 0) {
         return 0;
     }
-    // quantized activations for the general path (M rows of K/32 blocks)
-    return align_up((size_t) M * (size_t) (K / kQK) * kBlockBytes, 256);
+    // the larger of: quantized activations for the general path (M rows of
+    // K/32 blocks) and the tensor-core path's code and scale planes
+    const size_t general = align_up((size_t) M * (size_t) (K / kQK) * kBlockBytes, 256);
+    const size_t planes  = align_up(gemm_workspace_bytes(K, M), 256);
+    return M > 8 ? std::max(general, planes) : general;
 }
 
 b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_row_bytes, const float * x, int64_t M,
@@ -243,6 +247,15 @@ b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_ro
     p.y          = y;
     p.y_stride   = ys;
     p.mode       = mode;
+    if (M > 8 && gemm_supported(p.w, w_row_bytes, K, N, M)) {
+        const size_t need = b200q8_mul_mat_workspace_size(K, N, M);
+        if (workspace == nullptr || workspace_bytes < need) {
+            return set_error(B200Q8_ERR_INVALID_ARG, "mul_mat: M > 8 needs %zu bytes of workspace (got %zu)", need,
+                             workspace_bytes);
+        }
+        cudaError_t e = launch_gemm(p.w, w_row_bytes, K, N, x, xs, M, y, ys, mode, workspace, st, sms);
+        return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "mul_mat: tensor-core GEMM launch");
+    }
     if (gemv_supported(p)) {
         for (int64_t m0 = 0; m0 < M; m0 += 8) {
             p.M           = (int) std::min<int64_t>(M - m0, 8);

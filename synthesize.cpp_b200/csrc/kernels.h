@@ -63,6 +63,14 @@ cudaError_t launch_gemv(const GemvParams & p, cudaStream_t stream, int sm_count,
 cudaError_t launch_gemv_generic(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const uint8_t * xq,
                                 int64_t M, float * y, size_t y_stride_bytes, cudaStream_t stream);
 
+// ---- int8 tensor-core GEMM for M > 8 (gemm.cu)
+
+size_t      gemm_workspace_bytes(int64_t K, int64_t M);
+bool        gemm_supported(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, int64_t M);
+cudaError_t launch_gemm(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const float * x, size_t x_stride,
+                        int64_t M, float * y, size_t y_stride, int mode, void * workspace, cudaStream_t stream,
+                        int sm_count);
+
 // ---- the persistent decode step (decode_step.cu)
 
 struct StepLayerDev {

@@ -2,6 +2,7 @@
 // status word and the kernels share one module without relocatable device code.
 #include "quantize.cu"
 #include "gemv.cu"
+#include "gemm.cu"
 #include "decode_step.cu"
 #include "abi.cu"
 #include "chain.cu"

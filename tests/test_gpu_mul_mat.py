@@ -88,6 +88,28 @@ def test_batched_with_outliers(q8, O, dev, m):
     check_close(y, y_ref, bound)
 
 
+@pytest.mark.parametrize("n,k", [(1024, 1024), (3072, 1024), (1024, 3072), (2048, 2048), (1000, 2048), (33, 256),
+                                 (6144, 2048)])
+@pytest.mark.parametrize("m", [16, 20, 64, 256])
+def test_tensor_core_gemm(q8, O, dev, n, k, m):
+    # M > 8 runs the int8 mma.sync GEMM (config 3 shapes, outliers, ragged N and M)
+    wq_np = O.quantize_rows(O.normal(n * 3 + k, n * k, 0.02).reshape(n, k))
+    x = activations(m, k, seed=m * 5 + k, outliers=True)
+    y = q8.mul_mat(to_dev(wq_np, dev), k, to_dev(x, dev)).cpu().numpy()
+    y_ref, bound = O.mul_mat(wq_np, k, x)
+    check_close(y, y_ref, bound)
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_tensor_core_gemm_modes(q8, O, dev, mode):
+    n, k, m = 3072, 1024, 24
+    wq_np = O.quantize_rows(O.normal(77, n * k, 0.02).reshape(n, k))
+    x = activations(m, k, seed=mode + 40)
+    y = q8.mul_mat(to_dev(wq_np, dev), k, to_dev(x, dev), mode=mode).cpu().numpy()
+    y_ref, bound = O.mul_mat(wq_np, k, x, mode=mode)
+    check_close(y, y_ref, bound)
+
+
 @pytest.mark.parametrize("n,k,m", [(2, 32, 3), (1, 96, 4), (33, 160, 5), (5, 352, 17)])
 def test_general_shapes(q8, O, dev, n, k, m):
     wq_np = O.quantize_rows(O.normal(n * k, n * k, 0.5).reshape(n, k))
