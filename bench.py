@@ -41,7 +41,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b"])
+    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b"],
+                    help="talker: BASELINE config 2 (config 3 with --batch 16/64/256); talker-1.7b: config 4 shapes; "
+                         "dp-sweep: config 5, 512 streams split over the ranks in M=64 batches; "
+                         "pack-1.7b: config 4 packing of all 1.4 B weights (synthesize-quantize)")
     ap.add_argument("--batch", type=int, default=1, help="tokens (streams) per step per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chain", default="auto", choices=["auto", "per-op"],
@@ -127,11 +130,11 @@ def physical_gpu_index(local_rank):
     return local_rank
 
 
-def cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s, max_tokens):
+def cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s, max_tokens, m=1):
     """Oracle decode chain (ggml-cpu's Q8_0 arithmetic restated in C, OpenMP over rows) on the host cores."""
     from synthesize_cpp_b200.workloads import stream_inputs
 
-    x, ids = stream_inputs(1, shape.hidden, shape.table_rows)
+    x, ids = stream_inputs(m, shape.hidden, shape.table_rows)
     kw = dict(hidden=shape.hidden, n_head=shape.n_head, n_kv=shape.n_kv, head_dim=shape.head_dim,
               inter=shape.inter, eps=shape.eps, threads=threads)
     O.decoder_chain(mats, norms, table, ids, x, **kw)  # warm-up
@@ -143,7 +146,7 @@ def cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s, max_
     for _ in range(n):
         O.decoder_chain(mats, norms, table, ids, x, **kw)
     dt = time.perf_counter() - t0
-    return n / dt, n, dt
+    return n * m / dt, n, dt
 
 
 def run_reference(args, rank):
@@ -177,7 +180,7 @@ def run_reference(args, rank):
     threads = O.lib().oracle_max_threads()
     from synthesize_cpp_b200.workloads import stream_inputs
 
-    m = args.batch
+    m = 64 if args.workload == "dp-sweep" else args.batch
     x, ids = stream_inputs(m, shape.hidden, shape.table_rows)
     kw = dict(hidden=shape.hidden, n_head=shape.n_head, n_kv=shape.n_kv, head_dim=shape.head_dim,
               inter=shape.inter, eps=shape.eps, threads=threads)
@@ -208,6 +211,89 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_pack(args, rank, local_rank):
+    """BASELINE config 4 packing: F32 -> Q8_0 of every 1.7B-shaped matrix (1,415,577,600 weights)."""
+    import numpy as np
+    import torch
+
+    import __graft_entry__ as g
+
+    g.load_package()
+    from synthesize_cpp_b200 import host, q8
+    from synthesize_cpp_b200.workloads import TALKER_17B
+
+    if rank != 0:
+        return
+    shape = TALKER_17B
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    mats = [(n, k) for _ in range(shape.n_layers) for (n, k) in shape.matrices()] + [(3072, shape.hidden)]
+    weights = sum(n * k for n, k in mats)
+    f32 = [np.empty(n * k, np.float32) for n, k in mats]
+    host.normal_many([2000 + i for i in range(len(mats))], [0.02] * len(mats), f32)
+    src_dev = [torch.from_numpy(a).to(dev) for a in f32]
+    dst_dev = [torch.empty((n, k // 32 * 34), dtype=torch.uint8, device=dev) for n, k in mats]
+
+    def step():
+        for a, d, (n, k) in zip(src_dev, dst_dev, mats):
+            q8.quantize_rows(a.view(n, k), out=d)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t_dev = e0.elapsed_time(e1) / 1e3 / args.steps
+    clocks = sampler.stop()
+    # e2e: the quantize tool's own call, host F32 in, host Q8_0 out
+    dst_host = [np.empty(n * (k // 32 * 34), np.uint8) for n, k in mats]
+    t0 = time.perf_counter()
+    for a, d, (n, k) in zip(f32, dst_host, mats):
+        q8.quantize_chunk_host(a, d, 0, n, k, device=local_rank)
+    t_e2e = time.perf_counter() - t0
+    # spot parity on the largest tensor, and the CPU reference tool's rate (one thread, as ggml_quantize_chunk)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    n0, k0 = mats[4]
+    ref, _ = O.quantize_chunk(f32[4], 0, n0, k0)
+    assert np.array_equal(ref, dst_host[4]) and np.array_equal(ref, dst_dev[4].cpu().numpy().ravel())
+    cpu_w = 0
+    c0 = time.perf_counter()
+    for a, (n, k) in zip(f32[:14], mats[:14]):
+        O.quantize_chunk(a, 0, n, k)
+        cpu_w += n * k
+    cpu_t = time.perf_counter() - c0
+    peaks, peak_kind = measured_peaks()
+    bytes_step = weights * (4 + 34 / 32)
+    line = {
+        "metric": "Q8_0 packing throughput (synthesize-quantize, BASELINE config 4)", "value": weights / t_dev / 1e9,
+        "unit": "Gweight/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": 1e3 * t_dev, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 -> q8_0", "data": "synthetic (seeded 0.02*N(0,1) stream of src/random-stream.cpp)",
+        "config": {"workload": f"pack all {len(mats)} 1.7B-shaped matrices + 3072x2048 head, {weights} weights",
+                   "l2": "inputs larger than L2 (5.66 GB of F32 per step)"},
+        "roofline": {"bound": "hbm", "achieved": bytes_step / t_dev / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": bytes_step / t_dev / 1e9 / peaks["hbm_gbs"], "traffic": None,
+                     "kernel": "quantize_dense_kernel", "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+        "e2e": {"value": weights / t_e2e / 1e9, "unit": "Gweight/s", "h2d_bytes_per_step": weights * 4,
+                "d2h_bytes_per_step": weights * 34 // 32},
+        "gpu_launches": len(mats) * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": {"value": cpu_w / cpu_t / 1e9, "unit": "Gweight/s", "cores": 1, "kind": "port",
+                         "sample": f"{cpu_w} weights (first 2 layers) through the oracle's quantize_row_q8_0_ref, "
+                                   "one thread like ggml_quantize_chunk"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -215,6 +301,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "pack-1.7b":
+        run_pack(args, rank, local_rank)
         return
 
     import torch
@@ -229,41 +318,57 @@ def main():
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
+    from synthesize_cpp_b200 import dp as dpu
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    if world > 1:
+        dpu.init("nccl", timeout_s=300.0, device=dev)
 
     def barrier_sync():
         torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
+        dpu.barrier(dev)
         torch.cuda.synchronize(dev)
 
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return dpu.max_over_ranks(v, dev)
 
     shape = TALKER_17B if args.workload == "talker-1.7b" else TALKER_06B
-    m = args.batch
+    dp = args.workload == "dp-sweep"
+    if dp:
+        # 512 independent streams split evenly over the ranks, run as M=64 batches
+        first, sizes = dpu.partition_streams(512, world, rank, 64)
+    else:
+        first = rank * args.batch
+        sizes = [args.batch]
+    m_max = max(sizes)
     dm = build_model(shape, dev)
     os.environ["B200Q8_CHAIN_PER_OP"] = "1" if args.chain == "per-op" else "0"
     ch = chain_mod.DecodeChain(dm.layers, dm.table, hidden=shape.hidden, n_head=shape.n_head, n_kv=shape.n_kv,
-                               head_dim=shape.head_dim, inter=shape.inter, eps=shape.eps, max_m=max(8, m))
-    x_np, ids_np = stream_inputs(m, shape.hidden, shape.table_rows, first_stream=rank * m)
-    x_host = torch.from_numpy(x_np).pin_memory()
-    ids_host = torch.from_numpy(ids_np).pin_memory()
-    h_host = torch.empty((m, shape.hidden), dtype=torch.float32).pin_memory()
-    x_dev = x_host.to(dev)
-    ids_dev = ids_host.to(dev)
-    h_dev = torch.empty((m, shape.hidden), dtype=torch.float32, device=dev)
+                               head_dim=shape.head_dim, inter=shape.inter, eps=shape.eps, max_m=max(8, m_max))
+    batches = []
+    off = first
+    for m in sizes:
+        x_np, ids_np = stream_inputs(m, shape.hidden, shape.table_rows, first_stream=off)
+        off += m
+        x_host = torch.from_numpy(x_np).pin_memory()
+        ids_host = torch.from_numpy(ids_np).pin_memory()
+        h_host = torch.empty((m, shape.hidden), dtype=torch.float32).pin_memory()
+        batches.append((x_host, ids_host, h_host, x_host.to(dev), ids_host.to(dev),
+                        torch.empty((m, shape.hidden), dtype=torch.float32, device=dev)))
     stream = torch.cuda.current_stream(dev)
 
+    def step():
+        for (_, _, _, x_dev, ids_dev, h_dev) in batches:
+            ch.run(ids_dev, x_dev, h_dev)
+
+    def step_e2e():
+        for (x_host, ids_host, h_host, x_dev, ids_dev, h_dev) in batches:
+            x_dev.copy_(x_host, non_blocking=True)
+            ids_dev.copy_(ids_host, non_blocking=True)
+            ch.run(ids_dev, x_dev, h_dev)
+            h_host.copy_(h_dev, non_blocking=True)
+
     for _ in range(args.warmup):
-        ch.run(ids_dev, x_dev, h_dev)
+        step()
     barrier_sync()
     if q8.device_status(local_rank) != 0:
         raise RuntimeError("device status set during warm-up")
@@ -276,7 +381,7 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        ch.run(ids_dev, x_dev, h_dev)
+        step()
     e1.record(stream)
     barrier_sync()
     t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
@@ -287,42 +392,53 @@ def main():
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for _ in range(args.steps):
-        x_dev.copy_(x_host, non_blocking=True)
-        ids_dev.copy_(ids_host, non_blocking=True)
-        ch.run(ids_dev, x_dev, h_dev)
-        h_host.copy_(h_dev, non_blocking=True)
+        step_e2e()
     f1.record(stream)
     barrier_sync()
     t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
     if q8.device_status(local_rank) != 0:
         raise RuntimeError("device status set during the timed region")
 
-    tokens = world * m * args.steps
+    tokens = (512 if dp else world * args.batch) * args.steps
     value = tokens / t_dev
     step_s = t_dev / args.steps
     peaks, peak_kind = measured_peaks()
-    step_bytes = shape.step_bytes(m)
+    step_bytes = sum(shape.step_bytes(m) for m in sizes)
+    step_flops = sum(shape.step_flops(m) for m in sizes)
     achieved = step_bytes / step_s / 1e9
-    persistent = args.chain == "auto" and m <= 2
-    launches_per_step = 1 if persistent else 1 + 4 * shape.n_layers * ((m + 7) // 8)
-    kernel_name = ("decode_step_kernel (the whole step in one persistent launch)" if persistent
-                   else "gemv_q8_0_kernel (every launch of the step; 1 + 4*layers launches)")
+    persistent = args.chain == "auto" and m_max <= 2
+    per_batch = lambda m: 1 if persistent else (2 + 8 * shape.n_layers if m > 8 else 1 + 4 * shape.n_layers)
+    launches_per_step = sum(per_batch(m) for m in sizes)
+    if persistent:
+        kernel_name = "decode_step_kernel (the whole step in one persistent launch)"
+    elif m_max > 8:
+        kernel_name = "gemm_q8_0_kernel + stage_rows_kernel (int8 mma.sync GEMM per op, CUDA graph + PDL)"
+    else:
+        kernel_name = "gemv_q8_0_kernel (every launch of the step; 1 + 4*layers launches)"
+    h2d = sum(m * shape.hidden * 4 + m * 4 for m in sizes)
+    d2h = sum(m * shape.hidden * 4 for m in sizes)
+    if dp:
+        workload = (f"{shape.name} decode, BASELINE config 5: 512 streams over {world} GPU(s), "
+                    f"batches {sizes} per GPU per step")
+    else:
+        workload = f"{shape.name} decode step (BASELINE config {'2' if args.batch == 1 else '3'}), M={args.batch} per GPU"
     line = {
         "metric": "talker-shaped Q8_0 decode throughput", "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * step_s, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32, f32 scale (Q8_0 x F32)",
+        "scaling": "strong" if dp else "weak", "vs_baseline": None, "dtype": "int8xint8->int32, f32 scale (Q8_0 x F32)",
         "data": "synthetic (seeded N(0,1) stream of src/random-stream.cpp; weights 0.02*N, packed on device)",
-        "config": {"workload": f"{shape.name} decode step (BASELINE config 2), M={m} per GPU",
-                   "layers": shape.n_layers, "batch_per_gpu": m, "global_batch": world * m,
+        "config": {"workload": workload, "layers": shape.n_layers, "batch_per_gpu": sum(sizes),
+                   "global_batch": 512 if dp else world * args.batch,
                    "parallelism": f"replicas x{world} (no collectives)",
-                   "l2": "inputs larger than L2: 468 MB of weights streamed per step",
-                   "weight_bytes_per_step": shape.weight_bytes(), "algorithmic_bytes_per_step": step_bytes},
+                   "l2": "inputs larger than L2: weights streamed every step exceed 126 MB",
+                   "weight_bytes_per_step": shape.weight_bytes() * len(sizes), "algorithmic_bytes_per_step": step_bytes,
+                   "int8_ops_per_step": step_flops},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic(f"{shape.name}-m{m}"),
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic(f"{shape.name}-m{m_max}"),
                      "kernel": kernel_name,
-                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
-        "e2e": {"value": tokens / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": m * shape.hidden * 4 + m * 4,
-                "d2h_bytes_per_step": m * shape.hidden * 4},
+                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                     "int8_tops": step_flops / step_s / 1e12},
+        "e2e": {"value": tokens / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
@@ -332,9 +448,11 @@ def main():
 
         mats, norms, table = host_copy(dm)
         threads = O.lib().oracle_max_threads()
-        tps, n, dt = cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s=12.0, max_tokens=400)
+        mcpu = min(m_max, 64)
+        tps, n, dt = cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s=12.0, max_tokens=400,
+                                            m=mcpu)
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
-                                "sample": f"{n} tokens of the full {shape.n_layers}-layer step at M=1 "
+                                "sample": f"{n} steps of the full {shape.n_layers}-layer step at M={mcpu} "
                                           f"({dt:.1f} s; oracle C port of ggml-cpu Q8_0, OpenMP)"}
     ch.close()
     if rank == 0:

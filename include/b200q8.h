@@ -100,6 +100,16 @@ b200q8_status_t b200q8_quantize_rows(const float * x, int64_t rows, int64_t K, s
 b200q8_status_t b200q8_quantize_chunk(const float * src, void * dst, int64_t start, int64_t nrows,
                                       int64_t n_per_row, size_t * written, b200q8_stream_t stream);
 
+/* ggml_quantize_chunk(GGML_TYPE_Q8_0, src, dst, start, nrows, n_per_row, NULL)
+ * on HOST buffers -- the call tools/synthesize-quantize/quantize.cpp:300-301
+ * makes, with its arguments' meaning.  Rows stream through `device` in
+ * chunks; bytes identical to quantize_row_q8_0_ref.  Blocking.  Unlike the
+ * compute entry points it allocates (device staging, freed before it
+ * returns) and page-locks the caller's buffers for the duration when the
+ * driver allows: a tool call, not a hot-path one. */
+b200q8_status_t b200q8_quantize_chunk_host(const float * src, void * dst, int64_t start, int64_t nrows,
+                                           int64_t n_per_row, size_t * written, int32_t device);
+
 /* Q8_0 rows -> F32 rows: out = q * fp32(d) (exact). */
 b200q8_status_t b200q8_dequantize_rows(const void * src, int64_t rows, int64_t K, size_t src_row_stride, float * dst,
                                        size_t dst_row_stride, b200q8_stream_t stream);

@@ -49,9 +49,9 @@ class ChainDesc(ctypes.Structure):
                 ("layers", ctypes.POINTER(Layer)), ("table", ctypes.c_void_p), ("table_rows", ctypes.c_int64)]
 
 
-def header_symbols() -> list[str]:
-    """Every function the public header declares."""
-    text = open(HEADER).read()
+def header_symbols(header: str = HEADER) -> list[str]:
+    """Every function a public header declares."""
+    text = open(header).read()
     return sorted(set(re.findall(r"^\S[^\n;]*?\b(b200q8_\w+)\s*\(", text, flags=re.M)))
 
 
@@ -72,6 +72,8 @@ def lib() -> ctypes.CDLL:
     L.b200q8_quantize_rows.restype = i32
     L.b200q8_quantize_chunk.argtypes = [vp, vp, i64, i64, i64, ctypes.POINTER(sz), vp]
     L.b200q8_quantize_chunk.restype = i32
+    L.b200q8_quantize_chunk_host.argtypes = [vp, vp, i64, i64, i64, ctypes.POINTER(sz), i32]
+    L.b200q8_quantize_chunk_host.restype = i32
     L.b200q8_dequantize_rows.argtypes = [vp, i64, i64, sz, vp, sz, vp]
     L.b200q8_dequantize_rows.restype = i32
     L.b200q8_get_rows.argtypes = [vp, i64, i64, sz, vp, i64, vp, sz, vp]

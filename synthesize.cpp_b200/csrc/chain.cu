@@ -87,6 +87,7 @@ struct b200q8_chain {
     unsigned *                   sync         = nullptr;
     bool                         persistent   = false;
     void *                       timeline     = nullptr;  // B200Q8_TIMELINE analysis builds only
+    void *                       planes       = nullptr;  // batched path (M > 8): GEMM code/scale planes
 
     struct Graph {
         int64_t         M;
@@ -147,6 +148,62 @@ const uint8_t * contiguous(b200q8_chain * c, const void * a, size_t a_bytes, con
     return o;
 }
 
+// M > 8: per op, a per-token prologue kernel (norm / GQA / SwiGLU + residual,
+// quantized into code and scale planes) then the int8 tensor-core GEMM;
+// 2 launches per op with programmatic dependent launch between them.
+cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, int64_t M, float * h_out) {
+    const b200q8_chain_desc & d = c->d;
+    const int64_t H = d.hidden, Q = d.n_head * d.head_dim, KV = d.n_kv * d.head_dim, I = d.inter;
+    const int     hd = (int) d.head_dim, grp = (int) (d.n_head / d.n_kv);
+    const int64_t Kmax = std::max(std::max(H, Q), I);
+    int8_t *      codes;
+    float *       scales;
+    gemm_planes(c->planes, Kmax, M, &codes, &scales);
+    cudaError_t e = cudaSuccess;
+    for (int l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
+        auto B = [&](int layer, int which) { return c->buf(layer, which); };
+        const float * h_in   = l == 0 ? c->h0 : B(l - 1, kHout);
+        // qkv: n1 = rms_norm(h) * norm_in with h = h1(l-1) + d(l-1)
+        if (l == 0) {
+            e = launch_stage_rows(0, c->h0, nullptr, (size_t) H, nullptr, 0, c->layers[l].norm_in, d.eps, (int) H, hd,
+                                  grp, B(l, kN1), (size_t) H, M, d.mode, codes, scales, st, true);
+        } else {
+            e = launch_stage_rows(0, B(l - 1, kH1), B(l - 1, kDown), (size_t) H, B(l - 1, kHout), (size_t) H,
+                                  c->layers[l].norm_in, d.eps, (int) H, hd, grp, B(l, kN1), (size_t) H, M, d.mode, codes,
+                                  scales, st, true);
+        }
+        if (e == cudaSuccess)
+            e = launch_gemm_planes(c->w_qkv[l], c->rb_h, H, c->qkv_dim, codes, scales, M, B(l, kQkv),
+                                   (size_t) c->qkv_dim, st, c->sms, true);
+        // o: attend(v)
+        if (e == cudaSuccess)
+            e = launch_stage_rows(1, B(l, kQkv) + Q + KV, nullptr, (size_t) c->qkv_dim, nullptr, 0, nullptr, d.eps,
+                                  (int) Q, hd, grp, B(l, kAttn), (size_t) Q, M, d.mode, codes, scales, st, true);
+        if (e == cudaSuccess)
+            e = launch_gemm_planes(c->w_o[l], c->rb_q, Q, H, codes, scales, M, B(l, kO), (size_t) H, st, c->sms, true);
+        // gate|up: n2 = rms_norm(h1) * norm_post with h1 = h + o
+        if (e == cudaSuccess)
+            e = launch_stage_rows(0, h_in, B(l, kO), (size_t) H, B(l, kH1), (size_t) H, c->layers[l].norm_post, d.eps,
+                                  (int) H, hd, grp, B(l, kN2), (size_t) H, M, d.mode, codes, scales, st, true);
+        if (e == cudaSuccess)
+            e = launch_gemm_planes(c->w_gu[l], c->rb_h, H, 2 * I, codes, scales, M, B(l, kGu), (size_t) (2 * I), st,
+                                   c->sms, true);
+        // down: silu(g) * u
+        if (e == cudaSuccess)
+            e = launch_stage_rows(2, B(l, kGu), B(l, kGu) + I, (size_t) (2 * I), nullptr, 0, nullptr, d.eps, (int) I, hd,
+                                  grp, B(l, kS), (size_t) I, M, d.mode, codes, scales, st, true);
+        if (e == cudaSuccess)
+            e = launch_gemm_planes(c->w_d[l], c->rb_i, I, H, codes, scales, M, B(l, kDown), (size_t) H, st, c->sms,
+                                   true);
+    }
+    if (e == cudaSuccess) {
+        const int L = d.n_layers - 1;
+        e           = launch_residual_rows(c->buf(L, kH1), c->buf(L, kDown), (size_t) H, h_out, (size_t) H, (int) H, M,
+                                           st, true);
+    }
+    return e;
+}
+
 cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, int64_t M, const int32_t * ids, const float * x_in,
                          float * h_out) {
     const b200q8_chain_desc & d = c->d;
@@ -160,6 +217,9 @@ cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, int64_t M, const int
         if (e != cudaSuccess) {
             return e;
         }
+    }
+    if (M > 8 && c->planes != nullptr) {
+        return enqueue_step_batched(c, st, M, h_out);
     }
     for (int64_t m0 = 0; m0 < M; m0 += 8) {
         const int   mc = (int) std::min<int64_t>(M - m0, 8);
@@ -284,6 +344,21 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
     }
     if (e == cudaSuccess) {
         e = cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking);
+    }
+    bool batched_ok = d.max_m > 8;
+    for (int l = 0; l < d.n_layers && batched_ok; ++l) {
+        batched_ok = gemm_supported(c->w_qkv[l], c->rb_h, H, c->qkv_dim, d.max_m) &&
+                     gemm_supported(c->w_o[l], c->rb_q, Q, H, d.max_m) &&
+                     gemm_supported(c->w_gu[l], c->rb_h, H, 2 * I, d.max_m) &&
+                     gemm_supported(c->w_d[l], c->rb_i, I, H, d.max_m);
+    }
+    if (e == cudaSuccess && batched_ok && std::max(std::max(H, Q), I) <= 8192) {
+        void * p = nullptr;
+        e        = cudaMalloc(&p, gemm_workspace_bytes(std::max(std::max(H, Q), I), d.max_m));
+        if (e == cudaSuccess) {
+            c->owned.push_back(p);
+            c->planes = p;
+        }
     }
     // persistent step: per-layer weight table, LL hand-off words, sync words
     const char * per_op = getenv("B200Q8_CHAIN_PER_OP");

@@ -108,8 +108,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_launch_dependents();
 
     if (warp == kGemmConsumerWarps) {
+        // weights are constant: they may stream in before the previous kernel ends
         if (lane == 0) {
             const uint64_t pol    = l2_evict_first_policy();
             int            issued = 0;
@@ -149,6 +151,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
     const int tq    = lane & 3;
     const uint32_t ring_s = smem_addr(ring);
 
+    pdl_wait_primary();  // activations come from the previous kernel
     // Every consumer warp runs the same loop trip counts and reaches the same
     // named barriers whatever happens: a timed-out wait or a token group past
     // M only skips work, it never leaves the loop early.
@@ -178,30 +181,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
             const float * sc0    = a.scales + (size_t) min(tok0, a.M - 1) * NB;
             const float * sc1    = a.scales + (size_t) min(tok0 + 1, a.M - 1) * NB;
             float         acc[4] = { 0.f, 0.f, 0.f, 0.f };
-            for (int b = b0; work && b < b1; ++b) {
-                const int off = b * kBlockBytes + 2;
-                uint32_t  A[4];
-                A[0] = lds_u32_at(row_a, off + 4 * tq);
-                A[1] = lds_u32_at(row_b, off + 4 * tq);
-                A[2] = lds_u32_at(row_a, off + 16 + 4 * tq);
-                A[3] = lds_u32_at(row_b, off + 16 + 4 * tq);
-                uint32_t B[2];
-                B[0] = __ldg(reinterpret_cast<const uint32_t *>(xrow + b * kQK + 4 * tq));
-                B[1] = __ldg(reinterpret_cast<const uint32_t *>(xrow + b * kQK + 16 + 4 * tq));
-                int D[4] = { 0, 0, 0, 0 };
-                mma_s8(D, A, B);
-                const uint32_t wa = lds_u32(row_a + (uint32_t) ((b * kBlockBytes) & ~3));
-                const uint32_t wb = lds_u32(row_b + (uint32_t) ((b * kBlockBytes) & ~3));
-                const float    da = __half2float(__ushort_as_half(
-                    (unsigned short) (((b * kBlockBytes) & 3) ? (wa >> 16) : (wa & 0xffffu))));
-                const float db = __half2float(__ushort_as_half(
-                    (unsigned short) (((b * kBlockBytes) & 3) ? (wb >> 16) : (wb & 0xffffu))));
-                const float x0 = __ldg(sc0 + b);
-                const float x1 = __ldg(sc1 + b);
-                acc[0] = __fmaf_rn((float) D[0], __fmul_rn(da, x0), acc[0]);
-                acc[1] = __fmaf_rn((float) D[1], __fmul_rn(da, x1), acc[1]);
-                acc[2] = __fmaf_rn((float) D[2], __fmul_rn(db, x0), acc[2]);
-                acc[3] = __fmaf_rn((float) D[3], __fmul_rn(db, x1), acc[3]);
+            // Eight blocks per step: all of their activation fragments and
+            // scales are requested from L2 before the first MMA, so the loads
+            // overlap instead of costing one L2 round trip per block.
+            for (int bb = b0; work && bb < b1; bb += 8) {
+                const int nb8 = min(8, b1 - bb);
+                uint32_t  Bf[8][2];
+                float     x0s[8], x1s[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int b = bb + (j < nb8 ? j : 0);
+                    Bf[j][0]    = __ldg(reinterpret_cast<const uint32_t *>(xrow + b * kQK + 4 * tq));
+                    Bf[j][1]    = __ldg(reinterpret_cast<const uint32_t *>(xrow + b * kQK + 16 + 4 * tq));
+                    x0s[j]      = __ldg(sc0 + b);
+                    x1s[j]      = __ldg(sc1 + b);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (j < nb8) {
+                        const int b   = bb + j;
+                        const int off = b * kBlockBytes + 2;
+                        uint32_t  A[4];
+                        A[0] = lds_u32_at(row_a, off + 4 * tq);
+                        A[1] = lds_u32_at(row_b, off + 4 * tq);
+                        A[2] = lds_u32_at(row_a, off + 16 + 4 * tq);
+                        A[3] = lds_u32_at(row_b, off + 16 + 4 * tq);
+                        int            D[4] = { 0, 0, 0, 0 };
+                        const uint32_t Bj[2] = { Bf[j][0], Bf[j][1] };
+                        mma_s8(D, A, Bj);
+                        const uint32_t wa = lds_u32(row_a + (uint32_t) ((b * kBlockBytes) & ~3));
+                        const uint32_t wb = lds_u32(row_b + (uint32_t) ((b * kBlockBytes) & ~3));
+                        const float    da = __half2float(__ushort_as_half(
+                            (unsigned short) (((b * kBlockBytes) & 3) ? (wa >> 16) : (wa & 0xffffu))));
+                        const float db = __half2float(__ushort_as_half(
+                            (unsigned short) (((b * kBlockBytes) & 3) ? (wb >> 16) : (wb & 0xffffu))));
+                        acc[0] = __fmaf_rn((float) D[0], __fmul_rn(da, x0s[j]), acc[0]);
+                        acc[1] = __fmaf_rn((float) D[1], __fmul_rn(da, x1s[j]), acc[1]);
+                        acc[2] = __fmaf_rn((float) D[2], __fmul_rn(db, x0s[j]), acc[2]);
+                        acc[3] = __fmaf_rn((float) D[3], __fmul_rn(db, x1s[j]), acc[3]);
+                    }
+                }
             }
             // combine the K slices in a fixed order: slice 0 adds 1..ksplit-1
             if (a.ksplit > 1) {
@@ -244,7 +263,142 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
     }
 }
 
+// Per-token prologue of the batched step: one CTA per token builds that
+// token's fp32 input of the next MUL_MAT and quantizes it into the code and
+// scale planes the GEMM reads.  kind: 0 = RMS norm of (a [+ b]) (the sum is
+// also written to sum_out when given), 1 = GQA expansion of a, 2 = silu(a)*b.
+template <int MODE>
+__global__ void __launch_bounds__(256) stage_rows_kernel(int kind, const float * __restrict__ a, const float * __restrict__ b,
+                                                         size_t ab_stride, float * __restrict__ sum_out,
+                                                         size_t sum_stride, const float * __restrict__ norm, float eps,
+                                                         int K, int head_dim, int group, float * __restrict__ trace,
+                                                         size_t trace_stride, int8_t * __restrict__ codes,
+                                                         float * __restrict__ scales) {
+    __shared__ float  xs[8192];
+    __shared__ double part[8];
+    __shared__ float  scale_s;
+    pdl_launch_dependents();
+    pdl_wait_primary();
+    const int     m    = blockIdx.x;
+    const int     t    = threadIdx.x;
+    const float * am   = a + (size_t) m * ab_stride;
+    const float * bm   = b ? b + (size_t) m * ab_stride : nullptr;
+    double        ss   = 0.0;
+    for (int i = t; i < K; i += 256) {
+        float v;
+        if (kind == 0) {
+            v = bm ? __fadd_rn(am[i], bm[i]) : am[i];
+            if (sum_out) {
+                sum_out[(size_t) m * sum_stride + i] = v;
+            }
+            ss += (double) __fmul_rn(v, v);
+        } else if (kind == 1) {
+            const int head = i / head_dim;
+            v              = am[(head / group) * head_dim + i % head_dim];
+        } else {
+            v = __fmul_rn(silu_f32(am[i]), bm[i]);
+        }
+        xs[i] = v;
+    }
+    if (kind == 0) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        }
+        if ((t & 31) == 0) {
+            part[t >> 5] = ss;
+        }
+        __syncthreads();
+        if (t == 0) {
+            double tot = 0.0;
+            for (int w = 0; w < 8; ++w) {
+                tot += part[w];
+            }
+            const float mean = (float) (tot / (double) K);
+            scale_s          = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, eps)));
+        }
+        __syncthreads();
+        const float sc = scale_s;
+        for (int i = t; i < K; i += 256) {
+            xs[i] = __fmul_rn(__fmul_rn(xs[i], sc), norm[i]);
+        }
+    }
+    __syncthreads();
+    const int warp = t >> 5;
+    const int lane = t & 31;
+    const int NB   = K >> 5;
+    for (int blk = warp; blk < NB; blk += 8) {
+        const float       v     = xs[blk * kQK + lane];
+        float             vv[1] = { v };
+        const float       amx   = block_amax<32, 1>(vv, lane);
+        const QuantParams qp    = quant_params<MODE>(amx);
+        codes[((size_t) m * NB + blk) * kQK + lane] = (int8_t) quant_code<MODE>(v, qp.id);
+        if (lane == 0) {
+            scales[(size_t) m * NB + blk] = qp.d;
+        }
+        if (trace) {
+            trace[(size_t) m * trace_stride + blk * kQK + lane] = v;
+        }
+    }
+}
+
+__global__ void residual_rows_kernel(const float * __restrict__ a, const float * __restrict__ b, size_t ab_stride,
+                                     float * __restrict__ out, size_t out_stride, int K) {
+    pdl_launch_dependents();
+    pdl_wait_primary();
+    const int m = blockIdx.x;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        out[(size_t) m * out_stride + i] = __fadd_rn(a[(size_t) m * ab_stride + i], b[(size_t) m * ab_stride + i]);
+    }
+}
+
+template <typename F, typename... Args>
+cudaError_t launch_pdl(F fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = grid;
+    cfg.blockDim           = block;
+    cfg.dynamicSmemBytes   = smem;
+    cfg.stream             = stream;
+    cudaLaunchAttribute attr[1];
+    if (pdl) {
+        attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs                                          = attr;
+        cfg.numAttrs                                       = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, fn, args...);
+}
+
 }  // namespace
+
+cudaError_t launch_stage_rows(int kind, const float * a, const float * b, size_t ab_stride, float * sum_out,
+                              size_t sum_stride, const float * norm, float eps, int K, int head_dim, int group,
+                              float * trace, size_t trace_stride, int64_t M, int mode, int8_t * codes, float * scales,
+                              cudaStream_t stream, bool pdl) {
+    if (K > 8192 || K % kQK) {
+        return cudaErrorInvalidValue;
+    }
+    switch (mode) {
+        case B200Q8_QUANT_CPU_X86:
+            return launch_pdl(stage_rows_kernel<B200Q8_QUANT_CPU_X86>, dim3((unsigned) M), dim3(256), 0, stream, pdl,
+                              kind, a, b, ab_stride, sum_out, sum_stride, norm, eps, K, head_dim, group, trace,
+                              trace_stride, codes, scales);
+        case B200Q8_QUANT_CPU_ARM:
+            return launch_pdl(stage_rows_kernel<B200Q8_QUANT_CPU_ARM>, dim3((unsigned) M), dim3(256), 0, stream, pdl,
+                              kind, a, b, ab_stride, sum_out, sum_stride, norm, eps, K, head_dim, group, trace,
+                              trace_stride, codes, scales);
+        default:
+            return launch_pdl(stage_rows_kernel<B200Q8_QUANT_REF>, dim3((unsigned) M), dim3(256), 0, stream, pdl, kind,
+                              a, b, ab_stride, sum_out, sum_stride, norm, eps, K, head_dim, group, trace, trace_stride,
+                              codes, scales);
+    }
+}
+
+cudaError_t launch_residual_rows(const float * a, const float * b, size_t ab_stride, float * out, size_t out_stride,
+                                 int K, int64_t M, cudaStream_t stream, bool pdl) {
+    return launch_pdl(residual_rows_kernel, dim3((unsigned) M), dim3(256), 0, stream, pdl, a, b, ab_stride, out,
+                      out_stride, K);
+}
 
 size_t gemm_workspace_bytes(int64_t K, int64_t M) {
     const size_t codes = (size_t) M * (size_t) K;
@@ -261,35 +415,9 @@ bool gemm_supported(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, i
     return fixed + slot <= (size_t) kGemmSmemLimit;
 }
 
-cudaError_t launch_gemm(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const float * x, size_t x_stride,
-                        int64_t M, float * y, size_t y_stride, int mode, void * workspace, cudaStream_t stream,
-                        int sm_count) {
-    const int64_t NB     = K / kQK;
-    int8_t *      codes  = static_cast<int8_t *>(workspace);
-    float *       scales = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) +
-                                              (((size_t) M * (size_t) K + 255) & ~(size_t) 255));
-    {
-        const int64_t warps = M * NB;
-        int64_t       ctas  = std::min<int64_t>((warps + 7) / 8, (int64_t) sm_count * 8);
-        ctas                = std::max<int64_t>(ctas, 1);
-        switch (mode) {
-            case B200Q8_QUANT_CPU_X86:
-                quantize_planes_kernel<B200Q8_QUANT_CPU_X86><<<(unsigned) ctas, 256, 0, stream>>>(x, x_stride, M, NB,
-                                                                                                  codes, scales);
-                break;
-            case B200Q8_QUANT_CPU_ARM:
-                quantize_planes_kernel<B200Q8_QUANT_CPU_ARM><<<(unsigned) ctas, 256, 0, stream>>>(x, x_stride, M, NB,
-                                                                                                  codes, scales);
-                break;
-            default:
-                quantize_planes_kernel<B200Q8_QUANT_REF><<<(unsigned) ctas, 256, 0, stream>>>(x, x_stride, M, NB, codes,
-                                                                                              scales);
-        }
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) {
-            return e;
-        }
-    }
+cudaError_t launch_gemm_planes(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const int8_t * codes,
+                               const float * scales, int64_t M, float * y, size_t y_stride, cudaStream_t stream,
+                               int sm_count, bool pdl) {
     GemmArgs a   = {};
     a.w          = w;
     a.row_bytes  = row_bytes;
@@ -317,15 +445,52 @@ cudaError_t launch_gemm(const uint8_t * w, size_t row_bytes, int64_t K, int64_t 
     if (a.n_slots < 1) {
         return cudaErrorInvalidValue;
     }
-    const size_t smem  = fixed + (size_t) a.n_slots * a.slot_bytes;
+    const size_t  smem = fixed + (size_t) a.n_slots * a.slot_bytes;
     const int64_t n_rt = (N + 15) / 16;
     const int     grid = (int) std::min<int64_t>(n_rt, sm_count);
     cudaError_t   e    = cudaFuncSetAttribute(gemm_q8_0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     if (e != cudaSuccess) {
         return e;
     }
-    gemm_q8_0_kernel<<<grid, kGemmThreads, smem, stream>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(gemm_q8_0_kernel, dim3((unsigned) grid), dim3(kGemmThreads), smem, stream, pdl, a);
+}
+
+void gemm_planes(void * workspace, int64_t K, int64_t M, int8_t ** codes, float ** scales) {
+    *codes  = static_cast<int8_t *>(workspace);
+    *scales = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) +
+                                        (((size_t) M * (size_t) K + 255) & ~(size_t) 255));
+}
+
+cudaError_t launch_gemm(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const float * x, size_t x_stride,
+                        int64_t M, float * y, size_t y_stride, int mode, void * workspace, cudaStream_t stream,
+                        int sm_count) {
+    const int64_t NB = K / kQK;
+    int8_t *      codes;
+    float *       scales;
+    gemm_planes(workspace, K, M, &codes, &scales);
+    {
+        const int64_t warps = M * NB;
+        int64_t       ctas  = std::min<int64_t>((warps + 7) / 8, (int64_t) sm_count * 8);
+        ctas                = std::max<int64_t>(ctas, 1);
+        switch (mode) {
+            case B200Q8_QUANT_CPU_X86:
+                quantize_planes_kernel<B200Q8_QUANT_CPU_X86><<<(unsigned) ctas, 256, 0, stream>>>(x, x_stride, M, NB,
+                                                                                                  codes, scales);
+                break;
+            case B200Q8_QUANT_CPU_ARM:
+                quantize_planes_kernel<B200Q8_QUANT_CPU_ARM><<<(unsigned) ctas, 256, 0, stream>>>(x, x_stride, M, NB,
+                                                                                                  codes, scales);
+                break;
+            default:
+                quantize_planes_kernel<B200Q8_QUANT_REF><<<(unsigned) ctas, 256, 0, stream>>>(x, x_stride, M, NB, codes,
+                                                                                              scales);
+        }
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            return e;
+        }
+    }
+    return launch_gemm_planes(w, row_bytes, K, N, codes, scales, M, y, y_stride, stream, sm_count, false);
 }
 
 }  // namespace b200q8

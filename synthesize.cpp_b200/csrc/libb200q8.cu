@@ -6,4 +6,5 @@
 #include "decode_step.cu"
 #include "abi.cu"
 #include "chain.cu"
+#include "pack_host.cu"
 #include "noalloc.cu"

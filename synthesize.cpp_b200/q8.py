@@ -30,7 +30,7 @@ QK = 32
 BLOCK_BYTES = 34
 
 __all__ = ["QK", "BLOCK_BYTES", "QUANT_REF", "QUANT_CPU_X86", "QUANT_CPU_ARM", "B200Q8Error", "row_bytes",
-           "quantize_rows", "quantize_chunk", "dequantize_rows", "get_rows", "mul_mat", "workspace_size",
+           "quantize_rows", "quantize_chunk", "quantize_chunk_host", "dequantize_rows", "get_rows", "mul_mat", "workspace_size",
            "device_status", "stream_ptr"]
 
 
@@ -73,6 +73,18 @@ def quantize_chunk(src: torch.Tensor, dst: torch.Tensor, start: int, nrows: int,
     written = ctypes.c_size_t(0)
     check(lib().b200q8_quantize_chunk(src.data_ptr(), dst.data_ptr(), start, nrows, n_per_row,
                                       ctypes.byref(written), stream_ptr()))
+    return int(written.value)
+
+
+def quantize_chunk_host(src, dst, start: int, nrows: int, n_per_row: int, device: int = 0) -> int:
+    """ggml_quantize_chunk(Q8_0, ...) on host numpy/torch-CPU buffers (the quantize tool's call); returns bytes written."""
+    import numpy as np
+
+    def ptr(a):
+        return a.ctypes.data if isinstance(a, np.ndarray) else a.data_ptr()
+
+    written = ctypes.c_size_t(0)
+    check(lib().b200q8_quantize_chunk_host(ptr(src), ptr(dst), start, nrows, n_per_row, ctypes.byref(written), device))
     return int(written.value)
 
 

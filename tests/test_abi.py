@@ -23,6 +23,53 @@ def test_every_declared_symbol_is_exported(pkg):
     assert set(declared) <= exported
 
 
+def test_ggml_seam_header_is_exported_by_the_host_library(pkg):
+    import os
+
+    from synthesize_cpp_b200 import _abi, host
+
+    hdr = os.path.join(os.path.dirname(_abi.HEADER), "b200q8_ggml.h")
+    declared = _abi.header_symbols(hdr)
+    assert declared == ["b200q8_ggml_compute_node", "b200q8_ggml_graph_compute", "b200q8_ggml_supports_op",
+                        "b200q8_ggml_workspace_size"]
+    L = host.lib()
+    for name in declared:
+        assert hasattr(L, name), name
+
+
+def test_ggml_supports_op_rules(pkg):
+    from synthesize_cpp_b200 import ggml_seam as G
+
+    K, N, M = 1024, 3072, 3
+    w = G.tensor(G.TYPE_Q8_0, [K, N], [34, K // 32 * 34])
+    x = G.tensor(G.TYPE_F32, [K, M], [4, K * 4])
+    y = G.tensor(G.TYPE_F32, [N, M], [4, N * 4], op=G.OP_MUL_MAT, src=(w, x))
+    assert G.supports_op(y)
+    assert G.lib().b200q8_ggml_workspace_size(y) == pkg.lib().b200q8_mul_mat_workspace_size(K, N, M)
+    # F16 weights, odd K, shape mismatch, strided elements: refused (ggml-cpu keeps them)
+    w16 = G.tensor(G.TYPE_F16, [K, N], [2, K * 2])
+    assert not G.supports_op(G.tensor(G.TYPE_F32, [N, M], [4, N * 4], op=G.OP_MUL_MAT, src=(w16, x)))
+    wodd = G.tensor(G.TYPE_Q8_0, [40, N], [34, 68])
+    xodd = G.tensor(G.TYPE_F32, [40, M], [4, 160])
+    assert not G.supports_op(G.tensor(G.TYPE_F32, [N, M], [4, N * 4], op=G.OP_MUL_MAT, src=(wodd, xodd)))
+    assert not G.supports_op(G.tensor(G.TYPE_F32, [N + 1, M], [4, N * 4 + 4], op=G.OP_MUL_MAT, src=(w, x)))
+    xs = G.tensor(G.TYPE_F32, [K, M], [8, K * 8])
+    assert not G.supports_op(G.tensor(G.TYPE_F32, [N, M], [4, N * 4], op=G.OP_MUL_MAT, src=(w, xs)))
+    # broadcast over dim 2: src0 ne2 = 2, src1 ne2 = 4 is fine, 3 is not
+    w3 = G.tensor(G.TYPE_Q8_0, [K, N, 2], [34, K // 32 * 34, N * K // 32 * 34])
+    x4 = G.tensor(G.TYPE_F32, [K, M, 4], [4, K * 4, K * M * 4])
+    assert G.supports_op(G.tensor(G.TYPE_F32, [N, M, 4], [4, N * 4, N * M * 4], op=G.OP_MUL_MAT, src=(w3, x4)))
+    x3 = G.tensor(G.TYPE_F32, [K, M, 3], [4, K * 4, K * M * 4])
+    assert not G.supports_op(G.tensor(G.TYPE_F32, [N, M, 3], [4, N * 4, N * M * 4], op=G.OP_MUL_MAT, src=(w3, x3)))
+    # GET_ROWS of a Q8_0 table by I32 ids
+    table = G.tensor(G.TYPE_Q8_0, [K, 3072], [34, K // 32 * 34])
+    ids = G.tensor(G.TYPE_I32, [5], [4])
+    assert G.supports_op(G.tensor(G.TYPE_F32, [K, 5], [4, K * 4], op=G.OP_GET_ROWS, src=(table, ids)))
+    ids16 = G.tensor(G.TYPE_F16, [5], [2])
+    assert not G.supports_op(G.tensor(G.TYPE_F32, [K, 5], [4, K * 4], op=G.OP_GET_ROWS, src=(table, ids16)))
+    assert not G.supports_op(G.tensor(G.TYPE_F32, [K, 5], [4, K * 4], op=99, src=(table, ids)))
+
+
 def test_version_and_workspace(pkg):
     from synthesize_cpp_b200 import _abi
 

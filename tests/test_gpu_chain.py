@@ -74,12 +74,12 @@ def make_chain(chain_mod, layers, t_table, path, **kw):
 
 
 @pytest.mark.parametrize("m,path", [(1, "persistent"), (2, "persistent"), (1, "per_op"), (2, "per_op"),
-                                    (9, "per_op")])
+                                    (8, "per_op"), (9, "per_op"), (64, "per_op")])
 def test_chain_per_op(chain_mod, O, dev, m, path):
     n_layers = 2
     mats, norms, table = make_model(O, n_layers)
     layers, t_table = upload(mats, norms, table, dev)
-    ch = make_chain(chain_mod, layers, t_table, path, max_m=16)
+    ch = make_chain(chain_mod, layers, t_table, path, max_m=max(16, m))
     ids = np.arange(m, dtype=np.int32) * 5 % 64
     x_in = np.asarray(np.random.default_rng(m).standard_normal((m, H)), np.float32)
     h_out = torch.empty((m, H), dtype=torch.float32, device=dev)

@@ -107,3 +107,23 @@ def test_bad_arguments_raise(q8, dev):
     with pytest.raises(q8.B200Q8Error) as e:
         q8.quantize_rows(x)
     assert e.value.status == 1
+
+
+def test_quantize_chunk_host_matches_oracle(q8, O):
+    # the quantize tool's call on host buffers: start offset, several chunks, bytes as the reference
+    rows, k = 1200, 3072  # 14.7 MB of F32 -> several 128 MB-bounded chunks? one; exercise start too
+    src = O.normal(91, rows * k, 0.05)
+    dst = np.zeros(rows * (k // 32 * 34), np.uint8)
+    n = q8.quantize_chunk_host(src, dst, 200 * k, 1000, k)
+    ref, nref = O.quantize_chunk(src, 200 * k, 1000, k)
+    assert n == nref == 1000 * (k // 32 * 34)
+    assert np.array_equal(dst, ref)
+
+
+def test_quantize_chunk_host_many_chunks(q8, O):
+    rows, k = 12000, 4096  # 196 MB of F32: two 128 MB chunks through both streams
+    src = np.asarray(np.random.default_rng(3).standard_normal(rows * k), np.float32)
+    dst = np.zeros(rows * (k // 32 * 34), np.uint8)
+    assert q8.quantize_chunk_host(src, dst, 0, rows, k) == dst.size
+    ref, _ = O.quantize_chunk(src, 0, rows, k)
+    assert np.array_equal(dst, ref)
