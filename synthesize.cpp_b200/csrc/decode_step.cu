@@ -121,13 +121,13 @@ struct Smem {
     unsigned * epoch;
     int *      abort_local;
     double *   rms_part;   // [kStepConsumerWarps][2] (header room for 16 warps)
-    float *    rms_scale;  // [2]
+    float *    rms_scale;  // unused slot kept for the header layout
     float *    hbuf;       // [M_T][H]
     float *    h1buf;      // [M_T][H]
     float *    normbuf;    // [H] the RMS-norm weight of the current norm op
     float *    ybuf;       // [M_T][2*kStepYMax]
-    uint8_t *  xc;         // codes [M_T][Kmax]
-    float *    xd;         // scales [M_T][Kmax/32]
+    uint8_t *  xc[2];      // staged codes [M_T][Kmax], double buffered by op parity
+    float *    xd[2];      // staged scales [M_T][Kmax/32]
     uint8_t *  ring;
 };
 
@@ -202,11 +202,11 @@ __device__ __forceinline__ bool ll_settle(const StepArgs & a, const Smem & s, co
 // Phase A of a norm stage: h_dst[m][i] = h_src[m][i] + published delta[m][i]
 // for all i < H (delta read as LL words; delta == nullptr: h_dst already
 // holds the values), accumulating sum of squares per token.  Then the
-// per-token RMS scale.  Leaves the result in s.rms_scale.
+// per-token RMS scale, returned in scale_out (every thread gets it).
 template <int M_T>
 __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsigned long long * delta,
                                  const float * h_src, float * h_dst, int M, unsigned epoch, float * trace_h,
-                                 const float * norm, bool & fail) {
+                                 const float * norm, bool & fail, float (&scale_out)[M_T]) {
     const int H = a.H;
     const int t = threadIdx.x;
     // The norm weight goes to shared memory now, its L2 latency hidden under
@@ -284,47 +284,56 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
         }
     }
     named_barrier_sync(1, kStepConsumers);
-    if (t < M) {
+    // every thread sums the per-warp partials in the same order (no second
+    // barrier needed to hand the scale around)
+#pragma unroll
+    for (int m = 0; m < M_T; ++m) {
         double tot = 0.0;
         for (int w = 0; w < kStepConsumerWarps; ++w) {
-            tot += s.rms_part[w * 2 + t];
+            tot += s.rms_part[w * 2 + m];
         }
         const float mean = (float) (tot / (double) H);
-        s.rms_scale[t]   = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
+        scale_out[m]     = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
     }
-    named_barrier_sync(1, kStepConsumers);
 }
 
-// Quantizes K values per token into s.xc / s.xd.  Four lanes per block,
-// eight values per lane, so each warp quantizes eight blocks at once.
-// src_kind: 0 = normed shared buffer (hsrc * scale * norm), 1 = LL words via
-// index map (GQA expansion when map_gqa, else identity).
-template <int M_T, int MODE>
-__device__ void stage_activations(const StepArgs & a, const Smem & s, int K, int M, int src_kind,
-                                  const float * hsrc, const float * norm, const unsigned long long * ll, size_t ll_stride,
-                                  bool map_gqa, unsigned epoch, float * trace_x, size_t trace_stride, bool & fail) {
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int NB   = K >> 5;
-    const int g4   = lane >> 2;
-    const int e4   = lane & 3;
+// Quantizes K values per token into the staging buffer xc/xd (chunk-major
+// layout of tile_dot.cuh).  LPB lanes per block, 32/LPB values per lane; the
+// caller picks LPB so that every block of a token is staged in one round
+// (LL inputs are waited for round by round).  src_kind: 0 = normed shared
+// buffer (hsrc * scale * norm), 1 = LL words via index map (GQA expansion
+// when map_gqa, else identity).  Ends with the consumer barrier, which also
+// ORs every thread's failure flag: returns true when the step must stop.
+template <int M_T, int MODE, int LPB>
+__device__ bool stage_activations_t(const StepArgs & a, const Smem & s, int K, int M, int src_kind, const float * hsrc,
+                                    const float * norm, const float (&scale)[M_T], const unsigned long long * ll,
+                                    size_t ll_stride, bool map_gqa, unsigned epoch, float * trace_x,
+                                    size_t trace_stride, uint8_t * xc, float * xd, bool & fail) {
+    constexpr int E    = 32 / LPB;  // values per lane
+    constexpr int BPW  = 32 / LPB;  // blocks per warp per round
+    const int     warp = threadIdx.x >> 5;
+    const int     lane = threadIdx.x & 31;
+    const int     NB   = K >> 5;
+    const int     NSB  = K >> 8;
+    const int     gb   = lane / LPB;  // block within the warp's BPW
+    const int     eb   = lane % LPB;  // values E*eb .. E*eb+E-1 of the block
     for (int m = 0; m < M; ++m)
-    for (int base = warp * 8; base < NB; base += kStepConsumerWarps * 8) {
-        const int  b     = base + g4;
+    for (int base = warp * BPW; base < NB; base += kStepConsumerWarps * BPW) {
+        const int  b     = base + gb;
         const bool valid = b < NB;
-        const int  i0    = (valid ? b : 0) * kQK + e4 * 8;
-        float      v[8];
+        const int  i0    = (valid ? b : 0) * kQK + eb * E;
+        float      v[E];
         if (src_kind == 0) {
+            const float sc = scale[m < M_T ? m : 0];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                v[k] = valid ? __fmul_rn(__fmul_rn(hsrc[(size_t) m * K + i0 + k], s.rms_scale[m]), norm[i0 + k])
-                             : 0.0f;
+            for (int k = 0; k < E; ++k) {
+                v[k] = valid ? __fmul_rn(__fmul_rn(hsrc[(size_t) m * K + i0 + k], sc), norm[i0 + k]) : 0.0f;
             }
         } else {
-            const unsigned long long * src[8];
-            unsigned long long         w[8];
+            const unsigned long long * src[E];
+            unsigned long long         w[E];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
+            for (int k = 0; k < E; ++k) {
                 int j = i0 + k;
                 if (map_gqa) {  // query head j >> lg_hd reads kv head (j >> lg_hd) >> lg_group
                     j = (((j >> a.lg_head_dim) >> a.lg_group) << a.lg_head_dim) | (j & ((1 << a.lg_head_dim) - 1));
@@ -332,39 +341,67 @@ __device__ void stage_activations(const StepArgs & a, const Smem & s, int K, int
                 src[k] = ll + (size_t) m * ll_stride + j;
                 w[k]   = valid ? ld_ll(src[k]) : ((unsigned long long) epoch << 32);
             }
-            if (!fail && !ll_settle<8>(a, s, src, w, valid ? 8 : 0, epoch)) {
+            if (!fail && !ll_settle<E>(a, s, src, w, valid ? E : 0, epoch)) {
                 fail = true;
             }
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
+            for (int k = 0; k < E; ++k) {
                 v[k] = valid ? __uint_as_float((unsigned) (w[k] & 0xffffffffu)) : 0.0f;
             }
         }
-        const float       am = block_amax<4, 8>(v, e4);
+        const float       am = block_amax<LPB, E>(v, eb);
         const QuantParams qp = quant_params<MODE>(am);
-        uint32_t          lo = 0, hi = 0;
+        uint32_t          words[E / 4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            lo |= (uint32_t) (quant_code<MODE>(v[k], qp.id) & 0xff) << (8 * k);
-            hi |= (uint32_t) (quant_code<MODE>(v[4 + k], qp.id) & 0xff) << (8 * k);
+        for (int q = 0; q < E / 4; ++q) {
+            words[q] = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                words[q] |= (uint32_t) (quant_code<MODE>(v[4 * q + k], qp.id) & 0xff) << (8 * k);
+            }
         }
         if (valid) {
-            // chunk-major layout of tile_dot.cuh's superblock path
-            const int pos = ((b & 7) << 5) + e4 * 8;
-            uint2 *   dst = reinterpret_cast<uint2 *>(s.xc + sb_code_offset(m, K, K >> 8, b >> 3, pos));
-            *dst          = make_uint2(lo, hi);
-            if (e4 == 0) {
-                s.xd[m * NB + b] = qp.d;
+            const int pos = ((b & 7) << 5) + eb * E;  // E consecutive codes stay inside one 16-byte chunk
+            uint8_t * dst = xc + sb_code_offset(m, K, NSB, b >> 3, pos);
+            if (E == 4) {
+                *reinterpret_cast<uint32_t *>(dst) = words[0];
+            } else if (E == 8) {
+                *reinterpret_cast<uint2 *>(dst) = make_uint2(words[0], words[1]);
+            } else {
+                *reinterpret_cast<uint4 *>(dst) = make_uint4(words[0], words[1], words[2], words[3 % (E / 4)]);
+            }
+            if (eb == 0) {
+                xd[m * NB + b] = qp.d;
             }
             if (trace_x != nullptr) {
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
+                for (int k = 0; k < E; ++k) {
                     trace_x[(size_t) m * trace_stride + i0 + k] = v[k];
                 }
             }
         }
     }
-    named_barrier_sync(1, kStepConsumers);
+    return consumers_any(fail || aborted(a, s));
+}
+
+// One round per token whatever K is: 8 lanes per block up to 32*kStepConsumerWarps/8
+// blocks, then 4, then 2.
+template <int M_T, int MODE>
+__device__ bool stage_activations(const StepArgs & a, const Smem & s, int K, int M, int src_kind, const float * hsrc,
+                                  const float * norm, const float (&scale)[M_T], const unsigned long long * ll,
+                                  size_t ll_stride, bool map_gqa, unsigned epoch, float * trace_x, size_t trace_stride,
+                                  uint8_t * xc, float * xd, bool & fail) {
+    const int NB = K >> 5;
+    if (NB <= kStepConsumerWarps * 4) {
+        return stage_activations_t<M_T, MODE, 8>(a, s, K, M, src_kind, hsrc, norm, scale, ll, ll_stride, map_gqa,
+                                                 epoch, trace_x, trace_stride, xc, xd, fail);
+    }
+    if (NB <= kStepConsumerWarps * 8) {
+        return stage_activations_t<M_T, MODE, 4>(a, s, K, M, src_kind, hsrc, norm, scale, ll, ll_stride, map_gqa,
+                                                 epoch, trace_x, trace_stride, xc, xd, fail);
+    }
+    return stage_activations_t<M_T, MODE, 2>(a, s, K, M, src_kind, hsrc, norm, scale, ll, ll_stride, map_gqa, epoch,
+                                             trace_x, trace_stride, xc, xd, fail);
 }
 
 // Consumes all tiles of one op in a single pass over all consumer warps.
@@ -376,7 +413,8 @@ __device__ void stage_activations(const StepArgs & a, const Smem & s, int K, int
 template <int M_T, typename Pub>
 __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, int S, int & sl, uint32_t & ph,
                                            const Seg * segs, int nseg, bool pair_units, int K, int M, int warp,
-                                           int lane, bool & fail, int op, Pub && publish) {
+                                           int lane, const uint8_t * xc, const float * xd, bool & fail, int op,
+                                           Pub && publish) {
     constexpr int kMaxOpTiles = 16;
     int           t_sl[kMaxOpTiles];
     uint32_t      t_ph[kMaxOpTiles];
@@ -399,9 +437,10 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
 #ifdef B200Q8_TIMELINE
     const long long tc0 = clock64();
 #endif
-    bool bad = fail || nt > kMaxOpTiles;
-    for (int i = 0; i < nt && !bad; ++i) {
-        if (!mbar_wait_bounded(&s.full[t_sl[i]], t_ph[i])) {
+    // lane i probes tile i's barrier, so the op's tiles are checked in one go
+    bool bad = fail || nt > kMaxOpTiles || nt > 32;
+    if (!bad && lane < nt) {
+        if (!mbar_wait_bounded(&s.full[t_sl[lane]], t_ph[lane])) {
             raise_abort(a, s);
             bad = true;
         }
@@ -415,13 +454,13 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
     if (!bad) {
         const int      NSB    = K >> 8;  // superblocks per row
         const int      NB     = K >> 5;
-        const int      lgs    = NSB <= 1 ? 0 : min(5, 32 - __clz(NSB - 1));  // ~1 superblock per lane
+        const int      lgs    = min(5, 32 - __clz(2 * NSB - 1));  // ~1 half-superblock per lane
         const int      GS     = 1 << lgs;
         const int      gpw    = 32 >> lgs;  // groups per warp
         const int      ngroup = kStepConsumerWarps * gpw;
         const int      gl     = lane & (GS - 1);
-        const uint32_t xc_s   = smem_addr(s.xc);
-        const uint32_t xd_s   = smem_addr(s.xd);
+        const uint32_t xc_s   = smem_addr(xc);
+        const uint32_t xd_s   = smem_addr(xd);
         const uint32_t ring_s = smem_addr(s.ring);
         const int      nunit  = segs[0].n;
         auto row_addr = [&](int g, int r) -> uint32_t {
@@ -442,9 +481,9 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
                 acc1[m] = 0.0f;
             }
             if (active) {
-                dot_row_sb<M_T>(row_addr(0, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc0);
+                dot_row_half<M_T>(row_addr(0, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc0);
                 if (pair_units) {
-                    dot_row_sb<M_T>(row_addr(1, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc1);
+                    dot_row_half<M_T>(row_addr(1, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc1);
                 }
             }
             group_reduce<M_T>(acc0, GS);
@@ -505,10 +544,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     off += (size_t) H * 4;
     s.ybuf = reinterpret_cast<float *>(smem + off);
     off += (size_t) M_T * 2 * kStepYMax * 4;
-    s.xc = smem + off;
-    off += (size_t) M_T * Kmax;
-    s.xd = reinterpret_cast<float *>(smem + off);
-    off += (size_t) M_T * (Kmax / kQK) * 4;
+    for (int i = 0; i < 2; ++i) {
+        s.xc[i] = smem + off;
+        off += (size_t) M_T * Kmax;
+        s.xd[i] = reinterpret_cast<float *>(smem + off);
+        off += (size_t) M_T * (Kmax / kQK) * 4;
+    }
     off    = (off + 127) & ~(size_t) 127;
     s.ring = smem + off;
     const int S = a.n_slots;
@@ -624,19 +665,28 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         Seg                        segs[5];
         layer_segs(a, plan, l, segs);
 
+        // Staged activations alternate between two buffers op by op.
+        float no_scale[M_T];
+#pragma unroll
+        for (int m = 0; m < M_T; ++m) {
+            no_scale[m] = 1.0f;
+        }
+        float scale[M_T];
         // ---- qkv = W_qkv * Q(rms_norm(h) * norm_in), h = h1 + d(l-1); v published
         TL(4 * l + 0, 0);
         const unsigned long long * prev_d = l > 0 ? a.ll + (size_t) (l - 1) * a.ll_layer + llm * (a.KV + a.H + a.I)
                                                   : nullptr;
         residual_and_rms<M_T>(a, s, prev_d, s.h1buf, s.hbuf, M, epoch, (l > 0 && c == 0) ? trace(l - 1, 9) : nullptr,
-                              L.norm_in, fail);
+                              L.norm_in, fail, scale);
         TL(4 * l + 0, 1);
-        stage_activations<M_T, MODE>(a, s, H, M, 0, s.hbuf, s.normbuf, nullptr, 0, false, epoch,
-                                     c == 0 ? trace(l, 0) : nullptr, (size_t) H, fail);
+        if (stage_activations<M_T, MODE>(a, s, H, M, 0, s.hbuf, s.normbuf, scale, nullptr, 0, false, epoch,
+                                         c == 0 ? trace(l, 0) : nullptr, (size_t) H, s.xc[0], s.xd[0], fail)) {
+            break;
+        }
         TL(4 * l + 0, 2);
         {
             float * tq = trace(l, 1);
-            consume_op<M_T>(a, s, S, sl, ph, &segs[0], 1, false, H, M, warp, lane, fail, 4 * l + 0,
+            consume_op<M_T>(a, s, S, sl, ph, &segs[0], 1, false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 0,
                             [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
                                 const int row = pq.r0 + u;
 #pragma unroll
@@ -653,18 +703,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                             });
         }
         TL(4 * l + 0, 3);
+        // park warps that are done until the whole op is: a warp polling the
+        // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
-        TL(4 * l + 0, 4);
         // ---- o = W_o * Q(attend(v)); attention over one cached position; o published
         TL(4 * l + 1, 0);
-        stage_activations<M_T, MODE>(a, s, a.Q, M, 1, nullptr, nullptr, ll_v, (size_t) a.KV, true, epoch,
-                                     c == 0 ? trace(l, 2) : nullptr, (size_t) a.Q, fail);
+        if (stage_activations<M_T, MODE>(a, s, a.Q, M, 1, nullptr, nullptr, no_scale, ll_v, (size_t) a.KV, true,
+                                         epoch, c == 0 ? trace(l, 2) : nullptr, (size_t) a.Q, s.xc[1], s.xd[1],
+                                         fail)) {
+            break;
+        }
         TL(4 * l + 1, 2);
         {
             float * to = trace(l, 3);
-            consume_op<M_T>(a, s, S, sl, ph, &segs[1], 1, false, a.Q, M, warp, lane, fail, 4 * l + 1,
+            consume_op<M_T>(a, s, S, sl, ph, &segs[1], 1, false, a.Q, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 1,
                             [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
 #pragma unroll
                                 for (int m = 0; m < M_T; ++m) {
@@ -678,22 +732,25 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                             });
         }
         TL(4 * l + 1, 3);
+        // park warps that are done until the whole op is: a warp polling the
+        // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
-        TL(4 * l + 1, 4);
         // ---- g|u = W_gate|W_up * Q(rms_norm(h1) * norm_post), h1 = h + o; s = silu(g)*u published
         TL(4 * l + 2, 0);
         residual_and_rms<M_T>(a, s, ll_o, s.hbuf, s.h1buf, M, epoch, c == 0 ? trace(l, 4) : nullptr, L.norm_post,
-                              fail);
+                              fail, scale);
         TL(4 * l + 2, 1);
-        stage_activations<M_T, MODE>(a, s, H, M, 0, s.h1buf, s.normbuf, nullptr, 0, false, epoch,
-                                     c == 0 ? trace(l, 5) : nullptr, (size_t) H, fail);
+        if (stage_activations<M_T, MODE>(a, s, H, M, 0, s.h1buf, s.normbuf, scale, nullptr, 0, false, epoch,
+                                         c == 0 ? trace(l, 5) : nullptr, (size_t) H, s.xc[0], s.xd[0], fail)) {
+            break;
+        }
         TL(4 * l + 2, 2);
         {
             float * tgu = trace(l, 6);
             float * ts  = trace(l, 7);
-            consume_op<M_T>(a, s, S, sl, ph, &segs[2], 2, true, H, M, warp, lane, fail, 4 * l + 2,
+            consume_op<M_T>(a, s, S, sl, ph, &segs[2], 2, true, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 2,
                             [&](int u, const float (&g)[M_T], const float (&up)[M_T]) {
 #pragma unroll
                                 for (int m = 0; m < M_T; ++m) {
@@ -712,19 +769,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                             });
         }
         TL(4 * l + 2, 3);
+        // park warps that are done until the whole op is: a warp polling the
+        // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
-        TL(4 * l + 2, 4);
         // ---- d = W_down * Q(s); d published (the last layer writes h_out = h1 + d)
         TL(4 * l + 3, 0);
-        stage_activations<M_T, MODE>(a, s, a.I, M, 1, nullptr, nullptr, ll_s, (size_t) a.I, false, epoch, nullptr,
-                                     0, fail);
+        if (stage_activations<M_T, MODE>(a, s, a.I, M, 1, nullptr, nullptr, no_scale, ll_s, (size_t) a.I, false,
+                                         epoch, nullptr, 0, s.xc[1], s.xd[1], fail)) {
+            break;
+        }
         TL(4 * l + 3, 2);
         {
             float *    td   = trace(l, 8);
             const bool last = l == a.n_layers - 1;
-            consume_op<M_T>(a, s, S, sl, ph, &segs[4], 1, false, a.I, M, warp, lane, fail, 4 * l + 3,
+            consume_op<M_T>(a, s, S, sl, ph, &segs[4], 1, false, a.I, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 3,
                             [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
                                 const int row = po.r0 + u;
 #pragma unroll
@@ -743,10 +803,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                             });
         }
         TL(4 * l + 3, 3);
+        // park warps that are done until the whole op is: a warp polling the
+        // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
             break;
         }
-        TL(4 * l + 3, 4);
     }
 }
 
@@ -758,8 +819,8 @@ size_t decode_step_smem_bytes(const StepArgs & a, int mt, int & n_slots) {
     off += (size_t) mt * a.H * 4 * 2;
     off += (size_t) a.H * 4;
     off += (size_t) mt * 2 * kStepYMax * 4;
-    off += (size_t) mt * Kmax;
-    off += (size_t) mt * (Kmax / kQK) * 4;
+    off += 2 * (size_t) mt * Kmax;
+    off += 2 * (size_t) mt * (Kmax / kQK) * 4;
     off                   = (off + 127) & ~(size_t) 127;
     const size_t limit    = 227 * 1024;
     if (off + kStepSlotBytes * 2 > limit) {

@@ -265,4 +265,66 @@ __device__ __forceinline__ void dot_row_sb(uint32_t row, int NSB, int NB, int K,
     }
 }
 
+// Half-superblock units: a lane takes 4 blocks (136 bytes, 8-byte aligned:
+// 17 64-bit shared loads) -- twice the lanes of dot_row_sb on the same row,
+// half the work per lane.  Unit u of a row is half (u & 1) of superblock
+// (u >> 1).
+template <int M_T>
+__device__ __forceinline__ void dot_row_half(uint32_t row, int NSB, int NB, int K, int gl, int GS, uint32_t xc_s,
+                                             uint32_t xd_s, int M, float (&acc)[M_T]) {
+    for (int u = gl; u < 2 * NSB; u += GS) {
+        const int j = u >> 1;
+        const int h = u & 1;
+        uint32_t  w[34];
+#pragma unroll
+        for (int k = 0; k < 17; ++k) {
+            uint32_t lo, hi;
+            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
+                         : "=r"(lo), "=r"(hi)
+                         : "r"(row + (uint32_t) (272 * j + 136 * h + 8 * k)));
+            w[2 * k]     = lo;
+            w[2 * k + 1] = hi;
+        }
+#pragma unroll
+        for (int m = 0; m < M_T; ++m) {
+            if (m < M) {
+                const uint4 dq    = lds_v4(xd_s + (uint32_t) ((m * NB + 8 * j + 4 * h) * 4));
+                const float dx[4] = { __uint_as_float(dq.x), __uint_as_float(dq.y), __uint_as_float(dq.z),
+                                      __uint_as_float(dq.w) };
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int      wb = 17 * (b >> 1);
+                    const float    dw = __half2float(__ushort_as_half(
+                        (unsigned short) ((b & 1) ? (w[wb + 8] >> 16) : (w[wb] & 0xffffu))));
+                    const int      bs = 4 * h + b;  // block within the superblock
+                    const uint32_t x0 = xc_s + (uint32_t) (m * K + (((2 * bs) * NSB + j) << 4));
+                    const uint4    xa = lds_v4(x0);
+                    const uint4    xb = lds_v4(x0 + (uint32_t) (NSB << 4));
+                    int            s0 = 0, s1 = 0;
+                    if (b & 1) {
+                        s0 = __dp4a((int) w[wb + 9], (int) xa.x, s0);
+                        s1 = __dp4a((int) w[wb + 10], (int) xa.y, s1);
+                        s0 = __dp4a((int) w[wb + 11], (int) xa.z, s0);
+                        s1 = __dp4a((int) w[wb + 12], (int) xa.w, s1);
+                        s0 = __dp4a((int) w[wb + 13], (int) xb.x, s0);
+                        s1 = __dp4a((int) w[wb + 14], (int) xb.y, s1);
+                        s0 = __dp4a((int) w[wb + 15], (int) xb.z, s0);
+                        s1 = __dp4a((int) w[wb + 16], (int) xb.w, s1);
+                    } else {
+                        s0 = __dp4a((int) __byte_perm(w[wb + 0], w[wb + 1], 0x5432), (int) xa.x, s0);
+                        s1 = __dp4a((int) __byte_perm(w[wb + 1], w[wb + 2], 0x5432), (int) xa.y, s1);
+                        s0 = __dp4a((int) __byte_perm(w[wb + 2], w[wb + 3], 0x5432), (int) xa.z, s0);
+                        s1 = __dp4a((int) __byte_perm(w[wb + 3], w[wb + 4], 0x5432), (int) xa.w, s1);
+                        s0 = __dp4a((int) __byte_perm(w[wb + 4], w[wb + 5], 0x5432), (int) xb.x, s0);
+                        s1 = __dp4a((int) __byte_perm(w[wb + 5], w[wb + 6], 0x5432), (int) xb.y, s1);
+                        s0 = __dp4a((int) __byte_perm(w[wb + 6], w[wb + 7], 0x5432), (int) xb.z, s0);
+                        s1 = __dp4a((int) __byte_perm(w[wb + 7], w[wb + 8], 0x5432), (int) xb.w, s1);
+                    }
+                    acc[m] = __fmaf_rn((float) (s0 + s1), __fmul_rn(dw, dx[b]), acc[m]);
+                }
+            }
+        }
+    }
+}
+
 }  // namespace b200q8
