@@ -155,10 +155,7 @@ cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, int64_t M, f
     const b200q8_chain_desc & d = c->d;
     const int64_t H = d.hidden, Q = d.n_head * d.head_dim, KV = d.n_kv * d.head_dim, I = d.inter;
     const int     hd = (int) d.head_dim, grp = (int) (d.n_head / d.n_kv);
-    const int64_t Kmax = std::max(std::max(H, Q), I);
-    int8_t *      codes;
-    float *       scales;
-    gemm_planes(c->planes, Kmax, M, &codes, &scales);
+    uint8_t *     xrec = static_cast<uint8_t *>(c->planes);
     cudaError_t e = cudaSuccess;
     for (int l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
         auto B = [&](int layer, int which) { return c->buf(layer, which); };
@@ -166,34 +163,34 @@ cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, int64_t M, f
         // qkv: n1 = rms_norm(h) * norm_in with h = h1(l-1) + d(l-1)
         if (l == 0) {
             e = launch_stage_rows(0, c->h0, nullptr, (size_t) H, nullptr, 0, c->layers[l].norm_in, d.eps, (int) H, hd,
-                                  grp, B(l, kN1), (size_t) H, M, d.mode, codes, scales, st, true);
+                                  grp, B(l, kN1), (size_t) H, M, d.mode, xrec, st, true);
         } else {
             e = launch_stage_rows(0, B(l - 1, kH1), B(l - 1, kDown), (size_t) H, B(l - 1, kHout), (size_t) H,
-                                  c->layers[l].norm_in, d.eps, (int) H, hd, grp, B(l, kN1), (size_t) H, M, d.mode, codes,
-                                  scales, st, true);
+                                  c->layers[l].norm_in, d.eps, (int) H, hd, grp, B(l, kN1), (size_t) H, M, d.mode, xrec,
+                                  st, true);
         }
         if (e == cudaSuccess)
-            e = launch_gemm_planes(c->w_qkv[l], c->rb_h, H, c->qkv_dim, codes, scales, M, B(l, kQkv),
+            e = launch_gemm_staged(c->w_qkv[l], c->rb_h, H, c->qkv_dim, xrec, M, B(l, kQkv),
                                    (size_t) c->qkv_dim, st, c->sms, true);
         // o: attend(v)
         if (e == cudaSuccess)
             e = launch_stage_rows(1, B(l, kQkv) + Q + KV, nullptr, (size_t) c->qkv_dim, nullptr, 0, nullptr, d.eps,
-                                  (int) Q, hd, grp, B(l, kAttn), (size_t) Q, M, d.mode, codes, scales, st, true);
+                                  (int) Q, hd, grp, B(l, kAttn), (size_t) Q, M, d.mode, xrec, st, true);
         if (e == cudaSuccess)
-            e = launch_gemm_planes(c->w_o[l], c->rb_q, Q, H, codes, scales, M, B(l, kO), (size_t) H, st, c->sms, true);
+            e = launch_gemm_staged(c->w_o[l], c->rb_q, Q, H, xrec, M, B(l, kO), (size_t) H, st, c->sms, true);
         // gate|up: n2 = rms_norm(h1) * norm_post with h1 = h + o
         if (e == cudaSuccess)
             e = launch_stage_rows(0, h_in, B(l, kO), (size_t) H, B(l, kH1), (size_t) H, c->layers[l].norm_post, d.eps,
-                                  (int) H, hd, grp, B(l, kN2), (size_t) H, M, d.mode, codes, scales, st, true);
+                                  (int) H, hd, grp, B(l, kN2), (size_t) H, M, d.mode, xrec, st, true);
         if (e == cudaSuccess)
-            e = launch_gemm_planes(c->w_gu[l], c->rb_h, H, 2 * I, codes, scales, M, B(l, kGu), (size_t) (2 * I), st,
+            e = launch_gemm_staged(c->w_gu[l], c->rb_h, H, 2 * I, xrec, M, B(l, kGu), (size_t) (2 * I), st,
                                    c->sms, true);
         // down: silu(g) * u
         if (e == cudaSuccess)
             e = launch_stage_rows(2, B(l, kGu), B(l, kGu) + I, (size_t) (2 * I), nullptr, 0, nullptr, d.eps, (int) I, hd,
-                                  grp, B(l, kS), (size_t) I, M, d.mode, codes, scales, st, true);
+                                  grp, B(l, kS), (size_t) I, M, d.mode, xrec, st, true);
         if (e == cudaSuccess)
-            e = launch_gemm_planes(c->w_d[l], c->rb_i, I, H, codes, scales, M, B(l, kDown), (size_t) H, st, c->sms,
+            e = launch_gemm_staged(c->w_d[l], c->rb_i, I, H, xrec, M, B(l, kDown), (size_t) H, st, c->sms,
                                    true);
     }
     if (e == cudaSuccess) {
@@ -345,7 +342,7 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
     if (e == cudaSuccess) {
         e = cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking);
     }
-    bool batched_ok = d.max_m > 8;
+    bool batched_ok = d.max_m > 8 && d.head_dim % 4 == 0;
     for (int l = 0; l < d.n_layers && batched_ok; ++l) {
         batched_ok = gemm_supported(c->w_qkv[l], c->rb_h, H, c->qkv_dim, d.max_m) &&
                      gemm_supported(c->w_o[l], c->rb_q, Q, H, d.max_m) &&

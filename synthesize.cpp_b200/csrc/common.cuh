@@ -276,6 +276,25 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     return policy;
 }
 
+// L2 policy for data that other CTAs read again soon (shared activations).
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+__device__ __forceinline__ uint64_t lds_u64(uint32_t addr) {
+    uint64_t v;
+    asm volatile("ld.shared.u64 %0, [%1];" : "=l"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
+}
+
 // Programmatic dependent launch: no-ops unless the launch enabled it.
 __device__ __forceinline__ void pdl_wait_primary() {
     asm volatile("griddepcontrol.wait;" ::: "memory");

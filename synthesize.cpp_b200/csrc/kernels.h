@@ -65,23 +65,30 @@ cudaError_t launch_gemv_generic(const uint8_t * w, size_t row_bytes, int64_t K, 
 
 // ---- int8 tensor-core GEMM for M > 8 (gemm.cu)
 
-size_t      gemm_workspace_bytes(int64_t K, int64_t M);
-bool        gemm_supported(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, int64_t M);
-cudaError_t launch_gemm(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const float * x, size_t x_stride,
-                        int64_t M, float * y, size_t y_stride, int mode, void * workspace, cudaStream_t stream,
-                        int sm_count);
-// The code / scale planes inside a GEMM workspace of these sizes.
-void        gemm_planes(void * workspace, int64_t K, int64_t M, int8_t ** codes, float ** scales);
-cudaError_t launch_gemm_planes(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const int8_t * codes,
-                               const float * scales, int64_t M, float * y, size_t y_stride, cudaStream_t stream,
-                               int sm_count, bool pdl);
-// Batched-step prologue (one CTA per token): kind 0 = rms_norm(a [+ b]) * norm
-// (a + b also written to sum_out), 1 = GQA expansion of a, 2 = silu(a) * b;
-// the result is quantized into the planes.
-cudaError_t launch_stage_rows(int kind, const float * a, const float * b, size_t ab_stride, float * sum_out,
-                              size_t sum_stride, const float * norm, float eps, int K, int head_dim, int group,
-                              float * trace, size_t trace_stride, int64_t M, int mode, int8_t * codes, float * scales,
-                              cudaStream_t stream, bool pdl);
+// Token chunking shared by the stage kernels and the GEMM: n_tc chunks of tm
+// tokens (tm a multiple of 8, at most 64; the last chunk may be partial).
+struct GemmChunking {
+    int tm;
+    int n_tc;
+};
+GemmChunking gemm_chunking(int64_t M);
+// Bytes of the staged activations of M tokens of K values (K % 256 == 0).
+size_t       gemm_workspace_bytes(int64_t K, int64_t M);
+bool         gemm_supported(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, int64_t M);
+// Stage (quantize) x into the workspace, then the GEMM.
+cudaError_t  launch_gemm(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const float * x, size_t x_stride,
+                         int64_t M, float * y, size_t y_stride, int mode, void * workspace, cudaStream_t stream,
+                         int sm_count);
+// The GEMM on activations already staged by launch_stage_rows.
+cudaError_t  launch_gemm_staged(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const uint8_t * xrec,
+                                int64_t M, float * y, size_t y_stride, cudaStream_t stream, int sm_count, bool pdl);
+// Per-token prologue (one CTA per token): kind 0 = rms_norm(a [+ b]) * norm
+// (a + b also written to sum_out), 1 = GQA expansion of a, 2 = silu(a) * b,
+// 3 = a; the result is quantized into the staged records xrec.
+cudaError_t  launch_stage_rows(int kind, const float * a, const float * b, size_t ab_stride, float * sum_out,
+                               size_t sum_stride, const float * norm, float eps, int K, int head_dim, int group,
+                               float * trace, size_t trace_stride, int64_t M, int mode, uint8_t * xrec,
+                               cudaStream_t stream, bool pdl);
 cudaError_t launch_residual_rows(const float * a, const float * b, size_t ab_stride, float * out, size_t out_stride,
                                  int K, int64_t M, cudaStream_t stream, bool pdl);
 

@@ -100,6 +100,17 @@ def test_tensor_core_gemm(q8, O, dev, n, k, m):
     check_close(y, y_ref, bound)
 
 
+@pytest.mark.parametrize("n,k,m", [(1024, 1024, 72), (1000, 2048, 130), (3072, 1024, 1024), (256, 8192, 24),
+                                   (48, 512, 9)])
+def test_tensor_core_gemm_token_chunks(q8, O, dev, n, k, m):
+    # M > 64 splits tokens into chunks of <= 64 (72 -> 2 x 40, 130 -> 3 x 48); K up to 8192
+    wq_np = O.quantize_rows(O.normal(n + 7 * k, n * k, 0.02).reshape(n, k))
+    x = activations(m, k, seed=m + k, outliers=True)
+    y = q8.mul_mat(to_dev(wq_np, dev), k, to_dev(x, dev)).cpu().numpy()
+    y_ref, bound = O.mul_mat(wq_np, k, x)
+    check_close(y, y_ref, bound)
+
+
 @pytest.mark.parametrize("mode", [1, 2])
 def test_tensor_core_gemm_modes(q8, O, dev, mode):
     n, k, m = 3072, 1024, 24
