@@ -14,15 +14,19 @@
 // 256-wide K chunk for a chunk of tm tokens: tm rows of 256 code bytes whose
 // 16-byte units are XOR-swizzled by token, then the chunk's 8 x tm fp32
 // scales.  A CTA works on units of (token chunk, RB weight rows, all of K):
-// each 256-wide K chunk of the unit's weight rows (RB 1-D copies of 272
-// bytes, one per row) and the matching activation record (one copy) land in
-// one shared-memory slot of a ring, so weights and activations stream
-// together and every byte is loaded once per unit.  Eight consumer warps
+// each 256-wide K chunk of the unit's weight rows (one 2-D tiled TMA load of
+// a 272-byte x RB-row box through a tensor map over the standard Q8_0 rows)
+// and the matching activation record (one 1-D bulk copy) land in one
+// shared-memory slot of a ring, so weights and activations stream together
+// and every byte is loaded once per unit.  Eight consumer warps
 // split the unit into 16-row tiles x block subsets of the chunk; partial sums
 // over K are combined through shared memory in a fixed order, so results are
 // deterministic.  Copies are never multicast.
 #include "common.cuh"
 #include "kernels.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 
@@ -40,11 +44,25 @@ constexpr int   kMaxTokenChunk     = 64;
 constexpr int   kMmaBias           = 0x4B400000;  // float 12582912.0f
 constexpr float kMmaBiasF          = 12582912.0f;
 
-__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-    asm volatile(
+// Registers only: not volatile, so the compiler may interleave MMAs with loads.
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint2 b) {
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
+}
+
+// 2-D tiled TMA load of the box at (x, y) of `map` into this CTA's shared
+// memory (128-byte aligned), completing on `bar`.  x counts 2-byte elements
+// and is a multiple of 8 (16-byte aligned); rows past the tensor read as 0.
+// Never multicast.
+__device__ __forceinline__ void tma_load_2d(void * dst_smem, const CUtensorMap * map, int x, int y, uint64_t * bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst_smem)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
 }
 
 // Byte offset of code byte i (0..31) of block j (0..7) of token t inside a
@@ -56,34 +74,59 @@ __host__ __device__ __forceinline__ int rec_code_offset(int t, int j, int i) {
 }
 
 // The 8 code bytes 8*tq .. 8*tq+7 of block j of a staged weight row (34-byte
-// blocks, so only 2-byte aligned; the alignment class depends on j alone).
-// Lanes load 8 consecutive bytes rather than the two 4-byte groups of the
-// standard fragment: A and B use the same permutation of k, so every MMA
-// still sums exactly the products of matching codes.
-template <int J>
-__device__ __forceinline__ uint2 lds_w8(uint32_t row, int tq) {
-    const uint32_t off = (uint32_t) (J * kBlockBytes + 2 + 8 * tq);
-    uint2          r;
-    if ((off & 7) == 0) {
-        const uint64_t v = lds_u64(row + off);
-        r.x              = (uint32_t) v;
-        r.y              = (uint32_t) (v >> 32);
-    } else if ((off & 3) == 0) {
-        r.x = lds_u32(row + off);
-        r.y = lds_u32(row + off + 4);
-    } else if (((off - 2) & 7) == 0) {
-        const uint64_t v  = lds_u64(row + off - 2);
-        const uint32_t w2 = lds_u32(row + off + 6);
-        r.x               = __byte_perm((uint32_t) v, (uint32_t) (v >> 32), 0x5432);
-        r.y               = __byte_perm((uint32_t) (v >> 32), w2, 0x5432);
-    } else {
-        const uint32_t w0 = lds_u32(row + off - 2);
-        const uint64_t v  = lds_u64(row + off + 2);
-        r.x               = __byte_perm(w0, (uint32_t) v, 0x5432);
-        r.y               = __byte_perm((uint32_t) v, (uint32_t) (v >> 32), 0x5432);
+// blocks, so only 2-byte aligned; the alignment class depends on j alone and
+// folds away once j is a constant).  Lanes load 8 consecutive bytes rather
+// than the two 4-byte groups of the standard fragment: A and B use the same
+// permutation of k, so every MMA still sums exactly the products of matching
+// codes.  Plain loads: the compiler may schedule them, but not across the
+// mbarrier operations (which clobber memory).
+__device__ __forceinline__ void ld_w8(int j, const uint8_t * row, int tq, uint2 & r) {
+    const int       cls = (j * kBlockBytes + 2) & 7;
+    const uint8_t * p   = row + j * kBlockBytes + 2 + 8 * tq;
+    if (cls == 0) {
+        r = *reinterpret_cast<const uint2 *>(p);
+    } else if (cls == 4) {
+        r.x = *reinterpret_cast<const uint32_t *>(p);
+        r.y = *reinterpret_cast<const uint32_t *>(p + 4);
+    } else if (cls == 2) {
+        const uint2    v  = *reinterpret_cast<const uint2 *>(p - 2);
+        const uint32_t w2 = *reinterpret_cast<const uint32_t *>(p + 6);
+        r.x               = __byte_perm(v.x, v.y, 0x5432);
+        r.y               = __byte_perm(v.y, w2, 0x5432);
+    } else {  // cls == 6
+        const uint32_t w0 = *reinterpret_cast<const uint32_t *>(p - 2);
+        const uint2    v  = *reinterpret_cast<const uint2 *>(p + 2);
+        r.x               = __byte_perm(w0, v.x, 0x5432);
+        r.y               = __byte_perm(v.x, v.y, 0x5432);
     }
-    return r;
 }
+
+#ifdef B200Q8_TIMELINE
+// Analysis builds only: globaltimer stamps per (launch slot, CTA, event) of
+// the GEMM and stage kernels; slots are assigned on the host at launch (or
+// capture) time.
+constexpr int kTlSlots = 256, kTlCtas = 256;
+__device__ unsigned long long g_tl[kTlSlots * kTlCtas * 8];
+__device__ __forceinline__ void tl_stamp(int slot, int ev) {
+    unsigned long long g;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g));
+    if (slot >= 0 && slot < kTlSlots && blockIdx.x < kTlCtas) {
+        g_tl[((size_t) slot * kTlCtas + blockIdx.x) * 8 + ev] = g;
+    }
+}
+static int  g_tl_next = 0;
+static char g_tl_kind[kTlSlots];
+int tl_take(char kind) {
+    const int s = g_tl_next++;
+    if (s < kTlSlots) {
+        g_tl_kind[s] = kind;
+    }
+    return s;
+}
+#define GTL(ev) tl_stamp(a.tl_slot, ev)
+#else
+#define GTL(ev) ((void) 0)
+#endif
 
 struct GemmArgs {
     const uint8_t * w;
@@ -98,11 +141,13 @@ struct GemmArgs {
     int             n_rb;      // row blocks = ceil(N / rb)
     int             n_units;   // n_tc * n_rb
     int             n_slots;
+    int             tl_slot;   // timeline builds only
 };
 
-// TG: token groups of 8 a warp can hold (>= tm / 8).
+// TG: token groups of 8 in a token chunk (tm = 8 * TG).
 template <int TG>
-__global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_q8_0_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *     full       = reinterpret_cast<uint64_t *>(smem);
     uint64_t *     empty      = full + kGemmMaxSlots;
@@ -121,6 +166,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
     const int    G         = gridDim.x;
 
     if (threadIdx.x == 0) {
+        GTL(0);
         for (int i = 0; i < kGemmMaxSlots; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], kGemmConsumerWarps);
@@ -132,30 +178,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
     pdl_launch_dependents();
 
     if (warp == kGemmConsumerWarps) {
-        // Producer warp: lane 0 arms each slot, then all lanes issue the row
-        // copies.  Weights are constant, so the first S slots' weights stream
-        // before the wait on the kernel that wrote the activations.
+        // Producer warp (lane 0 issues): weights are constant, so the first
+        // S slots' weights stream before the wait on the kernel that wrote
+        // the activations.
         const uint64_t wpol     = a.n_tc == 1 ? l2_evict_first_policy() : l2_evict_last_policy();
         const uint64_t xpol     = l2_evict_last_policy();
         const int      my_units = (a.n_units - (int) blockIdx.x + G - 1) / G;
         const int      total    = my_units * n_kc;
         // fill i = chunk kc of the CTA's unit i / n_kc; it uses slot i % S
         auto issue_w = [&](int i, int si) {
-            const int ui   = i / n_kc;
-            const int kc   = i - ui * n_kc;
-            const int u    = (int) blockIdx.x + ui * G;
-            const int tc   = u / a.n_rb;
-            const int r0   = (u - tc * a.n_rb) * a.rb;
-            const int rows = min(a.rb, a.N - r0);
+            const int ui = i / n_kc;
+            const int kc = i - ui * n_kc;
+            const int u  = (int) blockIdx.x + ui * G;
+            const int tc = u / a.n_rb;
+            const int r0 = (u - tc * a.n_rb) * a.rb;
             if (lane == 0) {
-                mbar_arrive_expect_tx(&full[si], (uint32_t) (rows * kChunkRowBytes + rec_bytes));
-            }
-            __syncwarp();
-            uint8_t * dst = ring + (size_t) si * slot;
-            for (int r = lane; r < rows; r += 32) {
-                bulk_copy_g2s(dst + (size_t) r * kChunkRowBytes,
-                              a.w + (size_t) (r0 + r) * a.row_bytes + (size_t) kc * kChunkRowBytes,
-                              (uint32_t) kChunkRowBytes, &full[si], wpol);
+                // the box counts in full, rows past N included (they read as 0)
+                mbar_arrive_expect_tx(&full[si], (uint32_t) (w_bytes + rec_bytes));
+                tma_load_2d(ring + (size_t) si * slot, &wmap, kc * (kChunkRowBytes / 2), r0, &full[si], wpol);
             }
         };
         auto issue_x = [&](int i, int si) {
@@ -173,7 +213,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
         for (int i = 0; i < pre; ++i) {
             issue_w(i, i);
         }
+        if (lane == 0) GTL(1);
         pdl_wait_primary();
+        if (lane == 0) GTL(2);
         for (int i = 0; i < pre; ++i) {
             issue_x(i, i);
         }
@@ -213,22 +255,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
                     record_device_error((unsigned) B200Q8_ERR_DEVICE_TIMEOUT);
                 }
             }
+            GTL(6);
         }
         return;
     }
 
     // consumer roles: 16-row tile rt of the unit, block subset ks of each chunk
-    const int rt_n  = a.rb >> 4;
-    const int ks_n  = kChunkBlocks / rt_n > 0 ? kChunkBlocks / rt_n : 1;  // K subsets (8 warps = rt_n x ks_n)
-    const int rt    = warp % rt_n;
-    const int ks    = warp / rt_n;
-    const int j0    = ks * (kChunkBlocks / ks_n);
-    const int j1    = j0 + kChunkBlocks / ks_n;
-    const int g     = lane >> 2;
-    const int tq    = lane & 3;
-    const int n_tg  = a.tm >> 3;
-    const uint32_t ring_s = smem_addr(ring);
-    const float2   biasf  = make_float2(kMmaBiasF, kMmaBiasF);
+    const int rt_n = a.rb >> 4;
+    const int ks_n = kChunkBlocks / rt_n;  // 8 warps = rt_n row tiles x ks_n block subsets
+    const int rt   = warp % rt_n;
+    const int ks   = warp / rt_n;
+    const int j0   = ks * rt_n;            // this warp's blocks of each chunk: j0 .. j0 + rt_n - 1
+    const int j1   = j0 + rt_n;
+    const int g    = lane >> 2;
+    const int tq   = lane & 3;
+    const float2 nbias = make_float2(-kMmaBiasF, -kMmaBiasF);
+    float4 *     red4  = reinterpret_cast<float4 *>(red);
 
     int      s    = 0;
     uint32_t ph   = 0;
@@ -253,54 +295,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
                 fail        = true;
             }
             fail = __any_sync(0xffffffffu, fail);  // mma.sync needs the whole warp
+#ifdef B200Q8_TIMELINE
+            if (threadIdx.x == 0 && kc == 0 && u == (int) blockIdx.x) GTL(3);
+#endif
             if (!fail) {
-                const uint32_t wt    = ring_s + (uint32_t) (s * slot);
-                const uint32_t row_a = wt + (uint32_t) ((rt * 16 + g) * kChunkRowBytes);
-                const uint32_t row_b = row_a + 8 * kChunkRowBytes;
-                const uint32_t xc    = wt + (uint32_t) w_bytes;
-                const uint32_t xsc   = xc + (uint32_t) (a.tm * kChunkBlocks * kQK);
+                const uint8_t * wt    = ring + (size_t) s * slot;
+                const uint8_t * row_a = wt + (rt * 16 + g) * kChunkRowBytes;
+                const uint8_t * row_b = row_a + 8 * kChunkRowBytes;
+                const uint8_t * xc    = wt + w_bytes;
+                const float *   xsc   = reinterpret_cast<const float *>(xc + TG * 8 * kChunkBlocks * kQK);
 #pragma unroll
                 for (int j = 0; j < kChunkBlocks; ++j) {
-                    if (j >= j0 && j < j1) {
+                    if (j >= j0 && j < j1) {  // warp-uniform
                         uint2 wa, wb;
-                        switch (j) {
-                            case 0: wa = lds_w8<0>(row_a, tq); wb = lds_w8<0>(row_b, tq); break;
-                            case 1: wa = lds_w8<1>(row_a, tq); wb = lds_w8<1>(row_b, tq); break;
-                            case 2: wa = lds_w8<2>(row_a, tq); wb = lds_w8<2>(row_b, tq); break;
-                            case 3: wa = lds_w8<3>(row_a, tq); wb = lds_w8<3>(row_b, tq); break;
-                            case 4: wa = lds_w8<4>(row_a, tq); wb = lds_w8<4>(row_b, tq); break;
-                            case 5: wa = lds_w8<5>(row_a, tq); wb = lds_w8<5>(row_b, tq); break;
-                            case 6: wa = lds_w8<6>(row_a, tq); wb = lds_w8<6>(row_b, tq); break;
-                            default: wa = lds_w8<7>(row_a, tq); wb = lds_w8<7>(row_b, tq); break;
-                        }
+                        ld_w8(j, row_a, tq, wa);
+                        ld_w8(j, row_b, tq, wb);
                         const uint32_t A[4] = { wa.x, wb.x, wa.y, wb.y };
-                        const float    da   = __half2float(__ushort_as_half(
-                            (unsigned short) lds_u16(row_a + (uint32_t) (j * kBlockBytes))));
-                        const float db = __half2float(__ushort_as_half(
-                            (unsigned short) lds_u16(row_b + (uint32_t) (j * kBlockBytes))));
+                        const float    da   = __half2float(*reinterpret_cast<const __half *>(row_a + j * kBlockBytes));
+                        const float    db   = __half2float(*reinterpret_cast<const __half *>(row_b + j * kBlockBytes));
+                        uint2  bv[TG];
+                        float2 xv[TG];
+#pragma unroll
+                        for (int tg = 0; tg < TG; ++tg) {
+                            const int unit = (2 * j + (tq >> 1)) ^ (g << 1);
+                            bv[tg]         = *reinterpret_cast<const uint2 *>(
+                                xc + (tg * 8 + g) * (kChunkBlocks * kQK) + unit * 16 + (tq & 1) * 8);
+                            xv[tg] = *reinterpret_cast<const float2 *>(xsc + j * (TG * 8) + tg * 8 + 2 * tq);
+                        }
+                        int D[TG][4];
+#pragma unroll
+                        for (int tg = 0; tg < TG; ++tg) {
+                            D[tg][0] = D[tg][1] = D[tg][2] = D[tg][3] = kMmaBias;
+                            mma_s8(D[tg], A, bv[tg]);
+                        }
                         const float2 da2 = make_float2(da, da);
                         const float2 db2 = make_float2(db, db);
 #pragma unroll
                         for (int tg = 0; tg < TG; ++tg) {
-                            if (tg < n_tg) {
-                                const int      t    = tg * 8 + g;
-                                const int      unit = (2 * j + (tq >> 1)) ^ (g << 1);
-                                const uint64_t bv =
-                                    lds_u64(xc + (uint32_t) (t * (kChunkBlocks * kQK) + unit * 16 + (tq & 1) * 8));
-                                const uint32_t B[2] = { (uint32_t) bv, (uint32_t) (bv >> 32) };
-                                const float2   x2 =
-                                    lds_f2(xsc + (uint32_t) ((j * a.tm + tg * 8 + 2 * tq) * 4));
-                                int D[4] = { kMmaBias, kMmaBias, kMmaBias, kMmaBias };
-                                mma_s8(D, A, B);
-                                const float2 s01 = __fadd2_rn(
-                                    make_float2(__int_as_float(D[0]), __int_as_float(D[1])),
-                                    make_float2(-biasf.x, -biasf.y));
-                                const float2 s23 = __fadd2_rn(
-                                    make_float2(__int_as_float(D[2]), __int_as_float(D[3])),
-                                    make_float2(-biasf.x, -biasf.y));
-                                acc[tg][0] = __ffma2_rn(s01, __fmul2_rn(da2, x2), acc[tg][0]);
-                                acc[tg][1] = __ffma2_rn(s23, __fmul2_rn(db2, x2), acc[tg][1]);
-                            }
+                            const float2 s01 =
+                                __fadd2_rn(make_float2(__int_as_float(D[tg][0]), __int_as_float(D[tg][1])), nbias);
+                            const float2 s23 =
+                                __fadd2_rn(make_float2(__int_as_float(D[tg][2]), __int_as_float(D[tg][3])), nbias);
+                            acc[tg][0] = __ffma2_rn(s01, __fmul2_rn(da2, xv[tg]), acc[tg][0]);
+                            acc[tg][1] = __ffma2_rn(s23, __fmul2_rn(db2, xv[tg]), acc[tg][1]);
                         }
                     }
                 }
@@ -314,59 +351,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q8_0_kernel(const GemmAr
                 ph ^= 1;
             }
         }
-        // combine the block subsets in a fixed order (subset 0 adds 1, 2, ...)
-        if (ks_n > 1) {
-            if (ks != 0) {
-                float4 * mine = reinterpret_cast<float4 *>(red) + (size_t) (warp * TG) * 32 + lane;
-#pragma unroll
-                for (int tg = 0; tg < TG; ++tg) {
-                    if (tg < n_tg) {
-                        mine[tg * 32] = make_float4(acc[tg][0].x, acc[tg][0].y, acc[tg][1].x, acc[tg][1].y);
-                    }
-                }
-            }
-            named_barrier_sync(1, kGemmConsumerWarps * 32);
-            if (ks == 0) {
-                for (int k2 = 1; k2 < ks_n; ++k2) {
-                    const float4 * o =
-                        reinterpret_cast<const float4 *>(red) + (size_t) ((warp + k2 * rt_n) * TG) * 32 + lane;
-#pragma unroll
-                    for (int tg = 0; tg < TG; ++tg) {
-                        if (tg < n_tg) {
-                            const float4 v = o[tg * 32];
-                            acc[tg][0].x += v.x;
-                            acc[tg][0].y += v.y;
-                            acc[tg][1].x += v.z;
-                            acc[tg][1].y += v.w;
-                        }
-                    }
-                }
-            }
-            named_barrier_sync(1, kGemmConsumerWarps * 32);
-        }
-        if (ks == 0 && !fail && *abort_flag == 0) {
+        if (threadIdx.x == 0) GTL(4);
+        // Combine the block subsets of each row tile in a fixed order
+        // (subset 0 + 1 + ...); the ks_n warps of a row tile share the token
+        // groups of the combine and the stores.
+        auto store = [&](int tg, float4 v) {
             const int ra = rt * 16 + g;
+            const int c0 = tg * 8 + 2 * tq;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int tok = tok0 + c0 + q;
+                if (tok < a.M) {
+                    float * dst = a.y + (size_t) tok * a.y_stride + r0;
+                    if (ra < rows) {
+                        dst[ra] = q ? v.y : v.x;
+                    }
+                    if (ra + 8 < rows) {
+                        dst[ra + 8] = q ? v.w : v.z;
+                    }
+                }
+            }
+        };
+        if (ks_n > 1) {
 #pragma unroll
             for (int tg = 0; tg < TG; ++tg) {
-                if (tg < n_tg) {
-                    const int c0 = tg * 8 + 2 * tq;
+                red4[(warp * TG + tg) * 32 + lane] = make_float4(acc[tg][0].x, acc[tg][0].y, acc[tg][1].x, acc[tg][1].y);
+            }
+            named_barrier_sync(1, kGemmConsumerWarps * 32);
+            const bool ok = !fail && *abort_flag == 0;
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        const int tok = tok0 + c0 + q;
-                        if (c0 + q < a.tm && tok < a.M) {
-                            float * dst = a.y + (size_t) tok * a.y_stride + r0;
-                            if (ra < rows) {
-                                dst[ra] = q ? acc[tg][0].y : acc[tg][0].x;
-                            }
-                            if (ra + 8 < rows) {
-                                dst[ra + 8] = q ? acc[tg][1].y : acc[tg][1].x;
-                            }
-                        }
+            for (int tg = 0; tg < TG; ++tg) {
+                if (tg % ks_n == ks) {
+                    float4 v = red4[(rt * TG + tg) * 32 + lane];
+                    for (int k2 = 1; k2 < ks_n; ++k2) {
+                        const float4 o = red4[((rt + k2 * rt_n) * TG + tg) * 32 + lane];
+                        v.x += o.x;
+                        v.y += o.y;
+                        v.z += o.z;
+                        v.w += o.w;
+                    }
+                    if (ok) {
+                        store(tg, v);
                     }
                 }
+            }
+            named_barrier_sync(1, kGemmConsumerWarps * 32);
+        } else if (!fail && *abort_flag == 0) {
+#pragma unroll
+            for (int tg = 0; tg < TG; ++tg) {
+                store(tg, make_float4(acc[tg][0].x, acc[tg][0].y, acc[tg][1].x, acc[tg][1].y));
             }
         }
     }
+    if (threadIdx.x == 0) GTL(5);
+    if (threadIdx.x == 32 * (kGemmConsumerWarps - 1)) GTL(7);
 }
 
 // Stage one token's GEMM input: one CTA per token, each thread holds E
@@ -392,14 +430,22 @@ struct StageArgs {
     size_t        trace_stride;
     uint8_t *     xrec;
     int           tm;
+    int           tl_slot;  // timeline builds only
 };
 
 template <int MODE, int E>
 __global__ void __launch_bounds__(1024) stage_rows_kernel(const StageArgs s) {
     __shared__ double part[32];
     __shared__ float  scale_s;
+#ifdef B200Q8_TIMELINE
+    const StageArgs & a = s;
+    if (threadIdx.x == 0) GTL(0);
+#endif
     pdl_launch_dependents();
     pdl_wait_primary();
+#ifdef B200Q8_TIMELINE
+    if (threadIdx.x == 0) GTL(1);
+#endif
     const int     m    = blockIdx.x;
     const int     t    = threadIdx.x;
     const int     T    = blockDim.x;
@@ -503,6 +549,10 @@ __global__ void __launch_bounds__(1024) stage_rows_kernel(const StageArgs s) {
             }
         }
     }
+#ifdef B200Q8_TIMELINE
+    __syncthreads();
+    if (threadIdx.x == 0) GTL(2);
+#endif
 }
 
 __global__ void residual_rows_kernel(const float * __restrict__ a, const float * __restrict__ b, size_t ab_stride,
@@ -569,9 +619,49 @@ size_t gemm_fixed_bytes(int tg) {
     return 128 + (size_t) kGemmConsumerWarps * 32 * tg * 4 * 4;
 }
 
+// cuTensorMapEncodeTiled from the driver, through the runtime (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *                          p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            p = nullptr;
+        }
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// Q8_0 rows viewed as a 2-D tensor of 2-byte elements: row_bytes / 2 wide,
+// N high; box = one 256-wide K chunk (136 elements = 272 bytes) x rb rows.
+bool encode_weight_map(CUtensorMap * map, const uint8_t * w, size_t row_bytes, int64_t N, int rb) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr) {
+        return false;
+    }
+    const cuuint64_t dims[2]    = { (cuuint64_t) (row_bytes / 2), (cuuint64_t) N };
+    const cuuint64_t strides[1] = { (cuuint64_t) row_bytes };
+    const cuuint32_t box[2]     = { (cuuint32_t) (kChunkRowBytes / 2), (cuuint32_t) rb };
+    const cuuint32_t estr[2]    = { 1, 1 };
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t *>(w), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// token groups of 8 per chunk: the kernel's template argument
 int gemm_tg(int tm) {
-    const int n_tg = tm / 8;
-    return n_tg <= 2 ? 2 : n_tg <= 4 ? 4 : 8;
+    return tm / 8;
+}
+
+template <int TG>
+cudaError_t launch_gemm_tg(const GemmArgs & a, const CUtensorMap & wmap, int grid, size_t smem, cudaStream_t stream,
+                           bool pdl) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemm_q8_0_kernel<TG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    return e != cudaSuccess ? e
+                            : launch_pdl(gemm_q8_0_kernel<TG>, dim3((unsigned) grid), dim3(kGemmThreads), smem, stream,
+                                         pdl, a, wmap);
 }
 
 }  // namespace
@@ -607,6 +697,11 @@ cudaError_t launch_stage_rows(int kind, const float * a, const float * b, size_t
     s.trace_stride = trace_stride;
     s.xrec         = xrec;
     s.tm           = gemm_chunking(M).tm;
+#ifdef B200Q8_TIMELINE
+    s.tl_slot = tl_take('s');
+#else
+    s.tl_slot = -1;
+#endif
     return launch_stage(s, M, mode, stream, pdl);
 }
 
@@ -623,7 +718,7 @@ size_t gemm_workspace_bytes(int64_t K, int64_t M) {
 
 bool gemm_supported(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, int64_t M) {
     // K % 256: whole 272-byte chunks, 16-byte aligned in every row
-    if (M < 1 || M > 1024 || N < 1 || N > (int64_t) 1 << 30 || K < 256 || K % 256 != 0 || K > 8192 ||
+    if (M < 1 || M > 1024 || N < 16 || N > (int64_t) 1 << 30 || K < 256 || K % 256 != 0 || K > 8192 ||
         row_bytes % 16 != 0 || row_bytes < (size_t) (K / kQK) * kBlockBytes ||
         (reinterpret_cast<uintptr_t>(w) % 16) != 0) {
         return false;
@@ -646,6 +741,11 @@ cudaError_t launch_gemm_staged(const uint8_t * w, size_t row_bytes, int64_t K, i
     a.y_stride           = y_stride;
     a.tm                 = c.tm;
     a.n_tc               = c.n_tc;
+#ifdef B200Q8_TIMELINE
+    a.tl_slot = tl_take('g');
+#else
+    a.tl_slot = -1;
+#endif
     const int tg         = gemm_tg(c.tm);
     const size_t fixed   = gemm_fixed_bytes(tg);
     // Rows per unit: fewer, larger units share each activation record among
@@ -653,7 +753,7 @@ cudaError_t launch_gemm_staged(const uint8_t * w, size_t row_bytes, int64_t K, i
     // a fixed share for the record and the unit's combine step).
     int    best_rb   = 16;
     double best_cost = 1e300;
-    for (int rb = 16; rb <= 128; rb *= 2) {
+    for (int rb = 16; rb <= 128 && rb <= N; rb *= 2) {
         if (fixed + 2 * gemm_slot_bytes(rb, c.tm) > (size_t) kGemmSmemLimit) {
             break;
         }
@@ -675,23 +775,20 @@ cudaError_t launch_gemm_staged(const uint8_t * w, size_t row_bytes, int64_t K, i
     }
     const size_t smem = fixed + (size_t) a.n_slots * slot;
     const int    grid = std::min(a.n_units, sm_count);
-    cudaError_t  e;
+    CUtensorMap  wmap;
+    if (!encode_weight_map(&wmap, w, row_bytes, N, a.rb)) {
+        return cudaErrorInvalidValue;
+    }
     switch (tg) {
-        case 2:
-            e = cudaFuncSetAttribute(gemm_q8_0_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-            return e != cudaSuccess ? e
-                                    : launch_pdl(gemm_q8_0_kernel<2>, dim3((unsigned) grid), dim3(kGemmThreads), smem,
-                                                 stream, pdl, a);
-        case 4:
-            e = cudaFuncSetAttribute(gemm_q8_0_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-            return e != cudaSuccess ? e
-                                    : launch_pdl(gemm_q8_0_kernel<4>, dim3((unsigned) grid), dim3(kGemmThreads), smem,
-                                                 stream, pdl, a);
-        default:
-            e = cudaFuncSetAttribute(gemm_q8_0_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-            return e != cudaSuccess ? e
-                                    : launch_pdl(gemm_q8_0_kernel<8>, dim3((unsigned) grid), dim3(kGemmThreads), smem,
-                                                 stream, pdl, a);
+        case 1: return launch_gemm_tg<1>(a, wmap, grid, smem, stream, pdl);
+        case 2: return launch_gemm_tg<2>(a, wmap, grid, smem, stream, pdl);
+        case 3: return launch_gemm_tg<3>(a, wmap, grid, smem, stream, pdl);
+        case 4: return launch_gemm_tg<4>(a, wmap, grid, smem, stream, pdl);
+        case 5: return launch_gemm_tg<5>(a, wmap, grid, smem, stream, pdl);
+        case 6: return launch_gemm_tg<6>(a, wmap, grid, smem, stream, pdl);
+        case 7: return launch_gemm_tg<7>(a, wmap, grid, smem, stream, pdl);
+        case 8: return launch_gemm_tg<8>(a, wmap, grid, smem, stream, pdl);
+        default: return cudaErrorInvalidValue;
     }
 }
 
@@ -708,3 +805,24 @@ cudaError_t launch_gemm(const uint8_t * w, size_t row_bytes, int64_t K, int64_t 
 }
 
 }  // namespace b200q8
+
+#ifdef B200Q8_TIMELINE
+// Copies the stamps and the slot kinds ('g' GEMM, 's' stage) and restarts slot numbering.
+extern "C" int b200q8_gemm_timeline(unsigned long long * host, size_t n, char * kinds, int reset) {
+    using namespace b200q8;
+    const size_t have = (size_t) kTlSlots * kTlCtas * 8;
+    int          rc   = 0;
+    if (host != nullptr) {
+        rc = cudaMemcpyFromSymbol(host, g_tl, sizeof(unsigned long long) * (n < have ? n : have)) == cudaSuccess ? 0 : 1;
+    }
+    if (kinds != nullptr) {
+        for (int i = 0; i < kTlSlots; ++i) {
+            kinds[i] = i < g_tl_next ? g_tl_kind[i] : 0;
+        }
+    }
+    if (reset) {
+        g_tl_next = 0;
+    }
+    return rc;
+}
+#endif
