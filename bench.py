@@ -149,6 +149,16 @@ def cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s, max_
     return n * m / dt, n, dt
 
 
+def host_threads() -> int:
+    """Every host core this process may run on.  torchrun exports
+    OMP_NUM_THREADS=1 to its ranks; the CPU arm passes its thread count
+    explicitly, so that setting does not shrink it."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def run_reference(args, rank):
     """The reference's CPU path for the same step: rank 0 only, all host threads."""
     if rank != 0:
@@ -177,7 +187,7 @@ def run_reference(args, rank):
     norms = np.stack(norms).astype(np.float32)
     table = O.quantize_rows(host.normal(999, shape.table_rows * shape.hidden, 0.02).reshape(shape.table_rows,
                                                                                              shape.hidden))
-    threads = O.lib().oracle_max_threads()
+    threads = host_threads()
     from synthesize_cpp_b200.workloads import stream_inputs
 
     m = 64 if args.workload == "dp-sweep" else args.batch
@@ -447,7 +457,7 @@ def main():
         import oracle as O
 
         mats, norms, table = host_copy(dm)
-        threads = O.lib().oracle_max_threads()
+        threads = host_threads()
         mcpu = min(m_max, 64)
         tps, n, dt = cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s=12.0, max_tokens=400,
                                             m=mcpu)
