@@ -41,10 +41,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b"],
+    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b", "gemv", "gemv-large"],
                     help="talker: BASELINE config 2 (config 3 with --batch 16/64/256); talker-1.7b: config 4 shapes; "
                          "dp-sweep: config 5, 512 streams split over the ranks in M=64 batches; "
-                         "pack-1.7b: config 4 packing of all 1.4 B weights (synthesize-quantize)")
+                         "pack-1.7b: config 4 packing of all 1.4 B weights (synthesize-quantize); "
+                         "gemv / gemv-large: config 1 GEMV (and a 142 MB one) as an HBM bandwidth measurement")
     ap.add_argument("--batch", type=int, default=1, help="tokens (streams) per step per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chain", default="auto", choices=["auto", "per-op"],
@@ -304,6 +305,120 @@ def run_pack(args, rank, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_gemv(args, rank, local_rank):
+    """BASELINE config 1 as a bandwidth measurement: MUL_MAT(Q8_0 W [N, K], F32 x [K, 1]) over rotating copies
+    of W totalling > 2x L2, captured as a CUDA graph of back-to-back calls (gemv: N=3072, K=1024; gemv-large:
+    N=32768, K=4096, one 142 MB matrix per call)."""
+    import numpy as np
+    import torch
+
+    import __graft_entry__ as g
+
+    g.load_package()
+    from synthesize_cpp_b200 import host, q8
+
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    n, k = (3072, 1024) if args.workload == "gemv" else (32768, 4096)
+    rb = k // 32 * 34
+    w_bytes = n * rb
+    copies = max(2, int(2 * 126e6 // w_bytes) + 1)
+    # weights: the seeded 0.02*N(0,1) stream packed on the device; copies differ by their seed
+    ws = []
+    for c in range(copies):
+        f = np.empty(n * k, np.float32)
+        host.normal_many([c], [0.02], [f])
+        ws.append(q8.quantize_rows(torch.from_numpy(f).to(dev).view(n, k)))
+    x_np = np.empty(k, np.float32)
+    host.normal_many([1], [1.0], [x_np])
+    x = torch.from_numpy(x_np).to(dev).view(1, k)
+    y = torch.empty((1, n), dtype=torch.float32, device=dev)
+    calls_per_graph = copies * max(1, 64 // copies)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for i in range(calls_per_graph):  # warm-up outside capture
+            q8.mul_mat(ws[i % copies], k, x, out=y)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(calls_per_graph):
+            q8.mul_mat(ws[i % copies], k, x, out=y)
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    reps = max(1, args.steps // calls_per_graph)
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream(dev)
+    e0.record(cur)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    calls = reps * calls_per_graph
+    t_call = e0.elapsed_time(e1) / 1e3 / calls
+    if q8.device_status(local_rank) != 0:
+        raise RuntimeError("device status set during the timed region")
+    # parity spot check against the oracle on copy 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    y0 = q8.mul_mat(ws[0], k, x).cpu().numpy().ravel()
+    y_ref, bound = O.mul_mat(ws[0].cpu().numpy(), k, x_np.reshape(1, k))
+    assert np.all(np.abs(y0 - y_ref.ravel()) <= 1e-5 * bound.ravel() + 1e-30)
+    # e2e: host x in, host y out around each call
+    x_host = torch.from_numpy(x_np).view(1, k).pin_memory()
+    y_host = torch.empty((1, n), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(cur)
+    e2e_calls = min(calls, 2000)
+    for i in range(e2e_calls):
+        x_dev.copy_(x_host, non_blocking=True)
+        q8.mul_mat(ws[i % copies], k, x_dev, out=y)
+        y_host.copy_(y, non_blocking=True)
+    f1.record(cur)
+    torch.cuda.synchronize(dev)
+    t_e2e = f0.elapsed_time(f1) / 1e3 / e2e_calls
+    bytes_call = w_bytes + 4 * k + 4 * n
+    peaks, peak_kind = measured_peaks()
+    # CPU: the oracle port on a bounded sample, all host threads
+    threads = host_threads()
+    wq0 = ws[0].cpu().numpy()
+    O.mul_mat(wq0, k, x_np.reshape(1, k), threads=threads)
+    c0, cn = time.perf_counter(), 0
+    while time.perf_counter() - c0 < 3.0:
+        O.mul_mat(wq0, k, x_np.reshape(1, k), threads=threads)
+        cn += 1
+    cpu_t = (time.perf_counter() - c0) / cn
+    line = {
+        "metric": "Q8_0 MUL_MAT HBM GB/s (decode GEMV, M=1)", "value": bytes_call / t_call / 1e9, "unit": "GB/s",
+        "n_gpus": 1, "steps": calls, "warmup": max(args.warmup, 3), "ms_per_step": 1e3 * t_call,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32, f32 scale",
+        "data": "synthetic (seeded 0.02*N(0,1) weights packed on device, N(0,1) x)",
+        "config": {"workload": f"{'BASELINE config 1' if n == 3072 else 'large'} GEMV N={n} K={k} M=1, "
+                               f"{copies} rotating weight copies ({copies * w_bytes / 1e6:.0f} MB > L2), "
+                               f"CUDA graph of {calls_per_graph} calls",
+                   "l2": "weights rotated over copies totalling more than 2x L2"},
+        "roofline": {"bound": "hbm", "achieved": bytes_call / t_call / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": bytes_call / t_call / 1e9 / peaks["hbm_gbs"], "traffic": None,
+                     "kernel": "gemv_q8_0_kernel<1, REF, plain>",
+                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+        "e2e": {"value": bytes_call / t_e2e / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * k,
+                "d2h_bytes_per_step": 4 * n},
+        "gpu_launches": calls,
+        "clocks": clocks,
+        "cpu_baseline": {"value": bytes_call / cpu_t / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{cn} calls on copy 0 (L3-resident on the host; oracle C port, OpenMP)"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -314,6 +429,9 @@ def main():
         return
     if args.workload == "pack-1.7b":
         run_pack(args, rank, local_rank)
+        return
+    if args.workload in ("gemv", "gemv-large"):
+        run_gemv(args, rank, local_rank)
         return
 
     import torch

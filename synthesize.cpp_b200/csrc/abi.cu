@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -196,16 +197,33 @@ b200q8_status_t b200q8_get_rows(const void * table, int64_t K, int64_t rows, siz
     return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "get_rows launch");
 }
 
+// M <= 8 products with at least this many weight bytes (default: all of
+// them) run on the tensor-core GEMM too: one MMA per 16 rows x block, so the
+// weight stream is HBM-bound (a 142 MB M = 1 product streams at 4.8 TB/s,
+// against 2.5 TB/s for the dp4a GEMV, whose per-block instruction count caps
+// it).  Calls without a large enough workspace keep the GEMV.
+// B200Q8_GEMV_VIA_GEMM_MIN_BYTES overrides (bytes, read once).
+static size_t gemv_via_gemm_min_bytes() {
+    static const size_t v = [] {
+        const char * e = getenv("B200Q8_GEMV_VIA_GEMM_MIN_BYTES");
+        return e != nullptr && e[0] != '\0' ? (size_t) strtoull(e, nullptr, 10) : (size_t) 0;
+    }();
+    return v;
+}
+
+static bool small_m_via_gemm(int64_t K, int64_t N, int64_t M) {
+    return M >= 1 && M <= 8 && (size_t) N * (size_t) (K / kQK) * kBlockBytes >= gemv_via_gemm_min_bytes();
+}
+
 size_t b200q8_mul_mat_workspace_size(int64_t K, int64_t N, int64_t M) {
-    (void) N;
     if (K <= 0 || M <= 0 || K % kQK != 0) {
         return 0;
     }
     // the larger of: quantized activations for the general path (M rows of
-    // K/32 blocks) and the tensor-core path's code and scale planes
+    // K/32 blocks) and the tensor-core path's staged activation records
     const size_t general = align_up((size_t) M * (size_t) (K / kQK) * kBlockBytes, 256);
-    const size_t planes  = align_up(gemm_workspace_bytes(K, M), 256);
-    return M > 8 ? std::max(general, planes) : general;
+    const size_t staged  = K % 256 == 0 ? align_up(gemm_workspace_bytes(K, M), 256) : 0;
+    return M > 8 || small_m_via_gemm(K, N, M) ? std::max(general, staged) : general;
 }
 
 b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_row_bytes, const float * x, int64_t M,
@@ -253,6 +271,11 @@ b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_ro
             return set_error(B200Q8_ERR_INVALID_ARG, "mul_mat: M > 8 needs %zu bytes of workspace (got %zu)", need,
                              workspace_bytes);
         }
+        cudaError_t e = launch_gemm(p.w, w_row_bytes, K, N, x, xs, M, y, ys, mode, workspace, st, sms);
+        return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "mul_mat: tensor-core GEMM launch");
+    }
+    if (small_m_via_gemm(K, N, M) && gemm_supported(p.w, w_row_bytes, K, N, M) && workspace != nullptr &&
+        workspace_bytes >= gemm_workspace_bytes(K, M)) {
         cudaError_t e = launch_gemm(p.w, w_row_bytes, K, N, x, xs, M, y, ys, mode, workspace, st, sms);
         return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "mul_mat: tensor-core GEMM launch");
     }

@@ -24,6 +24,7 @@
 // deterministic.  Copies are never multicast.
 #include "common.cuh"
 #include "kernels.h"
+#include "mma_tile.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -41,16 +42,6 @@ constexpr int   kChunkBlocks       = 8;                           // Q8_0 blocks
 constexpr int   kChunkRowBytes     = kChunkBlocks * kBlockBytes;  // 272: one weight row of a chunk
 constexpr int   kRecTokenBytes     = kChunkBlocks * kQK + kChunkBlocks * 4;  // 288: codes + scales
 constexpr int   kMaxTokenChunk     = 64;
-constexpr int   kMmaBias           = 0x4B400000;  // float 12582912.0f
-constexpr float kMmaBiasF          = 12582912.0f;
-
-// Registers only: not volatile, so the compiler may interleave MMAs with loads.
-__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint2 b) {
-    asm(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
-}
 
 // 2-D tiled TMA load of the box at (x, y) of `map` into this CTA's shared
 // memory (128-byte aligned), completing on `bar`.  x counts 2-byte elements
@@ -73,33 +64,6 @@ __host__ __device__ __forceinline__ int rec_code_offset(int t, int j, int i) {
     return t * (kChunkBlocks * kQK) + unit * 16 + (i & 15);
 }
 
-// The 8 code bytes 8*tq .. 8*tq+7 of block j of a staged weight row (34-byte
-// blocks, so only 2-byte aligned; the alignment class depends on j alone and
-// folds away once j is a constant).  Lanes load 8 consecutive bytes rather
-// than the two 4-byte groups of the standard fragment: A and B use the same
-// permutation of k, so every MMA still sums exactly the products of matching
-// codes.  Plain loads: the compiler may schedule them, but not across the
-// mbarrier operations (which clobber memory).
-__device__ __forceinline__ void ld_w8(int j, const uint8_t * row, int tq, uint2 & r) {
-    const int       cls = (j * kBlockBytes + 2) & 7;
-    const uint8_t * p   = row + j * kBlockBytes + 2 + 8 * tq;
-    if (cls == 0) {
-        r = *reinterpret_cast<const uint2 *>(p);
-    } else if (cls == 4) {
-        r.x = *reinterpret_cast<const uint32_t *>(p);
-        r.y = *reinterpret_cast<const uint32_t *>(p + 4);
-    } else if (cls == 2) {
-        const uint2    v  = *reinterpret_cast<const uint2 *>(p - 2);
-        const uint32_t w2 = *reinterpret_cast<const uint32_t *>(p + 6);
-        r.x               = __byte_perm(v.x, v.y, 0x5432);
-        r.y               = __byte_perm(v.y, w2, 0x5432);
-    } else {  // cls == 6
-        const uint32_t w0 = *reinterpret_cast<const uint32_t *>(p - 2);
-        const uint2    v  = *reinterpret_cast<const uint2 *>(p + 2);
-        r.x               = __byte_perm(w0, v.x, 0x5432);
-        r.y               = __byte_perm(v.x, v.y, 0x5432);
-    }
-}
 
 #ifdef B200Q8_TIMELINE
 // Analysis builds only: globaltimer stamps per (launch slot, CTA, event) of
@@ -269,7 +233,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int j1   = j0 + rt_n;
     const int g    = lane >> 2;
     const int tq   = lane & 3;
-    const float2 nbias = make_float2(-kMmaBiasF, -kMmaBiasF);
+    const float2 nbias    = make_float2(-kMmaBiasF, -kMmaBiasF);
+    const int    cbias[4] = { kMmaBias, kMmaBias, kMmaBias, kMmaBias };
     float4 *     red4  = reinterpret_cast<float4 *>(red);
 
     int      s    = 0;
@@ -325,8 +290,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         int D[TG][4];
 #pragma unroll
                         for (int tg = 0; tg < TG; ++tg) {
-                            D[tg][0] = D[tg][1] = D[tg][2] = D[tg][3] = kMmaBias;
-                            mma_s8(D[tg], A, bv[tg]);
+                            mma_s8(D[tg], A, bv[tg], cbias);
                         }
                         const float2 da2 = make_float2(da, da);
                         const float2 db2 = make_float2(db, db);

@@ -75,7 +75,12 @@ def test_version_and_workspace(pkg):
 
     L = _abi.lib()
     assert L.b200q8_version() == 100
-    assert L.b200q8_mul_mat_workspace_size(1024, 3072, 1) == 256 * ((32 * 34 + 255) // 256)
+    # K % 256 == 0: room for the tensor-core path's staged activation records,
+    # (K / 256) chunks x 8 token slots x 288 bytes for M <= 8
+    assert L.b200q8_mul_mat_workspace_size(1024, 3072, 1) == 4 * 8 * 288
+    assert L.b200q8_mul_mat_workspace_size(1024, 3072, 64) == 4 * 64 * 288
+    # other K: the quantized activations of the general path, M rows of K/32 blocks
+    assert L.b200q8_mul_mat_workspace_size(96, 10, 3) == 256 * ((3 * 3 * 34 + 255) // 256)
     assert L.b200q8_mul_mat_workspace_size(33, 1, 1) == 0
 
 

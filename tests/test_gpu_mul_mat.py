@@ -56,13 +56,17 @@ SHAPES = [(2048, 1024), (1024, 1024), (1024, 2048), (3072, 1024), (1024, 3072), 
           (3072, 2048), (256, 256), (7, 512)]
 
 
+@pytest.mark.parametrize("path", ["workspace", "no-workspace"])
 @pytest.mark.parametrize("n,k", SHAPES)
 @pytest.mark.parametrize("m", [1, 2, 3, 8])
-def test_decode_shapes(q8, O, dev, n, k, m):
+def test_decode_shapes(q8, O, dev, n, k, m, path):
+    # with a workspace, M <= 8 runs on the tensor-core GEMM where the shape allows;
+    # without one, on the streaming dp4a GEMV
     w = O.normal(n + k, n * k, 0.02).reshape(n, k)
     wq_np = O.quantize_rows(w)
     x = activations(m, k, seed=n * 7 + k + m)
-    y = q8.mul_mat(to_dev(wq_np, dev), k, to_dev(x, dev)).cpu().numpy()
+    ws = None if path == "workspace" else torch.empty(0, dtype=torch.uint8, device=dev)
+    y = q8.mul_mat(to_dev(wq_np, dev), k, to_dev(x, dev), workspace=ws).cpu().numpy()
     y_ref, bound = O.mul_mat(wq_np, k, x)
     check_close(y, y_ref, bound)
 
@@ -106,6 +110,17 @@ def test_tensor_core_gemm_token_chunks(q8, O, dev, n, k, m):
     # M > 64 splits tokens into chunks of <= 64 (72 -> 2 x 40, 130 -> 3 x 48); K up to 8192
     wq_np = O.quantize_rows(O.normal(n + 7 * k, n * k, 0.02).reshape(n, k))
     x = activations(m, k, seed=m + k, outliers=True)
+    y = q8.mul_mat(to_dev(wq_np, dev), k, to_dev(x, dev)).cpu().numpy()
+    y_ref, bound = O.mul_mat(wq_np, k, x)
+    check_close(y, y_ref, bound)
+
+
+@pytest.mark.parametrize("m", [1, 5, 8])
+def test_small_m_large_weight_on_tensor_cores(q8, O, dev, m):
+    # M <= 8 with >= 16 MB of weights runs the tensor-core GEMM (one MMA per 16 rows x block)
+    n, k = 8192, 2048
+    wq_np = O.quantize_rows(O.normal(4242 + m, n * k, 0.02).reshape(n, k))
+    x = activations(m, k, seed=900 + m, outliers=True)
     y = q8.mul_mat(to_dev(wq_np, dev), k, to_dev(x, dev)).cpu().numpy()
     y_ref, bound = O.mul_mat(wq_np, k, x)
     check_close(y, y_ref, bound)
