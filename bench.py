@@ -41,11 +41,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b", "gemv", "gemv-large"],
+    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b", "gemv", "gemv-large", "mul-mat"],
                     help="talker: BASELINE config 2 (config 3 with --batch 16/64/256); talker-1.7b: config 4 shapes; "
                          "dp-sweep: config 5, 512 streams split over the ranks in M=64 batches; "
                          "pack-1.7b: config 4 packing of all 1.4 B weights (synthesize-quantize); "
-                         "gemv / gemv-large: config 1 GEMV (and a 142 MB one) as an HBM bandwidth measurement")
+                         "gemv / gemv-large: config 1 GEMV (and a 142 MB one) as an HBM bandwidth measurement; "
+                         "mul-mat: one MUL_MAT of --n x --k at M = --batch")
+    ap.add_argument("--n", type=int, default=4096, help="mul-mat: weight rows")
+    ap.add_argument("--k", type=int, default=1024, help="mul-mat: K")
     ap.add_argument("--batch", type=int, default=1, help="tokens (streams) per step per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chain", default="auto", choices=["auto", "per-op"],
@@ -305,10 +308,10 @@ def run_pack(args, rank, local_rank):
     print(json.dumps(line), flush=True)
 
 
-def run_gemv(args, rank, local_rank):
-    """BASELINE config 1 as a bandwidth measurement: MUL_MAT(Q8_0 W [N, K], F32 x [K, 1]) over rotating copies
-    of W totalling > 2x L2, captured as a CUDA graph of back-to-back calls (gemv: N=3072, K=1024; gemv-large:
-    N=32768, K=4096, one 142 MB matrix per call)."""
+def run_mul_mat(args, rank, local_rank):
+    """One MUL_MAT(Q8_0 W [N, K], F32 x [K, M]) per step, W rotated over copies totalling > 2x L2, steps captured
+    as CUDA graphs of back-to-back calls.  gemv: BASELINE config 1 (N=3072, K=1024, M=1); gemv-large: a 142 MB
+    M=1 product (N=32768, K=4096); mul-mat: --n/--k/--batch (config 3 op shapes)."""
     import numpy as np
     import torch
 
@@ -321,7 +324,12 @@ def run_gemv(args, rank, local_rank):
         return
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    n, k = (3072, 1024) if args.workload == "gemv" else (32768, 4096)
+    if args.workload == "gemv":
+        n, k, m = 3072, 1024, 1
+    elif args.workload == "gemv-large":
+        n, k, m = 32768, 4096, 1
+    else:
+        n, k, m = args.n, args.k, args.batch
     rb = k // 32 * 34
     w_bytes = n * rb
     copies = max(2, int(2 * 126e6 // w_bytes) + 1)
@@ -331,20 +339,22 @@ def run_gemv(args, rank, local_rank):
         f = np.empty(n * k, np.float32)
         host.normal_many([c], [0.02], [f])
         ws.append(q8.quantize_rows(torch.from_numpy(f).to(dev).view(n, k)))
-    x_np = np.empty(k, np.float32)
+    x_np = np.empty(m * k, np.float32)
     host.normal_many([1], [1.0], [x_np])
-    x = torch.from_numpy(x_np).to(dev).view(1, k)
-    y = torch.empty((1, n), dtype=torch.float32, device=dev)
+    x_np = x_np.reshape(m, k)
+    x = torch.from_numpy(x_np).to(dev)
+    y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    wsp = torch.empty(max(1, q8.workspace_size(k, n, m)), dtype=torch.uint8, device=dev)
     calls_per_graph = copies * max(1, 64 // copies)
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
         for i in range(calls_per_graph):  # warm-up outside capture
-            q8.mul_mat(ws[i % copies], k, x, out=y)
+            q8.mul_mat(ws[i % copies], k, x, out=y, workspace=wsp)
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for i in range(calls_per_graph):
-            q8.mul_mat(ws[i % copies], k, x, out=y)
+            q8.mul_mat(ws[i % copies], k, x, out=y, workspace=wsp)
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize(dev)
@@ -368,53 +378,56 @@ def run_gemv(args, rank, local_rank):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
-    y0 = q8.mul_mat(ws[0], k, x).cpu().numpy().ravel()
-    y_ref, bound = O.mul_mat(ws[0].cpu().numpy(), k, x_np.reshape(1, k))
-    assert np.all(np.abs(y0 - y_ref.ravel()) <= 1e-5 * bound.ravel() + 1e-30)
+    y0 = q8.mul_mat(ws[0], k, x, workspace=wsp).cpu().numpy()
+    y_ref, bound = O.mul_mat(ws[0].cpu().numpy(), k, x_np)
+    assert np.all(np.abs(y0 - y_ref) <= 1e-5 * bound + 1e-30)
     # e2e: host x in, host y out around each call
-    x_host = torch.from_numpy(x_np).view(1, k).pin_memory()
-    y_host = torch.empty((1, n), dtype=torch.float32).pin_memory()
+    x_host = torch.from_numpy(x_np).pin_memory()
+    y_host = torch.empty((m, n), dtype=torch.float32).pin_memory()
     x_dev = torch.empty_like(x)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(cur)
     e2e_calls = min(calls, 2000)
     for i in range(e2e_calls):
         x_dev.copy_(x_host, non_blocking=True)
-        q8.mul_mat(ws[i % copies], k, x_dev, out=y)
+        q8.mul_mat(ws[i % copies], k, x_dev, out=y, workspace=wsp)
         y_host.copy_(y, non_blocking=True)
     f1.record(cur)
     torch.cuda.synchronize(dev)
     t_e2e = f0.elapsed_time(f1) / 1e3 / e2e_calls
-    bytes_call = w_bytes + 4 * k + 4 * n
+    bytes_call = w_bytes + 4 * k * m + 4 * n * m
+    ops_call = 2 * n * k * m
     peaks, peak_kind = measured_peaks()
     # CPU: the oracle port on a bounded sample, all host threads
     threads = host_threads()
     wq0 = ws[0].cpu().numpy()
-    O.mul_mat(wq0, k, x_np.reshape(1, k), threads=threads)
+    O.mul_mat(wq0, k, x_np, threads=threads)
     c0, cn = time.perf_counter(), 0
     while time.perf_counter() - c0 < 3.0:
-        O.mul_mat(wq0, k, x_np.reshape(1, k), threads=threads)
+        O.mul_mat(wq0, k, x_np, threads=threads)
         cn += 1
     cpu_t = (time.perf_counter() - c0) / cn
+    name = {"gemv": "BASELINE config 1 GEMV", "gemv-large": "large GEMV"}.get(args.workload, "MUL_MAT")
     line = {
-        "metric": "Q8_0 MUL_MAT HBM GB/s (decode GEMV, M=1)", "value": bytes_call / t_call / 1e9, "unit": "GB/s",
+        "metric": f"Q8_0 MUL_MAT HBM GB/s ({'decode GEMV, ' if m == 1 else ''}M={m})",
+        "value": bytes_call / t_call / 1e9, "unit": "GB/s",
         "n_gpus": 1, "steps": calls, "warmup": max(args.warmup, 3), "ms_per_step": 1e3 * t_call,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32, f32 scale",
         "data": "synthetic (seeded 0.02*N(0,1) weights packed on device, N(0,1) x)",
-        "config": {"workload": f"{'BASELINE config 1' if n == 3072 else 'large'} GEMV N={n} K={k} M=1, "
-                               f"{copies} rotating weight copies ({copies * w_bytes / 1e6:.0f} MB > L2), "
-                               f"CUDA graph of {calls_per_graph} calls",
+        "config": {"workload": f"{name} N={n} K={k} M={m}, {copies} rotating weight copies "
+                               f"({copies * w_bytes / 1e6:.0f} MB > L2), CUDA graph of {calls_per_graph} calls",
                    "l2": "weights rotated over copies totalling more than 2x L2"},
         "roofline": {"bound": "hbm", "achieved": bytes_call / t_call / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": bytes_call / t_call / 1e9 / peaks["hbm_gbs"], "traffic": None,
-                     "kernel": "gemv_q8_0_kernel<1, REF, plain>",
-                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
-        "e2e": {"value": bytes_call / t_e2e / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * k,
-                "d2h_bytes_per_step": 4 * n},
-        "gpu_launches": calls,
+                     "frac": bytes_call / t_call / 1e9 / peaks["hbm_gbs"], "traffic": ncu_traffic(args.workload),
+                     "kernel": "stage_rows_kernel + gemm_q8_0_kernel (int8 mma.sync, TMA tensor-map weight boxes)",
+                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                     "int8_tops": ops_call / t_call / 1e12},
+        "e2e": {"value": bytes_call / t_e2e / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * k * m,
+                "d2h_bytes_per_step": 4 * n * m},
+        "gpu_launches": 2 * calls,
         "clocks": clocks,
         "cpu_baseline": {"value": bytes_call / cpu_t / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{cn} calls on copy 0 (L3-resident on the host; oracle C port, OpenMP)"},
+                         "sample": f"{cn} calls on copy 0 (cache-resident on the host; oracle C port, OpenMP)"},
     }
     print(json.dumps(line), flush=True)
 
@@ -430,8 +443,8 @@ def main():
     if args.workload == "pack-1.7b":
         run_pack(args, rank, local_rank)
         return
-    if args.workload in ("gemv", "gemv-large"):
-        run_gemv(args, rank, local_rank)
+    if args.workload in ("gemv", "gemv-large", "mul-mat"):
+        run_mul_mat(args, rank, local_rank)
         return
 
     import torch

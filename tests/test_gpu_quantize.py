@@ -16,7 +16,7 @@ PACK = json.load(open(os.path.join(GOLDEN, "q8_pack_fixtures.json")))
 
 
 def to_dev(a, dev):
-    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return torch.from_numpy(np.array(a, copy=True, order="C")).to(dev)
 
 
 @pytest.mark.parametrize("name", sorted(PACK["cases"]))
