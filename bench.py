@@ -266,8 +266,10 @@ def run_pack(args, rank, local_rank):
     torch.cuda.synchronize(dev)
     t_dev = e0.elapsed_time(e1) / 1e3 / args.steps
     clocks = sampler.stop()
-    # e2e: the quantize tool's own call, host F32 in, host Q8_0 out
+    # e2e: the quantize tool's own call, host F32 in, host Q8_0 out (its staging
+    # is created by a first small call, as a quantize run's first tensor would)
     dst_host = [np.empty(n * (k // 32 * 34), np.uint8) for n, k in mats]
+    q8.quantize_chunk_host(f32[0], dst_host[0], 0, 1, mats[0][1], device=local_rank)
     t0 = time.perf_counter()
     for a, d, (n, k) in zip(f32, dst_host, mats):
         q8.quantize_chunk_host(a, d, 0, n, k, device=local_rank)

@@ -103,12 +103,18 @@ b200q8_status_t b200q8_quantize_chunk(const float * src, void * dst, int64_t sta
 /* ggml_quantize_chunk(GGML_TYPE_Q8_0, src, dst, start, nrows, n_per_row, NULL)
  * on HOST buffers -- the call tools/synthesize-quantize/quantize.cpp:300-301
  * makes, with its arguments' meaning.  Rows stream through `device` in
- * chunks; bytes identical to quantize_row_q8_0_ref.  Blocking.  Unlike the
- * compute entry points it allocates (device staging, freed before it
- * returns) and page-locks the caller's buffers for the duration when the
- * driver allows: a tool call, not a hot-path one. */
+ * chunks (pinned host staging -> device -> pinned staging, two chunks in
+ * flight); bytes identical to quantize_row_q8_0_ref.  Blocking; calls on one
+ * device are serialised.  Unlike the compute entry points it allocates: the
+ * first call on a device creates about 170 MB of pinned and device staging
+ * that later calls reuse, until b200q8_quantize_chunk_host_release().  A tool
+ * call, not a hot-path one. */
 b200q8_status_t b200q8_quantize_chunk_host(const float * src, void * dst, int64_t start, int64_t nrows,
                                            int64_t n_per_row, size_t * written, int32_t device);
+
+/* Frees the staging b200q8_quantize_chunk_host keeps (every device).  No
+ * reference counterpart: ggml_quantize_chunk has no state to release. */
+void b200q8_quantize_chunk_host_release(void);
 
 /* Q8_0 rows -> F32 rows: out = q * fp32(d) (exact). */
 b200q8_status_t b200q8_dequantize_rows(const void * src, int64_t rows, int64_t K, size_t src_row_stride, float * dst,

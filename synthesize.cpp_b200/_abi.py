@@ -74,6 +74,8 @@ def lib() -> ctypes.CDLL:
     L.b200q8_quantize_chunk.restype = i32
     L.b200q8_quantize_chunk_host.argtypes = [vp, vp, i64, i64, i64, ctypes.POINTER(sz), i32]
     L.b200q8_quantize_chunk_host.restype = i32
+    L.b200q8_quantize_chunk_host_release.argtypes = []
+    L.b200q8_quantize_chunk_host_release.restype = None
     L.b200q8_dequantize_rows.argtypes = [vp, i64, i64, sz, vp, sz, vp]
     L.b200q8_dequantize_rows.restype = i32
     L.b200q8_get_rows.argtypes = [vp, i64, i64, sz, vp, i64, vp, sz, vp]

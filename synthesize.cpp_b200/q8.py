@@ -30,7 +30,7 @@ QK = 32
 BLOCK_BYTES = 34
 
 __all__ = ["QK", "BLOCK_BYTES", "QUANT_REF", "QUANT_CPU_X86", "QUANT_CPU_ARM", "B200Q8Error", "row_bytes",
-           "quantize_rows", "quantize_chunk", "quantize_chunk_host", "dequantize_rows", "get_rows", "mul_mat", "workspace_size",
+           "quantize_rows", "quantize_chunk", "quantize_chunk_host", "quantize_chunk_host_release", "dequantize_rows", "get_rows", "mul_mat", "workspace_size",
            "device_status", "stream_ptr"]
 
 
@@ -86,6 +86,11 @@ def quantize_chunk_host(src, dst, start: int, nrows: int, n_per_row: int, device
     written = ctypes.c_size_t(0)
     check(lib().b200q8_quantize_chunk_host(ptr(src), ptr(dst), start, nrows, n_per_row, ctypes.byref(written), device))
     return int(written.value)
+
+
+def quantize_chunk_host_release() -> None:
+    """Frees the pinned and device staging quantize_chunk_host keeps between calls."""
+    lib().b200q8_quantize_chunk_host_release()
 
 
 def dequantize_rows(q: torch.Tensor, k: int, out: torch.Tensor | None = None) -> torch.Tensor:

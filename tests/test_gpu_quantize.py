@@ -111,7 +111,7 @@ def test_bad_arguments_raise(q8, dev):
 
 def test_quantize_chunk_host_matches_oracle(q8, O):
     # the quantize tool's call on host buffers: start offset, several chunks, bytes as the reference
-    rows, k = 1200, 3072  # 14.7 MB of F32 -> several 128 MB-bounded chunks? one; exercise start too
+    rows, k = 1200, 3072  # 14.7 MB of F32, one chunk; a start offset into src and dst
     src = O.normal(91, rows * k, 0.05)
     dst = np.zeros(rows * (k // 32 * 34), np.uint8)
     n = q8.quantize_chunk_host(src, dst, 200 * k, 1000, k)
@@ -120,8 +120,24 @@ def test_quantize_chunk_host_matches_oracle(q8, O):
     assert np.array_equal(dst, ref)
 
 
+def test_quantize_chunk_host_shapes_and_release(q8, O):
+    # staging is kept between calls and must serve any row width; a row wider
+    # than the default staging grows it; release frees it and the next call re-creates it
+    for rows, k in [(7, 32), (300, 1024), (2, 9 * 1024 * 1024), (513, 6144)]:
+        src = O.normal(rows + k, rows * k, 0.3)
+        dst = np.zeros(rows * (k // 32 * 34), np.uint8)
+        assert q8.quantize_chunk_host(src, dst, 0, rows, k) == dst.size
+        ref, _ = O.quantize_chunk(src, 0, rows, k)
+        assert np.array_equal(dst, ref), (rows, k)
+    q8.quantize_chunk_host_release()
+    src = O.normal(5, 64 * 2048, 1.0)
+    dst = np.zeros(64 * (2048 // 32 * 34), np.uint8)
+    q8.quantize_chunk_host(src, dst, 0, 64, 2048)
+    assert np.array_equal(dst, O.quantize_chunk(src, 0, 64, 2048)[0])
+
+
 def test_quantize_chunk_host_many_chunks(q8, O):
-    rows, k = 12000, 4096  # 196 MB of F32: two 128 MB chunks through both streams
+    rows, k = 12000, 4096  # 196 MB of F32: seven 32 MB chunks through both staging buffers
     src = np.asarray(np.random.default_rng(3).standard_normal(rows * k), np.float32)
     dst = np.zeros(rows * (k // 32 * 34), np.uint8)
     assert q8.quantize_chunk_host(src, dst, 0, rows, k) == dst.size
