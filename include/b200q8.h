@@ -116,6 +116,26 @@ b200q8_status_t b200q8_quantize_chunk_host(const float * src, void * dst, int64_
  * reference counterpart: ggml_quantize_chunk has no state to release. */
 void b200q8_quantize_chunk_host_release(void);
 
+/* Source element types for the typed packing calls (ggml type ids). */
+#define B200Q8_SRC_F32  0
+#define B200Q8_SRC_F16  1
+#define B200Q8_SRC_BF16 30
+
+/* b200q8_quantize_rows for F32, F16 or BF16 source rows.  A 16-bit value is
+ * widened to fp32 exactly, as the quantize tool's dequantize_to_f32
+ * (tools/synthesize-quantize/quantize.cpp:67-83) does before
+ * ggml_quantize_chunk, so the Q8_0 bytes equal those of the F32 path on the
+ * widened values.  x_row_stride in bytes (a multiple of the element size). */
+b200q8_status_t b200q8_quantize_rows_typed(const void * x, int32_t src_type, int64_t rows, int64_t K,
+                                           size_t x_row_stride, void * dst, size_t dst_row_stride, int32_t mode,
+                                           b200q8_stream_t stream);
+
+/* b200q8_quantize_chunk_host for an F32, F16 or BF16 host source: replaces
+ * the tool's dequantize_to_f32 + ggml_quantize_chunk pair
+ * (quantize.cpp:297-301) for Q8_0 targets; start counts elements. */
+b200q8_status_t b200q8_quantize_chunk_host_typed(const void * src, int32_t src_type, void * dst, int64_t start,
+                                                 int64_t nrows, int64_t n_per_row, size_t * written, int32_t device);
+
 /* Q8_0 rows -> F32 rows: out = q * fp32(d) (exact). */
 b200q8_status_t b200q8_dequantize_rows(const void * src, int64_t rows, int64_t K, size_t src_row_stride, float * dst,
                                        size_t dst_row_stride, b200q8_stream_t stream);

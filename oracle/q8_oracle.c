@@ -95,15 +95,18 @@ float oracle_fp16_to_fp32(uint16_t h) {
 
 /* ------------------------------------------------------------ quantize ---- */
 
-/* Converts a rounded code to int8.  Finite codes lie in [-127, 127].  The
- * reference stores roundf(x*id) straight into an int8_t, which is undefined
- * for a non-finite value; gcc on x86 emits cvttss2si (0x80000000) and keeps
- * the low byte, i.e. 0.  This restatement fixes that outcome: non-finite -> 0. */
+/* Converts a rounded code to int8.  Codes normally lie in [-127, 127], but
+ * ggml's amax fold skips every value before the block's last NaN, so x*id can
+ * be any float.  The reference stores roundf(x*id) straight into an int8_t,
+ * undefined in C outside int32 and for non-finite values; gcc on x86 emits
+ * cvttss2si, which gives 0x80000000 for NaN, infinities and anything outside
+ * [-2^31, 2^31), and keeps the low byte: 0.  Inside int32 the low byte of the
+ * integer is kept.  This restatement fixes those outcomes explicitly. */
 static int8_t code_from_float(float r) {
-    if (!isfinite(r)) {
+    if (!(r >= -2147483648.0f && r < 2147483648.0f)) {
         return 0;
     }
-    return (int8_t) (int) r;
+    return (int8_t) (uint8_t) ((uint32_t) (int32_t) r & 0xffu);
 }
 
 void oracle_quantize_row_q8_0(const float * x, void * vy, int64_t k, int mode) {

@@ -74,6 +74,10 @@ def lib() -> ctypes.CDLL:
     L.b200q8_quantize_chunk.restype = i32
     L.b200q8_quantize_chunk_host.argtypes = [vp, vp, i64, i64, i64, ctypes.POINTER(sz), i32]
     L.b200q8_quantize_chunk_host.restype = i32
+    L.b200q8_quantize_rows_typed.argtypes = [vp, i32, i64, i64, sz, vp, sz, i32, vp]
+    L.b200q8_quantize_rows_typed.restype = i32
+    L.b200q8_quantize_chunk_host_typed.argtypes = [vp, i32, vp, i64, i64, i64, ctypes.POINTER(sz), i32]
+    L.b200q8_quantize_chunk_host_typed.restype = i32
     L.b200q8_quantize_chunk_host_release.argtypes = []
     L.b200q8_quantize_chunk_host_release.restype = None
     L.b200q8_dequantize_rows.argtypes = [vp, i64, i64, sz, vp, sz, vp]

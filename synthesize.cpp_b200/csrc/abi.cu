@@ -145,6 +145,34 @@ b200q8_status_t b200q8_quantize_rows(const float * x, int64_t rows, int64_t K, s
     return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "quantize_rows launch");
 }
 
+b200q8_status_t b200q8_quantize_rows_typed(const void * x, int32_t src_type, int64_t rows, int64_t K,
+                                           size_t x_row_stride, void * dst, size_t dst_row_stride, int32_t mode,
+                                           b200q8_stream_t stream) {
+    const size_t es = src_type == B200Q8_SRC_F32 ? 4 : (src_type == B200Q8_SRC_F16 || src_type == B200Q8_SRC_BF16) ? 2 : 0;
+    if (es == 0) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "quantize_rows_typed: unknown source type %d", src_type);
+    }
+    if (rows < 0 || K < 0 || K % kQK != 0) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "quantize_rows_typed: K (%lld) must be a non-negative multiple of 32",
+                         (long long) K);
+    }
+    if (!valid_mode(mode)) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "quantize_rows_typed: unknown mode %d", mode);
+    }
+    if (rows == 0 || K == 0) {
+        return B200Q8_OK;
+    }
+    const size_t nb = (size_t) K / kQK;
+    if (x == nullptr || dst == nullptr || !aligned(x, es) || x_row_stride % es != 0 ||
+        (rows > 1 && (x_row_stride < (size_t) K * es || dst_row_stride < nb * kBlockBytes))) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "quantize_rows_typed: bad pointer, alignment or stride");
+    }
+    cudaError_t e = launch_quantize_typed(x, src_type, rows, K, rows > 1 ? x_row_stride : (size_t) K * es, dst,
+                                          rows > 1 ? dst_row_stride : nb * kBlockBytes, mode,
+                                          reinterpret_cast<cudaStream_t>(stream), current_sm_count());
+    return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "quantize_rows_typed launch");
+}
+
 b200q8_status_t b200q8_quantize_chunk(const float * src, void * dst, int64_t start, int64_t nrows,
                                       int64_t n_per_row, size_t * written, b200q8_stream_t stream) {
     if (n_per_row <= 0 || n_per_row % kQK != 0 || start < 0 || nrows < 0 || start % n_per_row != 0) {

@@ -138,12 +138,15 @@ __device__ __forceinline__ QuantParams quant_params(float amax) {
 }
 
 // One code: x*id rounded (half away from zero for REF, half to even for the
-// SIMD forms); a non-finite product stores 0, as the reference does on x86.
+// SIMD forms), stored as the low byte of its int32 conversion.  ggml's amax
+// fold skips every value before a block's last NaN, so x*id can be any float:
+// NaN, infinities and values outside [-2^31, 2^31) store 0, which is what the
+// reference's float -> int8_t store gives on x86 (cvttss2si's 0x80000000).
 template <int MODE>
 __device__ __forceinline__ int quant_code(float x, float id) {
     const float x0 = __fmul_rn(x, id);
     const float r  = (MODE == B200Q8_QUANT_REF) ? roundf(x0) : rintf(x0);
-    return isfinite(r) ? static_cast<int>(r) : 0;
+    return (r >= -2147483648.0f && r < 2147483648.0f) ? static_cast<int>(r) : 0;
 }
 
 // silu as ggml's scalar form writes it: x / (1 + expf(-x)).  expf is CUDA's

@@ -42,6 +42,7 @@ constexpr int   kChunkBlocks       = 8;                           // Q8_0 blocks
 constexpr int   kChunkRowBytes     = kChunkBlocks * kBlockBytes;  // 272: one weight row of a chunk
 constexpr int   kRecTokenBytes     = kChunkBlocks * kQK + kChunkBlocks * 4;  // 288: codes + scales
 constexpr int   kMaxTokenChunk     = 64;
+constexpr int   kGemmMaxM          = 65536;  // tokens per call (chunks of <= 64)
 
 // 2-D tiled TMA load of the box at (x, y) of `map` into this CTA's shared
 // memory (128-byte aligned), completing on `bar`.  x counts 2-byte elements
@@ -682,7 +683,7 @@ size_t gemm_workspace_bytes(int64_t K, int64_t M) {
 
 bool gemm_supported(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, int64_t M) {
     // K % 256: whole 272-byte chunks, 16-byte aligned in every row
-    if (M < 1 || M > 1024 || N < 16 || N > (int64_t) 1 << 30 || K < 256 || K % 256 != 0 || K > 8192 ||
+    if (M < 1 || M > kGemmMaxM || N < 16 || N > (int64_t) 1 << 30 || K < 256 || K % 256 != 0 || K > 8192 ||
         row_bytes % 16 != 0 || row_bytes < (size_t) (K / kQK) * kBlockBytes ||
         (reinterpret_cast<uintptr_t>(w) % 16) != 0) {
         return false;

@@ -10,6 +10,13 @@ namespace b200q8 {
 cudaError_t launch_quantize(const float * x, int64_t rows, int64_t K, size_t x_stride, void * dst, size_t dst_stride,
                             int mode, cudaStream_t stream, int sm_count);
 
+// Source element types of the packing kernels (ggml type ids).
+enum SrcType : int { kSrcF32 = 0, kSrcF16 = 1, kSrcBF16 = 30 };
+
+// F32 / F16 / BF16 rows -> Q8_0 rows (16-bit sources widened exactly first).
+cudaError_t launch_quantize_typed(const void * x, int src_type, int64_t rows, int64_t K, size_t x_stride, void * dst,
+                                  size_t dst_stride, int mode, cudaStream_t stream, int sm_count);
+
 cudaError_t launch_dequant_rows(const void * src, size_t src_stride, int64_t src_rows, const int32_t * ids,
                                 int64_t n_out, int64_t K, float * out, size_t out_stride, cudaStream_t stream,
                                 int sm_count);

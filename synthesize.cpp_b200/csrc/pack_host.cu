@@ -69,15 +69,15 @@ void free_staging(Staging & s) {
 }
 
 // Staging that holds at least one row of this width (the current device).
-// Q8_0 output is 34/128 of the F32 input for every K, so one output size
-// serves every shape.
+// Q8_0 output is 34/64 of a 16-bit input (34/128 of an F32 one) for every K,
+// so one output size serves every shape and source type.
 cudaError_t ensure_staging(Staging & s, size_t row_in) {
     if (s.cap_in >= row_in) {
         return cudaSuccess;
     }
     free_staging(s);
     const size_t cap_in  = std::max(kChunkInBytes, row_in);
-    const size_t cap_out = (cap_in * kBlockBytes + 4 * kQK - 1) / (4 * kQK);
+    const size_t cap_out = (cap_in * kBlockBytes + 2 * kQK - 1) / (2 * kQK);
     cudaError_t  e       = cudaSuccess;
     for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
         e = cudaHostAlloc(reinterpret_cast<void **>(&s.pin_in[i]), cap_in, cudaHostAllocDefault);
@@ -118,10 +118,8 @@ void parallel_copy(void * dst, const void * src, size_t bytes) {
     }
 }
 
-}  // namespace
-
-extern "C" b200q8_status_t b200q8_quantize_chunk_host(const float * src, void * dst, int64_t start, int64_t nrows,
-                                                      int64_t n_per_row, size_t * written, int32_t device) {
+b200q8_status_t pack_host(const void * src, int src_type, size_t es, void * dst, int64_t start, int64_t nrows,
+                          int64_t n_per_row, size_t * written, int32_t device) {
     if (n_per_row <= 0 || n_per_row % kQK != 0 || start < 0 || nrows < 0 || start % n_per_row != 0 ||
         (nrows > 0 && (src == nullptr || dst == nullptr))) {
         return set_error(B200Q8_ERR_INVALID_ARG,
@@ -130,7 +128,7 @@ extern "C" b200q8_status_t b200q8_quantize_chunk_host(const float * src, void * 
     if (device < 0 || device >= kMaxDevices) {
         return set_error(B200Q8_ERR_INVALID_ARG, "quantize_chunk_host: device %d out of range", device);
     }
-    const size_t  row_in    = (size_t) n_per_row * sizeof(float);
+    const size_t  row_in    = (size_t) n_per_row * es;
     const size_t  row_out   = (size_t) (n_per_row / kQK) * kBlockBytes;
     const int64_t start_row = start / n_per_row;
     if (written != nullptr) {
@@ -152,7 +150,7 @@ extern "C" b200q8_status_t b200q8_quantize_chunk_host(const float * src, void * 
         cudaSetDevice(prev);
         return cuda_error(e, "quantize_chunk_host: staging allocation");
     }
-    const float *  s_rows     = src + start;
+    const uint8_t * s_rows    = static_cast<const uint8_t *>(src) + (size_t) start * es;
     uint8_t *      d_rows     = static_cast<uint8_t *>(dst) + (size_t) start_row * row_out;
     const int64_t  chunk_rows = (int64_t) (s.cap_in / row_in);
     const int64_t  n_chunks   = (nrows + chunk_rows - 1) / chunk_rows;
@@ -176,11 +174,11 @@ extern "C" b200q8_status_t b200q8_quantize_chunk_host(const float * src, void * 
                 break;
             }
         }
-        parallel_copy(s.pin_in[i], s_rows + (size_t) (k * chunk_rows) * n_per_row, (size_t) rows * row_in);
+        parallel_copy(s.pin_in[i], s_rows + (size_t) (k * chunk_rows) * row_in, (size_t) rows * row_in);
         e = cudaMemcpyAsync(s.dev_in[i], s.pin_in[i], (size_t) rows * row_in, cudaMemcpyHostToDevice, s.st[i]);
         if (e == cudaSuccess) {
-            e = launch_quantize(s.dev_in[i], rows, n_per_row, row_in, s.dev_out[i], row_out, B200Q8_QUANT_REF, s.st[i],
-                                sms);
+            e = launch_quantize_typed(s.dev_in[i], src_type, rows, n_per_row, row_in, s.dev_out[i], row_out,
+                                      B200Q8_QUANT_REF, s.st[i], sms);
         }
         if (e == cudaSuccess) {
             e = cudaMemcpyAsync(s.pin_out[i], s.dev_out[i], (size_t) rows * row_out, cudaMemcpyDeviceToHost, s.st[i]);
@@ -199,6 +197,23 @@ extern "C" b200q8_status_t b200q8_quantize_chunk_host(const float * src, void * 
     }
     cudaSetDevice(prev);
     return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "quantize_chunk_host");
+}
+
+}  // namespace
+
+extern "C" b200q8_status_t b200q8_quantize_chunk_host(const float * src, void * dst, int64_t start, int64_t nrows,
+                                                      int64_t n_per_row, size_t * written, int32_t device) {
+    return pack_host(src, kSrcF32, 4, dst, start, nrows, n_per_row, written, device);
+}
+
+extern "C" b200q8_status_t b200q8_quantize_chunk_host_typed(const void * src, int32_t src_type, void * dst,
+                                                            int64_t start, int64_t nrows, int64_t n_per_row,
+                                                            size_t * written, int32_t device) {
+    const size_t es = src_type == B200Q8_SRC_F32 ? 4 : (src_type == B200Q8_SRC_F16 || src_type == B200Q8_SRC_BF16) ? 2 : 0;
+    if (es == 0) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "quantize_chunk_host_typed: unknown source type %d", src_type);
+    }
+    return pack_host(src, src_type, es, dst, start, nrows, n_per_row, written, device);
 }
 
 extern "C" void b200q8_quantize_chunk_host_release(void) {

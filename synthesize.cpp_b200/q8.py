@@ -30,7 +30,7 @@ QK = 32
 BLOCK_BYTES = 34
 
 __all__ = ["QK", "BLOCK_BYTES", "QUANT_REF", "QUANT_CPU_X86", "QUANT_CPU_ARM", "B200Q8Error", "row_bytes",
-           "quantize_rows", "quantize_chunk", "quantize_chunk_host", "quantize_chunk_host_release", "dequantize_rows", "get_rows", "mul_mat", "workspace_size",
+           "quantize_rows", "quantize_chunk", "quantize_chunk_host", "quantize_chunk_host_typed", "quantize_chunk_host_release", "dequantize_rows", "get_rows", "mul_mat", "workspace_size",
            "device_status", "stream_ptr"]
 
 
@@ -53,17 +53,24 @@ def _row_stride_bytes(t: torch.Tensor) -> int:
     return (t.stride(0) if t.dim() > 1 else t.shape[-1]) * t.element_size()
 
 
+SRC_TYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 30}  # ggml type ids
+
+
 def quantize_rows(x: torch.Tensor, mode: int = QUANT_REF, out: torch.Tensor | None = None) -> torch.Tensor:
-    """F32 [rows, K] -> Q8_0 uint8 [rows, K/32*34]."""
+    """F32 / F16 / BF16 [rows, K] -> Q8_0 uint8 [rows, K/32*34] (16-bit values widened to fp32 exactly)."""
     _need_cuda(x)
-    if x.dtype != torch.float32 or x.stride(-1) != 1:
-        raise ValueError("quantize_rows: x must be float32 with unit inner stride")
+    if x.dtype not in SRC_TYPES or x.stride(-1) != 1:
+        raise ValueError("quantize_rows: x must be float32, float16 or bfloat16 with unit inner stride")
     x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
     rows, k = x2.shape
     if out is None:
         out = torch.empty((rows, row_bytes(k)), dtype=torch.uint8, device=x.device)
-    check(lib().b200q8_quantize_rows(x2.data_ptr(), rows, k, _row_stride_bytes(x2), out.data_ptr(),
-                                     _row_stride_bytes(out), mode, stream_ptr()))
+    if x.dtype == torch.float32:
+        check(lib().b200q8_quantize_rows(x2.data_ptr(), rows, k, _row_stride_bytes(x2), out.data_ptr(),
+                                         _row_stride_bytes(out), mode, stream_ptr()))
+    else:
+        check(lib().b200q8_quantize_rows_typed(x2.data_ptr(), SRC_TYPES[x.dtype], rows, k, _row_stride_bytes(x2),
+                                               out.data_ptr(), _row_stride_bytes(out), mode, stream_ptr()))
     return out
 
 
@@ -85,6 +92,23 @@ def quantize_chunk_host(src, dst, start: int, nrows: int, n_per_row: int, device
 
     written = ctypes.c_size_t(0)
     check(lib().b200q8_quantize_chunk_host(ptr(src), ptr(dst), start, nrows, n_per_row, ctypes.byref(written), device))
+    return int(written.value)
+
+
+def quantize_chunk_host_typed(src, dst, start: int, nrows: int, n_per_row: int, device: int = 0) -> int:
+    """quantize_chunk_host for an F32 / F16 / BF16 host source (numpy float32/float16 array, or a CPU torch
+    tensor of float32/float16/bfloat16); returns bytes written."""
+    import numpy as np
+
+    if isinstance(src, np.ndarray):
+        st = {np.dtype(np.float32): 0, np.dtype(np.float16): 1}[src.dtype]
+        sp = src.ctypes.data
+    else:
+        st = SRC_TYPES[src.dtype]
+        sp = src.data_ptr()
+    dp = dst.ctypes.data if isinstance(dst, np.ndarray) else dst.data_ptr()
+    written = ctypes.c_size_t(0)
+    check(lib().b200q8_quantize_chunk_host_typed(sp, st, dp, start, nrows, n_per_row, ctypes.byref(written), device))
     return int(written.value)
 
 

@@ -105,7 +105,7 @@ def test_tensor_core_gemm(q8, O, dev, n, k, m):
 
 
 @pytest.mark.parametrize("n,k,m", [(1024, 1024, 72), (1000, 2048, 130), (3072, 1024, 1024), (256, 8192, 24),
-                                   (48, 512, 9)])
+                                   (48, 512, 9), (512, 1024, 4100)])
 def test_tensor_core_gemm_token_chunks(q8, O, dev, n, k, m):
     # M > 64 splits tokens into chunks of <= 64 (72 -> 2 x 40, 130 -> 3 x 48); K up to 8192
     wq_np = O.quantize_rows(O.normal(n + 7 * k, n * k, 0.02).reshape(n, k))

@@ -143,3 +143,79 @@ def test_quantize_chunk_host_many_chunks(q8, O):
     assert q8.quantize_chunk_host(src, dst, 0, rows, k) == dst.size
     ref, _ = O.quantize_chunk(src, 0, rows, k)
     assert np.array_equal(dst, ref)
+
+
+def _bf16_bits_to_f32(bits):
+    return (np.asarray(bits, np.uint32) << 16).view(np.float32)
+
+
+def _special16(rng, n, dtype):
+    """Random 16-bit values with every class present: normals over a wide range, subnormals, zeros of both
+    signs, infinities and NaNs."""
+    if dtype == "f16":
+        v = (rng.standard_normal(n) * np.exp(rng.uniform(-12, 10, n))).astype(np.float16)
+        bits = v.view(np.uint16).copy()
+        sub = rng.integers(1, 0x400, n // 50, dtype=np.uint16)
+        specials = np.array([0x0000, 0x8000, 0x7C00, 0xFC00, 0x7E00, 0x3C00, 0xBC00], np.uint16)
+    else:
+        v = (rng.standard_normal(n) * np.exp(rng.uniform(-60, 60, n))).astype(np.float32)
+        bits = (v.view(np.uint32) >> 16).astype(np.uint16)
+        sub = rng.integers(1, 0x80, n // 50, dtype=np.uint16)
+        specials = np.array([0x0000, 0x8000, 0x7F80, 0xFF80, 0x7FC0, 0x3F80, 0xBF80], np.uint16)
+    pos = rng.choice(n, sub.size + specials.size * 3, replace=False)
+    bits[pos[:sub.size]] = sub
+    bits[pos[sub.size:]] = np.tile(specials, 3)
+    return bits
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_quantize_rows_16bit_sources(q8, O, dev, dtype, mode):
+    # F16 / BF16 rows are widened exactly and quantized like F32 (the quantize tool's dequantize_to_f32 path)
+    rng = np.random.default_rng(17 + mode)
+    rows, k = 96, 1024 + 512  # dense path with a ragged 8-block tail per row
+    bits = _special16(rng, rows * k, dtype)
+    f32 = bits.view(np.float16).astype(np.float32) if dtype == "f16" else _bf16_bits_to_f32(bits)
+    t = torch.from_numpy(bits.view(np.int16).copy()).to(dev)
+    x = t.view(torch.float16 if dtype == "f16" else torch.bfloat16).view(rows, k)
+    got = q8.quantize_rows(x, mode=mode).cpu().numpy()
+    ref = O.quantize_rows(f32.reshape(rows, k), mode=mode)
+    assert np.array_equal(got, ref)
+    # strided rows (general per-block path)
+    xs = torch.zeros((rows, k + 64), dtype=x.dtype, device=dev)
+    xs[:, :k] = x
+    got2 = q8.quantize_rows(xs[:, :k], mode=mode).cpu().numpy()
+    assert np.array_equal(got2, ref)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_quantize_chunk_host_16bit_sources(q8, O, dtype):
+    rng = np.random.default_rng(5)
+    rows, k = 3000, 2048  # 12 MB of 16-bit source
+    bits = _special16(rng, rows * k, dtype)
+    f32 = bits.view(np.float16).astype(np.float32) if dtype == "f16" else _bf16_bits_to_f32(bits)
+    src = bits.view(np.float16) if dtype == "f16" else torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)
+    dst = np.zeros(rows * (k // 32 * 34), np.uint8)
+    n = q8.quantize_chunk_host_typed(src, dst, 100 * k, rows - 100, k)
+    ref, nref = O.quantize_chunk(f32, 100 * k, rows - 100, k)
+    assert n == nref
+    assert np.array_equal(dst[100 * (k // 32 * 34):], ref[100 * (k // 32 * 34):])
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_nan_fold_out_of_range_codes(q8, O, dev, mode):
+    # ggml's amax fold skips every value before a block's last NaN, so x*id can leave int8 (low byte of the
+    # int32 kept) and even int32 (stored as 0, x86's cvttss2si result); GPU and oracle agree on both
+    rng = np.random.default_rng(23 + mode)
+    x = rng.uniform(-1, 1, (64, 32)).astype(np.float32)
+    x[:, 0] = rng.uniform(-9e3, 9e3, 64)          # int32 range after scaling: low byte kept
+    x[:, 1] = rng.uniform(-8e4, 8e4, 64)
+    x[:, 2] = np.float32(3e12) * np.sign(rng.uniform(-1, 1, 64))  # beyond int32: 0
+    x[::2, 3] = np.nan
+    x[1::2, 7] = np.nan
+    x = x.reshape(2, 1024)
+    got = q8.quantize_rows(torch.from_numpy(x).to(dev), mode=mode).cpu().numpy()
+    ref = O.quantize_rows(x, mode=mode)
+    assert np.array_equal(got, ref)
+    codes = ref.reshape(-1, 34)[:, 2:].view(np.int8)
+    assert np.all(codes[::2, 2] == 0)
