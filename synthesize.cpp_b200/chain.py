@@ -38,6 +38,19 @@ class DecodeChain:
         self.n_layers = len(layers)
         self.device = table.device
 
+    @classmethod
+    def from_handle(cls, handle: ctypes.c_void_p, *, hidden: int, n_layers: int, device: torch.device,
+                    keep=None) -> "DecodeChain":
+        """Wraps a chain the library already built (b200q8_gguf_talker_chain)."""
+        self = cls.__new__(cls)
+        self._keep = keep
+        self._arr = None
+        self._h = handle
+        self.hidden = hidden
+        self.n_layers = n_layers
+        self.device = device
+        return self
+
     def run(self, ids: torch.Tensor, x_in: torch.Tensor, h_out: torch.Tensor) -> torch.Tensor:
         m = ids.numel()
         check(lib().b200q8_chain_run(self._h, ids.data_ptr(), x_in.data_ptr(), h_out.data_ptr(), m, stream_ptr()))

@@ -1,0 +1,460 @@
+// gguf.cu -- GGUF package reader and the talker step built from a package
+// (include/b200q8_gguf.h).  Host code only.
+//
+// Format (GGUF v2/v3, little-endian): "GGUF", u32 version, u64 tensor count,
+// u64 metadata count; metadata entries {string key, u32 type, value}; tensor
+// infos {string name, u32 n_dims, u64 ne[n_dims], u32 type, u64 offset}; the
+// data section starts at the next multiple of general.alignment (32 when
+// absent).  A string is {u64 length, bytes}.  The reference reads packages
+// through ggml's gguf reader (src/gguf-metadata.cpp:12-46); this is a
+// separate reader with every read bounds-checked against the mapped file.
+#include "../../include/b200q8_gguf.h"
+
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace b200q8 {
+b200q8_status_t set_error(b200q8_status_t code, const char * fmt, ...);
+b200q8_status_t cuda_error(cudaError_t e, const char * what);
+}  // namespace b200q8
+
+using namespace b200q8;
+
+namespace {
+
+enum GgufValueType : uint32_t {
+    kU8 = 0, kI8 = 1, kU16 = 2, kI16 = 3, kU32 = 4, kI32 = 5, kF32 = 6, kBool = 7, kStr = 8, kArr = 9, kU64 = 10,
+    kI64 = 11, kF64 = 12,
+};
+
+size_t scalar_size(uint32_t t) {
+    switch (t) {
+        case kU8: case kI8: case kBool: return 1;
+        case kU16: case kI16: return 2;
+        case kU32: case kI32: case kF32: return 4;
+        case kU64: case kI64: case kF64: return 8;
+        default: return 0;
+    }
+}
+
+// Bytes of a tensor of this ggml type and element count; 0 when unknown.
+uint64_t tensor_bytes(int32_t type, uint64_t n) {
+    switch (type) {
+        case 0: return n * 4;                                  // F32
+        case 1: case 30: return n * 2;                         // F16, BF16
+        case 8: return n % 32 ? 0 : n / 32 * kBlockBytes;      // Q8_0
+        case 24: return n;                                     // I8
+        case 25: return n * 2;                                 // I16
+        case 26: return n * 4;                                 // I32
+        case 27: case 28: return n * 8;                        // I64, F64
+        default: return 0;
+    }
+}
+
+struct Reader {
+    const uint8_t * p;
+    size_t          size;
+    size_t          pos = 0;
+    bool            ok  = true;
+    bool need(size_t n) {
+        if (!ok || n > size - pos) {
+            ok = false;
+        }
+        return ok;
+    }
+    template <typename T>
+    T get() {
+        T v{};
+        if (need(sizeof(T))) {
+            memcpy(&v, p + pos, sizeof(T));
+            pos += sizeof(T);
+        }
+        return v;
+    }
+    std::string str() {
+        const uint64_t n = get<uint64_t>();
+        if (!ok || !need(n)) {
+            ok = false;
+            return std::string();
+        }
+        std::string s(reinterpret_cast<const char *>(p + pos), n);
+        pos += n;
+        return s;
+    }
+    // skips one value of type t (arrays of any depth, strings)
+    void skip(uint32_t t, int depth = 0) {
+        if (t == kStr) {
+            str();
+        } else if (t == kArr) {
+            const uint32_t et = get<uint32_t>();
+            const uint64_t n  = get<uint64_t>();
+            if (!ok || depth > 4) {
+                ok = false;
+                return;
+            }
+            const size_t es = scalar_size(et);
+            if (es != 0) {
+                if (n > (size - pos) / es) {
+                    ok = false;
+                    return;
+                }
+                pos += n * es;
+            } else {
+                for (uint64_t i = 0; i < n && ok; ++i) {
+                    skip(et, depth + 1);
+                }
+            }
+        } else {
+            const size_t es = scalar_size(t);
+            if (es == 0) {
+                ok = false;
+            } else if (need(es)) {
+                pos += es;
+            }
+        }
+    }
+};
+
+struct Kv {
+    std::string key;
+    uint32_t    type;
+    size_t      value_pos;  // file offset of the value
+};
+
+struct Tensor {
+    std::string name;
+    int32_t     type;
+    int32_t     n_dims;
+    int64_t     ne[4];
+    uint64_t    offset;
+    uint64_t    nbytes;
+};
+
+}  // namespace
+
+struct b200q8_gguf {
+    int                 fd   = -1;
+    const uint8_t *     map  = nullptr;
+    size_t              size = 0;
+    uint32_t            version = 0;
+    std::vector<Kv>     kv;
+    std::vector<Tensor> tensors;
+    size_t              data_start = 0;
+
+    const Kv * find_kv(const char * key) const {
+        for (const Kv & e : kv) {
+            if (e.key == key) {
+                return &e;
+            }
+        }
+        return nullptr;
+    }
+};
+
+extern "C" {
+
+void b200q8_gguf_close(b200q8_gguf * g) {
+    if (g == nullptr) {
+        return;
+    }
+    if (g->map != nullptr) {
+        munmap(const_cast<uint8_t *>(g->map), g->size);
+    }
+    if (g->fd >= 0) {
+        close(g->fd);
+    }
+    delete g;
+}
+
+b200q8_status_t b200q8_gguf_open(const char * path, b200q8_gguf ** out) {
+    if (path == nullptr || out == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_open: null argument");
+    }
+    *out             = nullptr;
+    b200q8_gguf * g  = new b200q8_gguf();
+    g->fd            = open(path, O_RDONLY);
+    struct stat st   = {};
+    if (g->fd < 0 || fstat(g->fd, &st) != 0 || st.st_size < 24) {
+        b200q8_gguf_close(g);
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_open: cannot read %s", path);
+    }
+    g->size = (size_t) st.st_size;
+    void * m = mmap(nullptr, g->size, PROT_READ, MAP_PRIVATE, g->fd, 0);
+    if (m == MAP_FAILED) {
+        b200q8_gguf_close(g);
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_open: cannot map %s", path);
+    }
+    g->map   = static_cast<const uint8_t *>(m);
+    Reader r = { g->map, g->size };
+    if (memcmp(g->map, "GGUF", 4) != 0) {
+        b200q8_gguf_close(g);
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_open: %s is not a GGUF file", path);
+    }
+    r.pos              = 4;
+    g->version         = r.get<uint32_t>();
+    const uint64_t n_t = r.get<uint64_t>();
+    const uint64_t n_k = r.get<uint64_t>();
+    if (!r.ok || g->version < 2 || g->version > 3 || n_t > g->size / 24 || n_k > g->size / 12) {
+        b200q8_gguf_close(g);
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_open: unsupported version or bad counts in %s", path);
+    }
+    uint32_t alignment = 32;
+    for (uint64_t i = 0; i < n_k && r.ok; ++i) {
+        Kv e;
+        e.key       = r.str();
+        e.type      = r.get<uint32_t>();
+        e.value_pos = r.pos;
+        if (e.key == "general.alignment" && e.type == kU32) {
+            alignment = r.get<uint32_t>();
+        } else {
+            r.skip(e.type);
+        }
+        g->kv.push_back(std::move(e));
+    }
+    for (uint64_t i = 0; i < n_t && r.ok; ++i) {
+        Tensor t;
+        t.name   = r.str();
+        t.n_dims = (int32_t) r.get<uint32_t>();
+        if (t.n_dims < 1 || t.n_dims > 4) {
+            r.ok = false;
+            break;
+        }
+        uint64_t n = 1;
+        for (int d = 0; d < 4; ++d) {
+            t.ne[d] = 1;
+        }
+        for (int d = 0; d < t.n_dims; ++d) {
+            const uint64_t v = r.get<uint64_t>();
+            if (v == 0 || v > ((uint64_t) 1 << 40) || n > ((uint64_t) 1 << 62) / v) {
+                r.ok = false;
+            }
+            t.ne[d] = (int64_t) v;
+            n *= v;
+        }
+        t.type   = (int32_t) r.get<uint32_t>();
+        t.offset = r.get<uint64_t>();
+        t.nbytes = tensor_bytes(t.type, n);
+        g->tensors.push_back(std::move(t));
+    }
+    if (!r.ok || alignment == 0 || (alignment & (alignment - 1)) != 0) {
+        b200q8_gguf_close(g);
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_open: truncated or malformed header in %s", path);
+    }
+    g->data_start = (r.pos + alignment - 1) / alignment * alignment;
+    for (const Tensor & t : g->tensors) {
+        if (g->data_start > g->size || t.offset > g->size - g->data_start ||
+            t.nbytes > g->size - g->data_start - t.offset) {
+            const std::string name = t.name;
+            b200q8_gguf_close(g);
+            return set_error(B200Q8_ERR_INVALID_ARG, "gguf_open: tensor %s extends past the end of %s", name.c_str(),
+                             path);
+        }
+    }
+    *out = g;
+    return B200Q8_OK;
+}
+
+int64_t b200q8_gguf_tensor_count(const b200q8_gguf * g) {
+    return g == nullptr ? 0 : (int64_t) g->tensors.size();
+}
+
+int64_t b200q8_gguf_find_tensor(const b200q8_gguf * g, const char * name) {
+    if (g == nullptr || name == nullptr) {
+        return -1;
+    }
+    for (size_t i = 0; i < g->tensors.size(); ++i) {
+        if (g->tensors[i].name == name) {
+            return (int64_t) i;
+        }
+    }
+    return -1;
+}
+
+b200q8_status_t b200q8_gguf_tensor(const b200q8_gguf * g, int64_t index, b200q8_gguf_tensor_info * out) {
+    if (g == nullptr || out == nullptr || index < 0 || index >= (int64_t) g->tensors.size()) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_tensor: bad handle or index %lld", (long long) index);
+    }
+    const Tensor & t = g->tensors[(size_t) index];
+    out->name        = t.name.c_str();
+    out->type        = t.type;
+    out->n_dims      = t.n_dims;
+    for (int d = 0; d < 4; ++d) {
+        out->ne[d] = t.ne[d];
+    }
+    out->offset = t.offset;
+    out->nbytes = t.nbytes;
+    out->data   = g->map + g->data_start + t.offset;
+    return B200Q8_OK;
+}
+
+static b200q8_status_t get_scalar(const b200q8_gguf * g, const char * key, uint32_t type, void * out, size_t n) {
+    if (g == nullptr || key == nullptr || out == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_get: null argument");
+    }
+    const Kv * e = g->find_kv(key);
+    if (e == nullptr || e->type != type) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_get: %s is missing or has another type", key);
+    }
+    memcpy(out, g->map + e->value_pos, n);
+    return B200Q8_OK;
+}
+
+b200q8_status_t b200q8_gguf_get_u32(const b200q8_gguf * g, const char * key, uint32_t * out) {
+    return get_scalar(g, key, kU32, out, 4);
+}
+
+b200q8_status_t b200q8_gguf_get_f32(const b200q8_gguf * g, const char * key, float * out) {
+    return get_scalar(g, key, kF32, out, 4);
+}
+
+b200q8_status_t b200q8_gguf_get_str(const b200q8_gguf * g, const char * key, char * buf, size_t buf_size) {
+    if (g == nullptr || key == nullptr || buf == nullptr || buf_size == 0) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_get_str: null argument");
+    }
+    const Kv * e = g->find_kv(key);
+    if (e == nullptr || e->type != kStr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_get_str: %s is missing or not a string", key);
+    }
+    uint64_t n;
+    memcpy(&n, g->map + e->value_pos, 8);  // bounds checked at open
+    const size_t c = (size_t) std::min<uint64_t>(n, buf_size - 1);
+    memcpy(buf, g->map + e->value_pos + 8, c);
+    buf[c] = '\0';
+    return B200Q8_OK;
+}
+
+b200q8_status_t b200q8_gguf_talker_chain(const b200q8_gguf * g, int32_t device, int64_t max_m, int32_t mode,
+                                         b200q8_chain ** out) {
+    if (g == nullptr || out == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: null argument");
+    }
+    *out = nullptr;
+    // hyperparameters (src/arch/qwen3-tts/weights.cpp:128-138)
+    const std::string p = "synthesize.qwen3-tts.talker.";
+    uint32_t layers = 0, hidden = 0, heads = 0, kv_heads = 0, head_dim = 0, inter = 0, vocab = 0;
+    float    eps    = 0.0f;
+    const struct {
+        const char * k;
+        uint32_t *   v;
+    } u32s[] = { { "layer_count", &layers },       { "hidden_size", &hidden },
+                 { "attention_head_count", &heads }, { "key_value_head_count", &kv_heads },
+                 { "head_dim", &head_dim },          { "intermediate_size", &inter },
+                 { "codec_vocab_size", &vocab } };
+    for (const auto & e : u32s) {
+        if (b200q8_gguf_get_u32(g, (p + e.k).c_str(), e.v) != B200Q8_OK) {
+            return B200Q8_ERR_INVALID_ARG;
+        }
+    }
+    if (b200q8_gguf_get_f32(g, (p + "rms_norm_eps").c_str(), &eps) != B200Q8_OK) {
+        return B200Q8_ERR_INVALID_ARG;
+    }
+    if (layers == 0 || hidden == 0 || heads == 0 || kv_heads == 0 || head_dim == 0 || inter == 0 || vocab == 0) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: zero hyperparameter");
+    }
+    // tensors (src/arch/qwen3-tts/catalog.cpp:239-281), expected type and ne
+    struct Need {
+        std::string name;
+        int32_t     type;
+        int64_t     ne0, ne1;
+    };
+    const int64_t     q_out = (int64_t) heads * head_dim, kv_out = (int64_t) kv_heads * head_dim;
+    std::vector<Need> need;
+    for (uint32_t l = 0; l < layers; ++l) {
+        const std::string b = "talker.model.layers." + std::to_string(l) + ".";
+        need.push_back({ b + "self_attn.q_proj.weight", 8, hidden, q_out });
+        need.push_back({ b + "self_attn.k_proj.weight", 8, hidden, kv_out });
+        need.push_back({ b + "self_attn.v_proj.weight", 8, hidden, kv_out });
+        need.push_back({ b + "self_attn.o_proj.weight", 8, q_out, hidden });
+        need.push_back({ b + "mlp.gate_proj.weight", 8, hidden, inter });
+        need.push_back({ b + "mlp.up_proj.weight", 8, hidden, inter });
+        need.push_back({ b + "mlp.down_proj.weight", 8, inter, hidden });
+        need.push_back({ b + "input_layernorm.weight", 0, hidden, 1 });
+        need.push_back({ b + "post_attn_norm.weight", 0, hidden, 1 });
+    }
+    need.push_back({ "talker.model.codec_embedding.weight", 8, hidden, vocab });
+    std::vector<const Tensor *> found;
+    size_t                      total = 0;
+    for (const Need & n : need) {
+        const int64_t i = b200q8_gguf_find_tensor(g, n.name.c_str());
+        if (i < 0) {
+            return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: tensor %s is missing", n.name.c_str());
+        }
+        const Tensor & t = g->tensors[(size_t) i];
+        if (t.ne[0] != n.ne0 || t.ne[1] != n.ne1 || t.ne[2] != 1 || t.ne[3] != 1) {
+            return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: %s has shape [%lld, %lld], expected [%lld, %lld]",
+                             n.name.c_str(), (long long) t.ne[0], (long long) t.ne[1], (long long) n.ne0,
+                             (long long) n.ne1);
+        }
+        if (t.type != n.type) {
+            return set_error(B200Q8_ERR_UNSUPPORTED, "gguf_talker_chain: %s is ggml type %d, the step needs %s",
+                             n.name.c_str(), t.type, n.type == 8 ? "Q8_0" : "F32");
+        }
+        found.push_back(&t);
+        total += (t.nbytes + 15) & ~(size_t) 15;
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) {
+        return cuda_error(e, "gguf_talker_chain: cudaSetDevice");
+    }
+    uint8_t * dev = nullptr;
+    e             = cudaMalloc(&dev, total);
+    if (e != cudaSuccess) {
+        cudaSetDevice(prev);
+        return cuda_error(e, "gguf_talker_chain: weight buffer");
+    }
+    std::vector<const void *> ptr(found.size());
+    size_t                    off = 0;
+    for (size_t i = 0; i < found.size() && e == cudaSuccess; ++i) {
+        ptr[i] = dev + off;
+        e      = cudaMemcpy(dev + off, g->map + g->data_start + found[i]->offset, found[i]->nbytes,
+                            cudaMemcpyHostToDevice);
+        // 16-byte steps keep q|k|v and gate|up adjacent, so the chain uses them in place
+        off += (found[i]->nbytes + 15) & ~(size_t) 15;
+    }
+    if (e != cudaSuccess) {
+        cudaFree(dev);
+        cudaSetDevice(prev);
+        return cuda_error(e, "gguf_talker_chain: weight upload");
+    }
+    std::vector<b200q8_layer> ls(layers);
+    for (uint32_t l = 0; l < layers; ++l) {
+        const void * const * q = &ptr[(size_t) l * 9];
+        ls[l]                  = { q[0], q[1], q[2], q[3], q[4], q[5], q[6], static_cast<const float *>(q[7]),
+                                   static_cast<const float *>(q[8]) };
+    }
+    b200q8_chain_desc d = {};
+    d.n_layers          = (int32_t) layers;
+    d.hidden            = hidden;
+    d.n_head            = heads;
+    d.n_kv              = kv_heads;
+    d.head_dim          = head_dim;
+    d.inter             = inter;
+    d.eps               = eps;
+    d.max_m             = max_m;
+    d.mode              = mode;
+    d.layers            = ls.data();
+    d.table             = ptr.back();
+    d.table_rows        = vocab;
+    b200q8_chain *        c  = nullptr;
+    const b200q8_status_t st = b200q8_chain_create(&d, device, &c);
+    if (st != B200Q8_OK) {
+        cudaFree(dev);
+        cudaSetDevice(prev);
+        return st;
+    }
+    c->owned.push_back(dev);  // the chain frees the weights with its own buffers
+    cudaSetDevice(prev);
+    *out = c;
+    return B200Q8_OK;
+}
+
+}  // extern "C"

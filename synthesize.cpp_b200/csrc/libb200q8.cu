@@ -8,3 +8,4 @@
 #include "chain.cu"
 #include "pack_host.cu"
 #include "noalloc.cu"
+#include "gguf.cu"
