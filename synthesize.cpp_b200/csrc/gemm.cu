@@ -407,14 +407,26 @@ __global__ void __launch_bounds__(1024) stage_rows_kernel(const StageArgs s) {
     if (threadIdx.x == 0) GTL(0);
 #endif
     pdl_launch_dependents();
+    const int t  = threadIdx.x;
+    const int T  = blockDim.x;
+    const int K4 = s.K >> 2;
+    // The norm weights are constant: load them before the wait on the kernel
+    // that wrote this op's input, so their latency overlaps it.
+    float4 nv[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int f = t + e * T;
+        nv[e]       = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+        if (s.kind == 0 && f < K4) {
+            const float * np = s.norm + 4 * f;  // caller's pointer: only 4-byte alignment is assumed
+            nv[e]            = make_float4(np[0], np[1], np[2], np[3]);
+        }
+    }
     pdl_wait_primary();
 #ifdef B200Q8_TIMELINE
     if (threadIdx.x == 0) GTL(1);
 #endif
     const int     m    = blockIdx.x;
-    const int     t    = threadIdx.x;
-    const int     T    = blockDim.x;
-    const int     K4   = s.K >> 2;
     const float * am   = s.a + (size_t) m * s.ab_stride;
     const float * bm   = s.b ? s.b + (size_t) m * s.ab_stride : nullptr;
     float4        v[E];
@@ -477,10 +489,8 @@ __global__ void __launch_bounds__(1024) stage_rows_kernel(const StageArgs s) {
         for (int e = 0; e < E; ++e) {
             const int f = t + e * T;
             if (f < K4) {
-                const float * np = s.norm + 4 * f;  // caller's pointer: only 4-byte alignment is assumed
-                const float4  nv = make_float4(np[0], np[1], np[2], np[3]);
-                v[e]            = make_float4(__fmul_rn(__fmul_rn(v[e].x, sc), nv.x), __fmul_rn(__fmul_rn(v[e].y, sc), nv.y),
-                                              __fmul_rn(__fmul_rn(v[e].z, sc), nv.z), __fmul_rn(__fmul_rn(v[e].w, sc), nv.w));
+                v[e] = make_float4(__fmul_rn(__fmul_rn(v[e].x, sc), nv[e].x), __fmul_rn(__fmul_rn(v[e].y, sc), nv[e].y),
+                                   __fmul_rn(__fmul_rn(v[e].z, sc), nv[e].z), __fmul_rn(__fmul_rn(v[e].w, sc), nv[e].w));
             }
         }
     }
