@@ -242,6 +242,17 @@ b200q8_status_t b200q8_chain_buffer(b200q8_chain * chain, int32_t layer, int32_t
 
 void b200q8_chain_destroy(b200q8_chain * chain);
 
+/* Fault injection for tests (host side; no GPU fault): skew != 0 shifts the
+ * persistent step's launch counter by `skew`, so that (unless skew is a
+ * multiple of the step's CTA count) the CTAs of the next persistent runs
+ * disagree on the step's epoch and the hand-off waits run out (about a
+ * second); such a run must end with B200Q8_ERR_DEVICE_TIMEOUT in
+ * b200q8_device_status and leave the context usable.  skew == 0 restores the
+ * chain: the counter is realigned and one epoch skipped, so no hand-off word
+ * written by a skewed run is taken as current later.  Synchronizes the device.
+ * No reference counterpart. */
+b200q8_status_t b200q8_chain_inject_epoch_skew(b200q8_chain * chain, int32_t skew);
+
 #ifdef __cplusplus
 }
 #endif

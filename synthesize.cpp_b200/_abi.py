@@ -78,6 +78,8 @@ def lib() -> ctypes.CDLL:
     L.b200q8_quantize_rows_typed.restype = i32
     L.b200q8_quantize_chunk_host_typed.argtypes = [vp, i32, vp, i64, i64, i64, ctypes.POINTER(sz), i32]
     L.b200q8_quantize_chunk_host_typed.restype = i32
+    L.b200q8_chain_inject_epoch_skew.argtypes = [vp, i32]
+    L.b200q8_chain_inject_epoch_skew.restype = i32
     L.b200q8_quantize_chunk_host_release.argtypes = []
     L.b200q8_quantize_chunk_host_release.restype = None
     L.b200q8_dequantize_rows.argtypes = [vp, i64, i64, sz, vp, sz, vp]

@@ -512,6 +512,32 @@ b200q8_status_t b200q8_chain_timeline(b200q8_chain * c, unsigned long long * hos
 }
 #endif
 
+b200q8_status_t b200q8_chain_inject_epoch_skew(b200q8_chain * c, int32_t skew) {
+    if (c == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_inject_epoch_skew: null chain");
+    }
+    if (!c->persistent || c->sync == nullptr) {
+        return set_error(B200Q8_ERR_UNSUPPORTED, "chain_inject_epoch_skew: the chain has no persistent step");
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(c->device);
+    unsigned    counter = 0;
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&counter, c->sync, sizeof(unsigned), cudaMemcpyDeviceToHost);
+    if (skew != 0) {
+        counter += (unsigned) skew;
+    } else {
+        // realign to the CTA count and skip one epoch, so no LL word written
+        // by a skewed run can be taken as current by the next one
+        const unsigned g = (unsigned) c->sms;
+        counter          = (counter + g - 1) / g * g + g;
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(c->sync, &counter, sizeof(unsigned), cudaMemcpyHostToDevice);
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_inject_epoch_skew");
+}
+
 void b200q8_chain_destroy(b200q8_chain * c) {
     chain_free(c);
 }

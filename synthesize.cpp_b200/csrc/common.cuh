@@ -218,6 +218,19 @@ __device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t * bar, uint32_t
     return true;
 }
 
+// Bounded wait that also gives up when *flag becomes non-zero (a stop
+// request from the CTA's other threads).  Returns true only if the phase
+// completed.
+__device__ __forceinline__ bool mbar_wait_bounded_or_flag(uint64_t * bar, uint32_t parity, const int * flag) {
+    const long long start = clock64();
+    while (!mbar_try_wait_sleep(bar, parity)) {
+        if (*(volatile const int *) flag != 0 || clock64() - start > kWaitLimitCycles) {
+            return false;
+        }
+    }
+    return true;
+}
+
 // Shared-memory loads by shared-window address (explicit .shared space).
 __device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
     uint32_t v;

@@ -160,14 +160,24 @@ __device__ __forceinline__ void layer_segs(const StepArgs & a, const Plan & p, i
     segs[4] = { L.w_down + (size_t) p.ph.r0 * a.rb_i, a.rb_i, p.ph.n, p.sr_i };
 }
 
+// The global abort word holds the epoch of the launch that raised it, so an
+// abort left by an earlier launch of the same plan does not stop this one.
 __device__ __forceinline__ bool aborted(const StepArgs & a, const Smem & s) {
-    return *(volatile int *) s.abort_local != 0 || *(volatile unsigned *) &a.sync[1] != 0;
+    return *(volatile int *) s.abort_local != 0 || *(volatile unsigned *) &a.sync[1] == *(volatile unsigned *) s.epoch;
 }
 
 __device__ void raise_abort(const StepArgs & a, const Smem & s) {
     record_device_error((unsigned) B200Q8_ERR_DEVICE_TIMEOUT);
     *(volatile int *) s.abort_local = 1;
-    atomicExch(&a.sync[1], 1u);
+    atomicExch(&a.sync[1], *(volatile unsigned *) s.epoch);
+}
+
+// Consumers that stop early tell their producer, which then stops waiting
+// for slots to be released.
+__device__ __forceinline__ void stop_producer(const Smem & s) {
+    if (threadIdx.x == 0) {
+        *(volatile int *) s.abort_local = 1;
+    }
 }
 
 // Reads n LL words (this thread's share, already loaded in w[]) until all
@@ -249,6 +259,7 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
                     }
                 }
                 if (!fail && !ll_settle<kPer>(a, s, src, w, n, epoch)) {
+                    raise_abort(a, s);  // records the timeout; other CTAs stop at their next check
                     fail = true;
                 }
             }
@@ -342,6 +353,7 @@ __device__ bool stage_activations_t(const StepArgs & a, const Smem & s, int K, i
                 w[k]   = valid ? ld_ll(src[k]) : ((unsigned long long) epoch << 32);
             }
             if (!fail && !ll_settle<E>(a, s, src, w, valid ? E : 0, epoch)) {
+                raise_abort(a, s);
                 fail = true;
             }
 #pragma unroll
@@ -512,7 +524,10 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
             (unsigned long long) (tc2 - tc1 - tc_pub) | ((unsigned long long) tc_pub << 32);
     }
 #endif
-    if (lane == 0 && nt <= kMaxOpTiles) {
+    // Release the op's slots only after their data was seen to land: a slot
+    // whose copy may still be in flight must not be handed back to the
+    // producer (it then times out instead, and drains before it exits).
+    if (lane == 0 && !bad) {
         for (int i = 0; i < nt; ++i) {
             mbar_arrive(&s.empty[t_sl[i]]);
         }
@@ -591,8 +606,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
 #endif
                     for (int r = 0; r < segs[g].n; r += segs[g].sr) {
                         // slot sl was last filled in round ph^1: wait until it was released
-                        if (t >= S && !mbar_wait_bounded_sleep(&s.empty[sl], ph ^ 1u)) {
-                            raise_abort(a, s);
+                        // (or the consumers stopped, which they signal through abort_local)
+                        if (t >= S && !mbar_wait_bounded_or_flag(&s.empty[sl], ph ^ 1u, s.abort_local)) {
+                            if (*(volatile int *) s.abort_local == 0) {
+                                raise_abort(a, s);
+                            }
                             stop = true;
                             break;
                         }
@@ -681,6 +699,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 0, 1);
         if (stage_activations<M_T, MODE>(a, s, H, M, 0, s.hbuf, s.normbuf, scale, nullptr, 0, false, epoch,
                                          c == 0 ? trace(l, 0) : nullptr, (size_t) H, s.xc[0], s.xd[0], fail)) {
+            stop_producer(s);
             break;
         }
         TL(4 * l + 0, 2);
@@ -706,6 +725,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // park warps that are done until the whole op is: a warp polling the
         // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
+            stop_producer(s);
             break;
         }
         // ---- o = W_o * Q(attend(v)); attention over one cached position; o published
@@ -713,6 +733,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (stage_activations<M_T, MODE>(a, s, a.Q, M, 1, nullptr, nullptr, no_scale, ll_v, (size_t) a.KV, true,
                                          epoch, c == 0 ? trace(l, 2) : nullptr, (size_t) a.Q, s.xc[1], s.xd[1],
                                          fail)) {
+            stop_producer(s);
             break;
         }
         TL(4 * l + 1, 2);
@@ -735,6 +756,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // park warps that are done until the whole op is: a warp polling the
         // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
+            stop_producer(s);
             break;
         }
         // ---- g|u = W_gate|W_up * Q(rms_norm(h1) * norm_post), h1 = h + o; s = silu(g)*u published
@@ -744,6 +766,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 2, 1);
         if (stage_activations<M_T, MODE>(a, s, H, M, 0, s.h1buf, s.normbuf, scale, nullptr, 0, false, epoch,
                                          c == 0 ? trace(l, 5) : nullptr, (size_t) H, s.xc[0], s.xd[0], fail)) {
+            stop_producer(s);
             break;
         }
         TL(4 * l + 2, 2);
@@ -772,12 +795,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // park warps that are done until the whole op is: a warp polling the
         // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
+            stop_producer(s);
             break;
         }
         // ---- d = W_down * Q(s); d published (the last layer writes h_out = h1 + d)
         TL(4 * l + 3, 0);
         if (stage_activations<M_T, MODE>(a, s, a.I, M, 1, nullptr, nullptr, no_scale, ll_s, (size_t) a.I, false,
                                          epoch, nullptr, 0, s.xc[1], s.xd[1], fail)) {
+            stop_producer(s);
             break;
         }
         TL(4 * l + 3, 2);
@@ -806,6 +831,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // park warps that are done until the whole op is: a warp polling the
         // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
+            stop_producer(s);
             break;
         }
     }

@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int i = pre; i < total; ++i) {
             bool ok = true;
             if (lane == 0) {
-                ok = mbar_wait_bounded_sleep(&empty[s], ph ^ 1);
+                // gives up early when a consumer already failed (abort_flag)
+                ok = mbar_wait_bounded_or_flag(&empty[s], ph ^ 1, const_cast<const int *>(abort_flag));
                 if (!ok) {
                     record_device_error((unsigned) B200Q8_ERR_DEVICE_TIMEOUT);
                     *abort_flag = 1;
@@ -308,7 +309,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
             __syncwarp();
-            if (lane == 0) {
+            // a slot is handed back only after its data was seen to land
+            if (lane == 0 && !fail) {
                 mbar_arrive(&empty[s]);
             }
             if (++s == S) {
