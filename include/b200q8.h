@@ -200,6 +200,19 @@ typedef struct b200q8_layer {
     const float * norm_post;
 } b200q8_layer;
 
+/* The reference's attention in the step (src/arch/qwen3-tts/operations.cpp:
+ * 86-135): per-head RMS norms of q and k (q_norm / k_norm weights), NEOX RoPE
+ * at each token's position (ggml_rope_ext, freq_base = rope_theta), an F32
+ * KV cache per stream slot, softmax(q K^T / sqrt(head_dim)) V over the
+ * cached prefix.  Chains built with it run through b200q8_chain_run_at. */
+typedef struct b200q8_attention_desc {
+    float                 rope_theta; /* synthesize.qwen3-tts.talker.rope_theta           */
+    int64_t               n_ctx;      /* cache capacity in positions, per slot            */
+    int64_t               n_slots;    /* independent streams with a cache                 */
+    const float * const * q_norm;     /* n_layers device pointers, F32 [head_dim]         */
+    const float * const * k_norm;     /* n_layers device pointers, F32 [head_dim]         */
+} b200q8_attention_desc;
+
 typedef struct b200q8_chain_desc {
     int32_t              n_layers;
     int64_t              hidden;   /* 1024 for the 0.6B talker          */
@@ -213,6 +226,9 @@ typedef struct b200q8_chain_desc {
     const b200q8_layer * layers;   /* n_layers entries, copied          */
     const void *         table;    /* Q8_0 embedding [hidden, table_rows] */
     int64_t              table_rows;
+    /* NULL: attention over a single cached position (query head h returns v
+     * of kv head h / (n_head / n_kv)), the talker-shaped benchmark step. */
+    const b200q8_attention_desc * attention;
 } b200q8_chain_desc;
 
 typedef struct b200q8_chain b200q8_chain;
@@ -241,6 +257,17 @@ b200q8_status_t b200q8_chain_buffer(b200q8_chain * chain, int32_t layer, int32_t
                                     int64_t * stride);
 
 void b200q8_chain_destroy(b200q8_chain * chain);
+
+/* One step of a chain built with an attention desc: token m belongs to
+ * stream slot slots[m] (slots == NULL: slot m) and sits at position pos[m]
+ * (device int32 arrays of M entries).  Its k and v are written to that
+ * slot's cache at pos[m] and it attends over positions 0..pos[m], so a stream
+ * decodes with pos = 0, 1, 2, ...  A position outside [0, n_ctx) or a slot
+ * outside [0, n_slots) records B200Q8_ERR_INVALID_ARG in the device status
+ * and zeroes that token's attention. */
+b200q8_status_t b200q8_chain_run_at(b200q8_chain * chain, const int32_t * ids, const float * x_in,
+                                    const int32_t * pos, const int32_t * slots, float * h_out, int64_t M,
+                                    b200q8_stream_t stream);
 
 /* Fault injection for tests (host side; no GPU fault): skew != 0 shifts the
  * persistent step's launch counter by `skew`, so that (unless skew is a

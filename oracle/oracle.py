@@ -83,6 +83,13 @@ def lib() -> ctypes.CDLL:
         L.oracle_decoder_chain.argtypes = [c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
                                            ctypes.c_float, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
                                            c_int, c_int]
+        L.oracle_head_norm_rope.argtypes = [c_void_p, c_int64, c_int64, c_void_p, ctypes.c_float, ctypes.c_int32,
+                                            ctypes.c_float, c_int]
+        L.oracle_attend.argtypes = [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p]
+        L.oracle_decoder_chain_attn.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                                c_int64, c_int64, ctypes.c_float, ctypes.c_float, c_void_p, c_int64,
+                                                c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+                                                c_void_p, c_int, c_int]
         _lib = L
     return _lib
 
@@ -205,6 +212,48 @@ def decoder_chain(weights_q, norms: np.ndarray, table_q: np.ndarray, ids: np.nda
     h = np.empty((m, hidden), dtype=np.float32)
     lib().oracle_decoder_chain(n_layers, ptrs, _ptr(norms), hidden, n_head, n_kv, head_dim, inter, eps,
                                _ptr(table_q), table_q.shape[0], _ptr(ids), _ptr(x_in), m, _ptr(h), mode, threads)
+    return h
+
+
+def head_norm_rope(x: np.ndarray, head_dim: int, w, eps: float, pos: int, theta: float, rope: bool = True) -> np.ndarray:
+    """Per-head RMS norm (w: [head_dim] or None) then NEOX RoPE at pos; x: [..., n_heads*head_dim] (one token)."""
+    y = np.array(x, dtype=np.float32, copy=True).ravel()
+    wp = None if w is None else np.ascontiguousarray(w, dtype=np.float32)
+    lib().oracle_head_norm_rope(_ptr(y), y.size // head_dim, head_dim, None if wp is None else _ptr(wp), eps, pos,
+                                theta, 1 if rope else 0)
+    return y
+
+
+def attend(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, npos: int, n_head: int, n_kv: int,
+           head_dim: int) -> np.ndarray:
+    """One token's attention over npos cached rows (kc, vc: [>=npos, n_kv*head_dim])."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    kc = np.ascontiguousarray(kc, dtype=np.float32)
+    vc = np.ascontiguousarray(vc, dtype=np.float32)
+    out = np.empty(n_head * head_dim, np.float32)
+    lib().oracle_attend(_ptr(q), _ptr(kc), _ptr(vc), npos, n_head, n_kv, head_dim, _ptr(out))
+    return out
+
+
+def decoder_chain_attn(weights_q, norms: np.ndarray, qk_norms: np.ndarray, table_q: np.ndarray, ids: np.ndarray,
+                       x_in: np.ndarray, pos: np.ndarray, kcache: np.ndarray, vcache: np.ndarray, *, hidden: int,
+                       n_head: int, n_kv: int, head_dim: int, inter: int, eps: float = 1e-6, theta: float = 1e6,
+                       mode: int = QUANT_REF, threads: int = 0) -> np.ndarray:
+    """The decode step with the reference's attention; kcache/vcache [n_layers, M, n_ctx, n_kv*head_dim] float32,
+    updated in place (token m uses slot m at position pos[m])."""
+    n_layers = len(weights_q) // 7
+    ptrs = (ctypes.c_void_p * len(weights_q))(*[_ptr(np.ascontiguousarray(w)) for w in weights_q])
+    norms = np.ascontiguousarray(norms, dtype=np.float32)
+    qk_norms = np.ascontiguousarray(qk_norms, dtype=np.float32)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    x_in = np.ascontiguousarray(x_in, dtype=np.float32).reshape(-1, hidden)
+    assert kcache.flags.c_contiguous and vcache.flags.c_contiguous and kcache.dtype == np.float32
+    m = x_in.shape[0]
+    h = np.empty((m, hidden), dtype=np.float32)
+    lib().oracle_decoder_chain_attn(n_layers, ptrs, _ptr(norms), _ptr(qk_norms), hidden, n_head, n_kv, head_dim,
+                                    inter, eps, theta, _ptr(table_q), table_q.shape[0], _ptr(ids), _ptr(x_in),
+                                    _ptr(pos), m, kcache.shape[2], _ptr(kcache), _ptr(vcache), _ptr(h), mode, threads)
     return h
 
 

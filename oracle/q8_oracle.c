@@ -339,6 +339,83 @@ static float silu_f32(float x) {
     return x / (1.0f + expf(-x));
 }
 
+/* Qwen3's per-head RMS norm followed by NEOX RoPE, in place, for one token:
+ * x holds n_heads heads of head_dim values (src/arch/qwen3-tts/operations.cpp:
+ * 95-101: rms_norm(q, q_norm) then ggml_rope_ext(..., GGML_ROPE_TYPE_NEOX,
+ * freq_base = rope_theta, freq_scale 1, ext_factor 0, attn_factor 1)).  The
+ * rotation angle follows ggml's published RoPE recurrence: theta_0 = pos,
+ * theta_{i+1} = theta_i * base^(-2/head_dim) in fp32; NEOX pairs element i with
+ * element i + head_dim/2.  w == NULL skips the norm (v is not normed). */
+void oracle_head_norm_rope(float * x, int64_t n_heads, int64_t head_dim, const float * w, float eps, int32_t pos,
+                           float theta_base, int rope) {
+    float * t = (float *) malloc(sizeof(float) * (size_t) head_dim);
+    for (int64_t h = 0; h < n_heads; ++h) {
+        float * xh = x + h * head_dim;
+        if (w != NULL) {
+            rms_norm_mul(xh, w, t, head_dim, eps);
+            memcpy(xh, t, sizeof(float) * (size_t) head_dim);
+        }
+        if (!rope) {
+            continue;
+        }
+        const float   theta_scale = powf(theta_base, -2.0f / (float) head_dim);
+        float         theta       = (float) pos;
+        const int64_t half        = head_dim / 2;
+        for (int64_t i = 0; i < half; ++i) {
+            const float c  = cosf(theta);
+            const float sn = sinf(theta);
+            const float x0 = xh[i];
+            const float x1 = xh[i + half];
+            t[i]           = x0 * c - x1 * sn;
+            t[i + half]    = x0 * sn + x1 * c;
+            theta          = theta * theta_scale;
+        }
+        memcpy(xh, t, sizeof(float) * (size_t) head_dim);
+    }
+    free(t);
+}
+
+/* Single-token attention over npos cached positions (operations.cpp:120-131:
+ * scores = K q / sqrt(head_dim), softmax, then the softmax-weighted sum of V),
+ * query head h reading kv head h / (n_head / n_kv).  kc / vc hold npos rows of
+ * n_kv * head_dim floats.  Sums in double, one rounding to fp32 at the end:
+ * the reference's summation order is ggml-cpu's SIMD order, which the GPU
+ * does not follow either, so this is the tolerance anchor. */
+void oracle_attend(const float * q, const float * kc, const float * vc, int64_t npos, int64_t n_head, int64_t n_kv,
+                   int64_t head_dim, float * out) {
+    const int64_t group  = n_head / n_kv;
+    const int64_t kv_dim = n_kv * head_dim;
+    const double  scale  = 1.0 / sqrt((double) head_dim);
+    double *      p      = (double *) malloc(sizeof(double) * (size_t) npos);
+    for (int64_t h = 0; h < n_head; ++h) {
+        const float * qh = q + h * head_dim;
+        const int64_t kh = h / group;
+        double        mx = -INFINITY;
+        for (int64_t j = 0; j < npos; ++j) {
+            const float * kj  = kc + j * kv_dim + kh * head_dim;
+            double        dot = 0.0;
+            for (int64_t d = 0; d < head_dim; ++d) {
+                dot += (double) qh[d] * (double) kj[d];
+            }
+            p[j] = dot * scale;
+            mx   = p[j] > mx ? p[j] : mx;
+        }
+        double sum = 0.0;
+        for (int64_t j = 0; j < npos; ++j) {
+            p[j] = exp(p[j] - mx);
+            sum += p[j];
+        }
+        for (int64_t d = 0; d < head_dim; ++d) {
+            double acc = 0.0;
+            for (int64_t j = 0; j < npos; ++j) {
+                acc += p[j] * (double) vc[j * kv_dim + kh * head_dim + d];
+            }
+            out[h * head_dim + d] = (float) (acc / sum);
+        }
+    }
+    free(p);
+}
+
 void oracle_decoder_chain(int n_layers, const void * const * weights, const float * norms, int64_t hidden,
                           int64_t n_head, int64_t n_kv, int64_t head_dim, int64_t inter, float eps,
                           const void * table, int64_t table_rows, const int32_t * ids, const float * x_in, int64_t M,
@@ -382,6 +459,84 @@ void oracle_decoder_chain(int n_layers, const void * const * weights, const floa
                 const int64_t head = j / head_dim;
                 a[m * q_dim + j]   = v[m * kv_dim + (head / group) * head_dim + j % head_dim];
             }
+        }
+        oracle_mul_mat_q8_0_f32(W[3], q_dim, hidden, rb_q, a, M, q_dim * 4, o, hidden * 4, mode, NULL, threads);
+        for (int64_t i = 0; i < M * hidden; ++i) {
+            h[i] = h[i] + o[i];
+        }
+        for (int64_t m = 0; m < M; ++m) {
+            rms_norm_mul(h + m * hidden, n_post, tmp + m * hidden, hidden, eps);
+        }
+        oracle_mul_mat_q8_0_f32(W[4], hidden, inter, rb_h, tmp, M, hidden * 4, g, inter * 4, mode, NULL, threads);
+        oracle_mul_mat_q8_0_f32(W[5], hidden, inter, rb_h, tmp, M, hidden * 4, u, inter * 4, mode, NULL, threads);
+        for (int64_t i = 0; i < M * inter; ++i) {
+            s[i] = silu_f32(g[i]) * u[i];
+        }
+        oracle_mul_mat_q8_0_f32(W[6], inter, hidden, rb_i, s, M, inter * 4, o, hidden * 4, mode, NULL, threads);
+        for (int64_t i = 0; i < M * hidden; ++i) {
+            h[i] = h[i] + o[i];
+        }
+    }
+    free(tmp);
+    free(q);
+    free(k);
+    free(v);
+    free(a);
+    free(o);
+    free(g);
+    free(u);
+    free(s);
+}
+
+/* oracle_decoder_chain with the reference's attention: per layer the q and k
+ * heads are RMS-normed (qk_norms: per layer q_norm then k_norm, head_dim
+ * floats each) and rotated at pos[m]; k and v go into the caches at pos[m] of
+ * slot m (kcache / vcache: [n_layers][M][n_ctx][n_kv * head_dim], updated in
+ * place); token m attends over cached positions 0..pos[m]. */
+void oracle_decoder_chain_attn(int n_layers, const void * const * weights, const float * norms,
+                               const float * qk_norms, int64_t hidden, int64_t n_head, int64_t n_kv, int64_t head_dim,
+                               int64_t inter, float eps, float rope_theta, const void * table, int64_t table_rows,
+                               const int32_t * ids, const float * x_in, const int32_t * pos, int64_t M, int64_t n_ctx,
+                               float * kcache, float * vcache, float * h_out, int mode, int threads) {
+    const int64_t q_dim  = n_head * head_dim;
+    const int64_t kv_dim = n_kv * head_dim;
+    const size_t  rb_h   = (size_t) (hidden / ORACLE_QK8_0) * ORACLE_BLOCK_BYTES;
+    const size_t  rb_q   = (size_t) (q_dim / ORACLE_QK8_0) * ORACLE_BLOCK_BYTES;
+    const size_t  rb_i   = (size_t) (inter / ORACLE_QK8_0) * ORACLE_BLOCK_BYTES;
+    float *       h      = h_out;
+    float *       tmp    = (float *) malloc(sizeof(float) * (size_t) (M * (hidden > q_dim ? hidden : q_dim)));
+    float *       q      = (float *) malloc(sizeof(float) * (size_t) (M * q_dim));
+    float *       k      = (float *) malloc(sizeof(float) * (size_t) (M * kv_dim));
+    float *       v      = (float *) malloc(sizeof(float) * (size_t) (M * kv_dim));
+    float *       a      = (float *) malloc(sizeof(float) * (size_t) (M * q_dim));
+    float *       o      = (float *) malloc(sizeof(float) * (size_t) (M * hidden));
+    float *       g      = (float *) malloc(sizeof(float) * (size_t) (M * inter));
+    float *       u      = (float *) malloc(sizeof(float) * (size_t) (M * inter));
+    float *       s      = (float *) malloc(sizeof(float) * (size_t) (M * inter));
+    oracle_get_rows_q8_0(table, hidden, table_rows, ids, M, h);
+    for (int64_t i = 0; i < M * hidden; ++i) {
+        h[i] = x_in[i] + h[i];
+    }
+    for (int l = 0; l < n_layers; ++l) {
+        const void * const * W      = weights + 7 * l;
+        const float *        n_in   = norms + (size_t) (2 * l) * hidden;
+        const float *        n_post = norms + (size_t) (2 * l + 1) * hidden;
+        const float *        qn     = qk_norms + (size_t) (2 * l) * head_dim;
+        const float *        kn     = qk_norms + (size_t) (2 * l + 1) * head_dim;
+        for (int64_t m = 0; m < M; ++m) {
+            rms_norm_mul(h + m * hidden, n_in, tmp + m * hidden, hidden, eps);
+        }
+        oracle_mul_mat_q8_0_f32(W[0], hidden, q_dim, rb_h, tmp, M, hidden * 4, q, q_dim * 4, mode, NULL, threads);
+        oracle_mul_mat_q8_0_f32(W[1], hidden, kv_dim, rb_h, tmp, M, hidden * 4, k, kv_dim * 4, mode, NULL, threads);
+        oracle_mul_mat_q8_0_f32(W[2], hidden, kv_dim, rb_h, tmp, M, hidden * 4, v, kv_dim * 4, mode, NULL, threads);
+        for (int64_t m = 0; m < M; ++m) {
+            oracle_head_norm_rope(q + m * q_dim, n_head, head_dim, qn, eps, pos[m], rope_theta, 1);
+            oracle_head_norm_rope(k + m * kv_dim, n_kv, head_dim, kn, eps, pos[m], rope_theta, 1);
+            float * kc = kcache + (((size_t) l * M + m) * n_ctx) * kv_dim;
+            float * vc = vcache + (((size_t) l * M + m) * n_ctx) * kv_dim;
+            memcpy(kc + (size_t) pos[m] * kv_dim, k + m * kv_dim, sizeof(float) * (size_t) kv_dim);
+            memcpy(vc + (size_t) pos[m] * kv_dim, v + m * kv_dim, sizeof(float) * (size_t) kv_dim);
+            oracle_attend(q + m * q_dim, kc, vc, (int64_t) pos[m] + 1, n_head, n_kv, head_dim, a + m * q_dim);
         }
         oracle_mul_mat_q8_0_f32(W[3], q_dim, hidden, rb_q, a, M, q_dim * 4, o, hidden * 4, mode, NULL, threads);
         for (int64_t i = 0; i < M * hidden; ++i) {

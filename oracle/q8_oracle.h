@@ -96,6 +96,16 @@ void oracle_decoder_chain(int n_layers, const void * const * weights, const floa
                           int64_t n_head, int64_t n_kv, int64_t head_dim, int64_t inter, float eps,
                           const void * table, int64_t table_rows, const int32_t * ids, const float * x_in, int64_t M,
                           float * h_out, int mode, int threads);
+
+void oracle_head_norm_rope(float * x, int64_t n_heads, int64_t head_dim, const float * w, float eps, int32_t pos,
+                           float theta_base, int rope);
+void oracle_attend(const float * q, const float * kc, const float * vc, int64_t npos, int64_t n_head, int64_t n_kv,
+                   int64_t head_dim, float * out);
+void oracle_decoder_chain_attn(int n_layers, const void * const * weights, const float * norms,
+                               const float * qk_norms, int64_t hidden, int64_t n_head, int64_t n_kv, int64_t head_dim,
+                               int64_t inter, float eps, float rope_theta, const void * table, int64_t table_rows,
+                               const int32_t * ids, const float * x_in, const int32_t * pos, int64_t M, int64_t n_ctx,
+                               float * kcache, float * vcache, float * h_out, int mode, int threads);
 int oracle_max_threads(void);
 
 #ifdef __cplusplus

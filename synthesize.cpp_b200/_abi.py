@@ -42,11 +42,17 @@ class Layer(ctypes.Structure):
                 ("wdown", ctypes.c_void_p), ("norm_in", ctypes.c_void_p), ("norm_post", ctypes.c_void_p)]
 
 
+class AttentionDesc(ctypes.Structure):
+    _fields_ = [("rope_theta", ctypes.c_float), ("n_ctx", ctypes.c_int64), ("n_slots", ctypes.c_int64),
+                ("q_norm", ctypes.POINTER(ctypes.c_void_p)), ("k_norm", ctypes.POINTER(ctypes.c_void_p))]
+
+
 class ChainDesc(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int32), ("hidden", ctypes.c_int64), ("n_head", ctypes.c_int64),
                 ("n_kv", ctypes.c_int64), ("head_dim", ctypes.c_int64), ("inter", ctypes.c_int64),
                 ("eps", ctypes.c_float), ("max_m", ctypes.c_int64), ("mode", ctypes.c_int32),
-                ("layers", ctypes.POINTER(Layer)), ("table", ctypes.c_void_p), ("table_rows", ctypes.c_int64)]
+                ("layers", ctypes.POINTER(Layer)), ("table", ctypes.c_void_p), ("table_rows", ctypes.c_int64),
+                ("attention", ctypes.POINTER(AttentionDesc))]
 
 
 def header_symbols(header: str = HEADER) -> list[str]:
@@ -96,6 +102,8 @@ def lib() -> ctypes.CDLL:
     L.b200q8_chain_create.restype = i32
     L.b200q8_chain_run.argtypes = [vp, vp, vp, vp, i64, vp]
     L.b200q8_chain_run.restype = i32
+    L.b200q8_chain_run_at.argtypes = [vp, vp, vp, vp, vp, vp, i64, vp]
+    L.b200q8_chain_run_at.restype = i32
     L.b200q8_chain_buffer.argtypes = [vp, i32, i32, ctypes.POINTER(vp), ctypes.POINTER(i64)]
     L.b200q8_chain_buffer.restype = i32
     L.b200q8_chain_destroy.argtypes = [vp]

@@ -11,7 +11,7 @@ import ctypes
 
 import torch
 
-from ._abi import ChainDesc, Layer, check, lib
+from ._abi import AttentionDesc, ChainDesc, Layer, check, lib
 from .q8 import QUANT_REF, stream_ptr
 
 BUFFERS = {"n1": 0, "qkv": 1, "attn": 2, "o": 3, "h1": 4, "n2": 5, "gu": 6, "s": 7, "down": 8, "h": 9}
@@ -22,15 +22,25 @@ class DecodeChain:
     norm_in, norm_post (float32 [hidden]); table: uint8 Q8_0 [table_rows, hidden/32*34]."""
 
     def __init__(self, layers, table: torch.Tensor, *, hidden: int, n_head: int, n_kv: int, head_dim: int,
-                 inter: int, eps: float = 1e-6, max_m: int = 8, mode: int = QUANT_REF):
+                 inter: int, eps: float = 1e-6, max_m: int = 8, mode: int = QUANT_REF, attention: dict | None = None):
+        """attention: None for the single-cached-position step, or dict(rope_theta, n_ctx, n_slots) with each layer
+        dict also holding q_norm and k_norm (float32 [head_dim]); such a chain runs through run_at."""
         self._keep = (layers, table)
         arr = (Layer * len(layers))()
         for i, L in enumerate(layers):
             arr[i] = Layer(*[L[k].data_ptr() for k in ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown",
                                                        "norm_in", "norm_post")])
         self._arr = arr
+        attn_ptr = None
+        if attention is not None:
+            qn = (ctypes.c_void_p * len(layers))(*[L["q_norm"].data_ptr() for L in layers])
+            kn = (ctypes.c_void_p * len(layers))(*[L["k_norm"].data_ptr() for L in layers])
+            self._attn = (AttentionDesc(attention["rope_theta"], attention["n_ctx"], attention["n_slots"],
+                                        ctypes.cast(qn, ctypes.POINTER(ctypes.c_void_p)),
+                                        ctypes.cast(kn, ctypes.POINTER(ctypes.c_void_p))), qn, kn)
+            attn_ptr = ctypes.pointer(self._attn[0])
         desc = ChainDesc(len(layers), hidden, n_head, n_kv, head_dim, inter, eps, max_m, mode,
-                         ctypes.cast(arr, ctypes.POINTER(Layer)), table.data_ptr(), table.shape[0])
+                         ctypes.cast(arr, ctypes.POINTER(Layer)), table.data_ptr(), table.shape[0], attn_ptr)
         handle = ctypes.c_void_p()
         check(lib().b200q8_chain_create(ctypes.byref(desc), table.device.index or 0, ctypes.byref(handle)))
         self._h = handle
@@ -54,6 +64,15 @@ class DecodeChain:
     def run(self, ids: torch.Tensor, x_in: torch.Tensor, h_out: torch.Tensor) -> torch.Tensor:
         m = ids.numel()
         check(lib().b200q8_chain_run(self._h, ids.data_ptr(), x_in.data_ptr(), h_out.data_ptr(), m, stream_ptr()))
+        return h_out
+
+    def run_at(self, ids: torch.Tensor, x_in: torch.Tensor, pos: torch.Tensor, h_out: torch.Tensor,
+               slots: torch.Tensor | None = None) -> torch.Tensor:
+        """One step with attention: token m at position pos[m] of stream slot slots[m] (default slot m)."""
+        m = ids.numel()
+        check(lib().b200q8_chain_run_at(self._h, ids.data_ptr(), x_in.data_ptr(), pos.data_ptr(),
+                                        slots.data_ptr() if slots is not None else None, h_out.data_ptr(), m,
+                                        stream_ptr()))
         return h_out
 
     def buffer(self, layer: int, name: str, m: int) -> torch.Tensor:

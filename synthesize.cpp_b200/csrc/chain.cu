@@ -88,14 +88,54 @@ struct b200q8_chain {
     bool                         persistent   = false;
     void *                       timeline     = nullptr;  // B200Q8_TIMELINE analysis builds only
     void *                       planes       = nullptr;  // batched path (M > 8): GEMM code/scale planes
+    // attention with a KV cache (desc.attention != nullptr)
+    bool                         attn         = false;
+    b200q8_attention_desc        ad           = {};
+    std::vector<const float *>   q_norm, k_norm;
+    float *                      kv_cache     = nullptr;  // K then V: [n_layers][n_slots][n_ctx][KV] each
+    float *                      q_rot        = nullptr;  // [max_m][Q]
+    float *                      attn_partial = nullptr;  // [max_m][n_head][kAttnMaxSplits][head_dim + 2]
+    unsigned *                   attn_count   = nullptr;  // [max_m][n_head]
 
     struct Graph {
         int64_t         M;
         const void *    ids;
         const void *    x;
         void *          h;
+        const void *    pos;
+        const void *    slots;
         cudaGraphExec_t exec;
     };
+
+    // attention arguments of layer l for tokens [m0, m0 + M)
+    AttnArgs attn_args(int l, float * qkv, size_t qkv_stride, float * out, size_t out_stride, const int32_t * pos,
+                       const int32_t * slots, int64_t m0) const {
+        AttnArgs a   = {};
+        const int64_t KV = d.n_kv * d.head_dim;
+        a.qkv        = qkv;
+        a.qkv_stride = qkv_stride;
+        a.n_head     = (int) d.n_head;
+        a.n_kv       = (int) d.n_kv;
+        a.head_dim   = (int) d.head_dim;
+        a.eps        = d.eps;
+        a.rope_theta = ad.rope_theta;
+        a.q_norm     = q_norm[l];
+        a.k_norm     = k_norm[l];
+        a.pos        = pos + m0;
+        a.slots      = slots ? slots + m0 : nullptr;
+        a.slot_base  = (int) m0;
+        a.n_ctx      = (int) ad.n_ctx;
+        a.n_slots    = (int) ad.n_slots;
+        a.q_rot      = q_rot + m0 * d.n_head * d.head_dim;
+        const size_t layer = (size_t) ad.n_slots * ad.n_ctx * KV;
+        a.k_cache    = kv_cache + (size_t) l * layer;
+        a.v_cache    = kv_cache + (size_t) d.n_layers * layer + (size_t) l * layer;
+        a.partial    = attn_partial + m0 * d.n_head * kAttnMaxSplits * (d.head_dim + 2);
+        a.counters   = attn_count + m0 * d.n_head;
+        a.out        = out;
+        a.out_stride = out_stride;
+        return a;
+    }
     std::vector<Graph> graphs;
 
     float * buf(int layer, int which) { return act + (size_t) layer * layer_floats + buf_off[which]; }
@@ -151,7 +191,8 @@ const uint8_t * contiguous(b200q8_chain * c, const void * a, size_t a_bytes, con
 // M > 8: per op, a per-token prologue kernel (norm / GQA / SwiGLU + residual,
 // quantized into code and scale planes) then the int8 tensor-core GEMM;
 // 2 launches per op with programmatic dependent launch between them.
-cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, int64_t M, float * h_out) {
+cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, int64_t M, const int32_t * pos,
+                                 const int32_t * slots, float * h_out) {
     const b200q8_chain_desc & d = c->d;
     const int64_t H = d.hidden, Q = d.n_head * d.head_dim, KV = d.n_kv * d.head_dim, I = d.inter;
     const int     hd = (int) d.head_dim, grp = (int) (d.n_head / d.n_kv);
@@ -172,10 +213,17 @@ cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, int64_t M, f
         if (e == cudaSuccess)
             e = launch_gemm_staged(c->w_qkv[l], c->rb_h, H, c->qkv_dim, xrec, M, B(l, kQkv),
                                    (size_t) c->qkv_dim, st, c->sms, true);
-        // o: attend(v)
-        if (e == cudaSuccess)
+        // o: attend(v) -- over the cache when the chain has attention, else the single cached position
+        if (e == cudaSuccess && c->attn) {
+            const AttnArgs aa = c->attn_args(l, B(l, kQkv), (size_t) c->qkv_dim, B(l, kAttn), (size_t) Q, pos, slots, 0);
+            e = launch_attention(aa, M, attention_splits(M, (int) d.n_head, c->sms), st, true);
+            if (e == cudaSuccess)
+                e = launch_stage_rows(3, B(l, kAttn), nullptr, (size_t) Q, nullptr, 0, nullptr, d.eps, (int) Q, hd,
+                                      grp, nullptr, 0, M, d.mode, xrec, st, true);
+        } else if (e == cudaSuccess) {
             e = launch_stage_rows(1, B(l, kQkv) + Q + KV, nullptr, (size_t) c->qkv_dim, nullptr, 0, nullptr, d.eps,
                                   (int) Q, hd, grp, B(l, kAttn), (size_t) Q, M, d.mode, xrec, st, true);
+        }
         if (e == cudaSuccess)
             e = launch_gemm_staged(c->w_o[l], c->rb_q, Q, H, xrec, M, B(l, kO), (size_t) H, st, c->sms, true);
         // gate|up: n2 = rms_norm(h1) * norm_post with h1 = h + o
@@ -202,7 +250,7 @@ cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, int64_t M, f
 }
 
 cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, int64_t M, const int32_t * ids, const float * x_in,
-                         float * h_out) {
+                         const int32_t * pos, const int32_t * slots, float * h_out) {
     const b200q8_chain_desc & d = c->d;
     const int64_t H = d.hidden, Q = d.n_head * d.head_dim, KV = d.n_kv * d.head_dim, I = d.inter;
     {
@@ -216,7 +264,7 @@ cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, int64_t M, const int
         }
     }
     if (M > 8 && c->planes != nullptr) {
-        return enqueue_step_batched(c, st, M, h_out);
+        return enqueue_step_batched(c, st, M, pos, slots, h_out);
     }
     for (int64_t m0 = 0; m0 < M; m0 += 8) {
         const int   mc = (int) std::min<int64_t>(M - m0, 8);
@@ -237,9 +285,16 @@ cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, int64_t M, const int
             if (e != cudaSuccess) return e;
             // h1 = h + W_o * Q(attend(v))
             p.w = c->w_o[l]; p.row_bytes = c->rb_q; p.K = (int) Q; p.N = (int) H;
-            p.pro = kProGqa; p.x = B(kQkv) + Q + KV; p.x_stride = (size_t) c->qkv_dim;
-            p.head_dim = (int) d.head_dim; p.group = (int) (d.n_head / d.n_kv);
-            p.pro_out = B(kAttn); p.pro_out_stride = (size_t) Q;
+            if (c->attn) {
+                const AttnArgs aa = c->attn_args(l, B(kQkv), (size_t) c->qkv_dim, B(kAttn), (size_t) Q, pos, slots, m0);
+                e = launch_attention(aa, mc, attention_splits(mc, (int) d.n_head, c->sms), st, true);
+                if (e != cudaSuccess) return e;
+                p.pro = kProPlain; p.x = B(kAttn); p.x_stride = (size_t) Q; p.pro_out = nullptr;
+            } else {
+                p.pro = kProGqa; p.x = B(kQkv) + Q + KV; p.x_stride = (size_t) c->qkv_dim;
+                p.head_dim = (int) d.head_dim; p.group = (int) (d.n_head / d.n_kv);
+                p.pro_out = B(kAttn); p.pro_out_stride = (size_t) Q;
+            }
             p.y = B(kO); p.y_stride = (size_t) H; p.res = h; p.y_res = B(kH1); p.res_stride = (size_t) H;
             e = launch_gemv(p, st, c->sms, true);
             if (e != cudaSuccess) return e;
@@ -262,6 +317,46 @@ cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, int64_t M, const int
         }
     }
     return cudaSuccess;
+}
+
+// The step as a CUDA graph, captured once per (M, buffers) and replayed.
+b200q8_status_t run_graph(b200q8_chain * c, const int32_t * ids, const float * x_in, const int32_t * pos,
+                          const int32_t * slots, float * h_out, int64_t M, b200q8_stream_t stream) {
+    cudaError_t     e    = cudaSuccess;
+    cudaGraphExec_t exec = nullptr;
+    for (auto & g : c->graphs) {
+        if (g.M == M && g.ids == ids && g.x == x_in && g.h == h_out && g.pos == pos && g.slots == slots) {
+            exec = g.exec;
+            break;
+        }
+    }
+    if (exec == nullptr) {
+        cudaGraph_t graph = nullptr;
+        e                 = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal);
+        if (e == cudaSuccess) {
+            cudaError_t e2 = enqueue_step(c, c->cap_stream, M, ids, x_in, pos, slots, h_out);
+            e              = cudaStreamEndCapture(c->cap_stream, &graph);
+            if (e2 != cudaSuccess) {
+                e = e2;
+            }
+        }
+        if (e == cudaSuccess) {
+            e = cudaGraphInstantiate(&exec, graph, 0);
+        }
+        if (graph) {
+            cudaGraphDestroy(graph);
+        }
+        if (e != cudaSuccess) {
+            return cuda_error(e, "chain_run: graph capture");
+        }
+        if (c->graphs.size() >= 8) {
+            cudaGraphExecDestroy(c->graphs.front().exec);
+            c->graphs.erase(c->graphs.begin());
+        }
+        c->graphs.push_back({ M, ids, x_in, h_out, pos, slots, exec });
+    }
+    e = cudaGraphLaunch(exec, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_run: graph launch");
 }
 
 }  // namespace
@@ -287,14 +382,37 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
             return set_error(B200Q8_ERR_INVALID_ARG, "chain_create: layer %d has a null pointer", l);
         }
     }
+    if (d.attention != nullptr) {
+        const b200q8_attention_desc & ad = *d.attention;
+        if (!attention_supported((int) d.head_dim, (int) d.n_head, (int) d.n_kv) || ad.n_ctx < 1 ||
+            ad.n_ctx > (1 << 30) || ad.n_slots < 1 || ad.n_slots > (1 << 20) || !(ad.rope_theta > 0.0f) ||
+            ad.q_norm == nullptr || ad.k_norm == nullptr) {
+            return set_error(B200Q8_ERR_INVALID_ARG, "chain_create: bad attention desc (head_dim must be a multiple "
+                                                     "of 32 up to 256; n_ctx, n_slots, rope_theta positive)");
+        }
+        for (int l = 0; l < d.n_layers; ++l) {
+            if (ad.q_norm[l] == nullptr || ad.k_norm[l] == nullptr) {
+                return set_error(B200Q8_ERR_INVALID_ARG, "chain_create: layer %d has a null q/k norm", l);
+            }
+        }
+    }
     b200q8_chain * c = new (std::nothrow) b200q8_chain();
     if (c == nullptr) {
         return set_error(B200Q8_ERR_OOM, "chain_create: out of host memory");
     }
+    if (d.attention != nullptr) {
+        c->attn = true;
+        c->ad   = *d.attention;
+        c->q_norm.assign(d.attention->q_norm, d.attention->q_norm + d.n_layers);
+        c->k_norm.assign(d.attention->k_norm, d.attention->k_norm + d.n_layers);
+        c->ad.q_norm = nullptr;
+        c->ad.k_norm = nullptr;
+    }
     c->device = device;
     c->d      = d;
     c->layers.assign(d.layers, d.layers + d.n_layers);
-    c->d.layers = nullptr;
+    c->d.layers    = nullptr;
+    c->d.attention = nullptr;
     int prev    = 0;
     cudaGetDevice(&prev);
     cudaError_t e = cudaSetDevice(device);
@@ -357,9 +475,29 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
             c->planes = p;
         }
     }
-    // persistent step: per-layer weight table, LL hand-off words, sync words
+    if (e == cudaSuccess && c->attn) {
+        const size_t kv_floats = 2 * (size_t) d.n_layers * c->ad.n_slots * c->ad.n_ctx * KV;
+        void *       p1 = nullptr, *p2 = nullptr, *p3 = nullptr, *p4 = nullptr;
+        e = cudaMalloc(&p1, kv_floats * sizeof(float));
+        if (e == cudaSuccess) { c->owned.push_back(p1); e = cudaMemset(p1, 0, kv_floats * sizeof(float)); }
+        if (e == cudaSuccess) e = cudaMalloc(&p2, sizeof(float) * (size_t) d.max_m * Q);
+        if (e == cudaSuccess) {
+            c->owned.push_back(p2);
+            e = cudaMalloc(&p3, sizeof(float) * (size_t) d.max_m * d.n_head * kAttnMaxSplits * (d.head_dim + 2));
+        }
+        if (e == cudaSuccess) { c->owned.push_back(p3); e = cudaMalloc(&p4, sizeof(unsigned) * (size_t) d.max_m * d.n_head); }
+        if (e == cudaSuccess) { c->owned.push_back(p4); e = cudaMemset(p4, 0, sizeof(unsigned) * (size_t) d.max_m * d.n_head); }
+        if (e == cudaSuccess) {
+            c->kv_cache     = static_cast<float *>(p1);
+            c->q_rot        = static_cast<float *>(p2);
+            c->attn_partial = static_cast<float *>(p3);
+            c->attn_count   = static_cast<unsigned *>(p4);
+        }
+    }
+    // persistent step (single-position attention only): per-layer weight
+    // table, LL hand-off words, sync words
     const char * per_op = getenv("B200Q8_CHAIN_PER_OP");
-    if (e == cudaSuccess && !(per_op && per_op[0] == '1')) {
+    if (e == cudaSuccess && !c->attn && !(per_op && per_op[0] == '1')) {
         std::vector<StepLayerDev> host_layers(d.n_layers);
         for (int l = 0; l < d.n_layers; ++l) {
             host_layers[l] = { c->w_qkv[l], c->w_o[l], c->w_gu[l], c->w_gu[l] + (size_t) I * c->rb_h, c->w_d[l],
@@ -412,6 +550,9 @@ b200q8_status_t b200q8_chain_run(b200q8_chain * c, const int32_t * ids, const fl
     if (c == nullptr || ids == nullptr || x_in == nullptr || h_out == nullptr || M < 1 || M > c->d.max_m) {
         return set_error(B200Q8_ERR_INVALID_ARG, "chain_run: bad argument (M must be in [1, max_m])");
     }
+    if (c->attn) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_run: this chain has attention; use chain_run_at");
+    }
     int prev = 0;
     cudaGetDevice(&prev);
     cudaError_t e = cudaSetDevice(c->device);
@@ -447,42 +588,33 @@ b200q8_status_t b200q8_chain_run(b200q8_chain * c, const int32_t * ids, const fl
             return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_run: persistent step launch");
         }
     }
-    cudaGraphExec_t exec = nullptr;
-    for (auto & g : c->graphs) {
-        if (g.M == M && g.ids == ids && g.x == x_in && g.h == h_out) {
-            exec = g.exec;
-            break;
-        }
-    }
-    if (exec == nullptr) {
-        cudaGraph_t graph = nullptr;
-        e                 = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal);
-        if (e == cudaSuccess) {
-            cudaError_t e2 = enqueue_step(c, c->cap_stream, M, ids, x_in, h_out);
-            e              = cudaStreamEndCapture(c->cap_stream, &graph);
-            if (e2 != cudaSuccess) {
-                e = e2;
-            }
-        }
-        if (e == cudaSuccess) {
-            e = cudaGraphInstantiate(&exec, graph, 0);
-        }
-        if (graph) {
-            cudaGraphDestroy(graph);
-        }
-        if (e != cudaSuccess) {
-            cudaSetDevice(prev);
-            return cuda_error(e, "chain_run: graph capture");
-        }
-        if (c->graphs.size() >= 8) {
-            cudaGraphExecDestroy(c->graphs.front().exec);
-            c->graphs.erase(c->graphs.begin());
-        }
-        c->graphs.push_back({ M, ids, x_in, h_out, exec });
-    }
-    e = cudaGraphLaunch(exec, reinterpret_cast<cudaStream_t>(stream));
+    const b200q8_status_t st = run_graph(c, ids, x_in, nullptr, nullptr, h_out, M, stream);
     cudaSetDevice(prev);
-    return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_run: graph launch");
+    return st;
+}
+
+b200q8_status_t b200q8_chain_run_at(b200q8_chain * c, const int32_t * ids, const float * x_in, const int32_t * pos,
+                                    const int32_t * slots, float * h_out, int64_t M, b200q8_stream_t stream) {
+    if (c == nullptr || ids == nullptr || x_in == nullptr || pos == nullptr || h_out == nullptr || M < 1 ||
+        M > c->d.max_m) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_run_at: bad argument (M must be in [1, max_m])");
+    }
+    if (!c->attn) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_run_at: the chain was built without an attention desc");
+    }
+    if (slots == nullptr && M > c->ad.n_slots) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_run_at: M (%lld) tokens need explicit slots beyond n_slots",
+                         (long long) M);
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) {
+        return cuda_error(e, "chain_run_at: cudaSetDevice");
+    }
+    const b200q8_status_t st = run_graph(c, ids, x_in, pos, slots, h_out, M, stream);
+    cudaSetDevice(prev);
+    return st;
 }
 
 b200q8_status_t b200q8_chain_buffer(b200q8_chain * c, int32_t layer, int32_t which, float ** ptr, int64_t * stride) {

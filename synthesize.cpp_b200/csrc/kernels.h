@@ -99,6 +99,34 @@ cudaError_t  launch_stage_rows(int kind, const float * a, const float * b, size_
 cudaError_t launch_residual_rows(const float * a, const float * b, size_t ab_stride, float * out, size_t out_stride,
                                  int K, int64_t M, cudaStream_t stream, bool pdl);
 
+// ---- attention with a KV cache (attention.cu)
+
+constexpr int kAttnMaxSplits = 32;
+
+struct AttnArgs {
+    const float *   qkv;         // [M][qkv_stride]: q heads, then k heads, then v heads
+    size_t          qkv_stride;  // floats
+    int             n_head, n_kv, head_dim;
+    float           eps, rope_theta;
+    const float *   q_norm;      // [head_dim] of this layer
+    const float *   k_norm;
+    const int32_t * pos;         // [M] positions
+    const int32_t * slots;       // [M] cache slots, or null: slot = slot_base + token index
+    int             slot_base;
+    int             n_ctx, n_slots;
+    float *         q_rot;       // [M][n_head*head_dim] normed, rotated q
+    float *         k_cache;     // this layer: [n_slots][n_ctx][n_kv][head_dim]
+    float *         v_cache;
+    float *         partial;     // [M][n_head][splits][head_dim + 2]
+    unsigned *      counters;    // [M][n_head], zero between launches
+    float *         out;         // [M][out_stride]: attention output, head-major
+    size_t          out_stride;
+};
+
+bool        attention_supported(int head_dim, int n_head, int n_kv);
+int         attention_splits(int64_t M, int n_head, int sm_count);
+cudaError_t launch_attention(const AttnArgs & a, int64_t M, int splits, cudaStream_t stream, bool pdl);
+
 // ---- the persistent decode step (decode_step.cu)
 
 struct StepLayerDev {

@@ -4,6 +4,7 @@
 #include "gemv.cu"
 #include "gemm.cu"
 #include "decode_step.cu"
+#include "attention.cu"
 #include "abi.cu"
 #include "chain.cu"
 #include "pack_host.cu"
