@@ -213,6 +213,17 @@ typedef struct b200q8_attention_desc {
     const float * const * k_norm;     /* n_layers device pointers, F32 [head_dim]         */
 } b200q8_attention_desc;
 
+/* The output side of a step (src/arch/qwen3-tts/talker.cpp:169-185,
+ * code-predictor.cpp:66-80): the final RMS norm of the residual stream and
+ * one or more Q8_0 heads applied to it.  The talker has one head
+ * (codec_head), the code predictor one per acoustic group (lm_head.{g}). */
+typedef struct b200q8_output_desc {
+    const float *        norm;    /* F32 [hidden] (model.norm.weight)                      */
+    const void * const * heads;   /* n_heads device pointers, Q8_0 with ne = [hidden, vocab] */
+    int32_t              n_heads;
+    int64_t              vocab;
+} b200q8_output_desc;
+
 typedef struct b200q8_chain_desc {
     int32_t              n_layers;
     int64_t              hidden;   /* 1024 for the 0.6B talker          */
@@ -229,6 +240,8 @@ typedef struct b200q8_chain_desc {
     /* NULL: attention over a single cached position (query head h returns v
      * of kv head h / (n_head / n_kv)), the talker-shaped benchmark step. */
     const b200q8_attention_desc * attention;
+    /* NULL: the step ends at the residual stream (h_out). */
+    const b200q8_output_desc *    output;
 } b200q8_chain_desc;
 
 typedef struct b200q8_chain b200q8_chain;
@@ -268,6 +281,100 @@ void b200q8_chain_destroy(b200q8_chain * chain);
 b200q8_status_t b200q8_chain_run_at(b200q8_chain * chain, const int32_t * ids, const float * x_in,
                                     const int32_t * pos, const int32_t * slots, float * h_out, int64_t M,
                                     b200q8_stream_t stream);
+
+/* One step with every input and output the reference's graphs vary
+ * (talker.cpp:135-185 for the talker, code-predictor.cpp:34-80 for the code
+ * predictor, whose calls differ in input table, head and input rows):
+ *   h0     = x_in + get_rows(table, ids)    (either term may be absent)
+ *   h      = the layers of b200q8_chain_run / _run_at applied to h0
+ *   hidden = rms_norm(h) * output.norm
+ *   logits = heads[head] * Q(hidden)
+ * All pointers are device pointers; the buffers must not overlap. */
+typedef struct b200q8_step_args {
+    int64_t         M;          /* tokens, 1..max_m                                         */
+    const int32_t * ids;        /* [M] rows of `table`, or NULL: no lookup                  */
+    const void *    table;      /* Q8_0 [hidden, table_rows]; NULL: the desc's table        */
+    int64_t         table_rows;
+    const float *   x_in;       /* [M][hidden], or NULL: zeros (ids then required)          */
+    const int32_t * pos;        /* [M] positions (attention chains only, else NULL)         */
+    const int32_t * slots;      /* [M] stream slots, or NULL: slot m                        */
+    float *         h_out;      /* [M][hidden] residual stream after the last layer, or NULL */
+    float *         hidden_out; /* [M][hidden], or NULL (chains with an output desc)        */
+    float *         logits;     /* [M][vocab], or NULL (chains with an output desc)         */
+    int32_t         head;       /* which head computes logits                               */
+} b200q8_step_args;
+
+/* Runs one step as a CUDA graph captured once per distinct argument set
+ * (pointers, M, head).  With hidden_out and logits both NULL the output stage
+ * is skipped.  Errors: B200Q8_ERR_INVALID_ARG for a missing required pointer,
+ * M outside [1, max_m], pos on a chain without attention (or none on one
+ * with), an output on a chain without an output desc, head outside
+ * [0, n_heads). */
+b200q8_status_t b200q8_chain_step(b200q8_chain * chain, const b200q8_step_args * args, b200q8_stream_t stream);
+
+/* ---- one frame of Qwen3-TTS decoding: talker + code predictor ----------- */
+
+/* A frame as src/arch/qwen3-tts/model.cpp:1310-1489 computes it, for M
+ * independent streams in one CUDA graph, with G = groups codes per frame:
+ *
+ *   x      = sum_{g=1..G-1} ptable[g-1][prev[g]]  + ttable[prev[0]] + text
+ *            (sum_code_embeddings, code-predictor.cpp:84-109, in group order;
+ *            then build_talker_step_input, talker.cpp:120-133)
+ *   talker step at pos -> hidden, logits        -> codes[0]
+ *   predictor at positions 0, 1 over [hidden, ttable[codes[0]]], head 0
+ *                                               -> codes[1]
+ *   for g = 1..G-2: predictor at position g+1 over ptable[g-1][codes[g]],
+ *                   head g                      -> codes[g+1]
+ *
+ * (the schedule of code-predictor-host.cpp:15-41).  A code is either the
+ * replayed one (request.replay_codes) or the reference's greedy choice
+ * (request.sample == false): the first index of the largest logit
+ * (std::max_element, code-predictor-host.cpp:45-49,71-80), after the
+ * talker's repetition penalty over the stream's previously chosen semantic
+ * codes (apply_repetition_penalty, code-predictor-host.cpp:51-69).  Sampling
+ * with a temperature is not done on the device. */
+typedef struct b200q8_frame_desc {
+    b200q8_chain *       talker;     /* attention + output desc with >= 1 head; its table = ttable  */
+    b200q8_chain *       predictor;  /* attention + output desc with >= G-1 heads, n_ctx >= G,
+                                        max_m >= 2 * the frame's M, same device and hidden width   */
+    int32_t              groups;     /* code_group_count (16)                                       */
+    const void * const * tables;     /* G-1 device pointers: predictor codec_embedding.{g}, Q8_0
+                                        [talker hidden, table_rows]                                 */
+    int64_t              table_rows;
+    float                repetition_penalty;  /* the talker's; values <= 1 apply none             */
+} b200q8_frame_desc;
+
+typedef struct b200q8_frame b200q8_frame;
+
+/* Builds the frame plan: device copies of the table list, the predictor's
+ * position arrays and a per-slot history of chosen semantic codes (cleared;
+ * one per talker slot).  The chains stay owned by the caller and must
+ * outlive the frame. */
+b200q8_status_t b200q8_frame_create(const b200q8_frame_desc * desc, b200q8_frame ** out);
+
+typedef struct b200q8_frame_args {
+    int64_t         M;
+    /* 1: the talker already ran (the prompt pass, through b200q8_chain_step);
+     * hidden and talker_logits then hold its outputs and are read, text /
+     * prev / pos are ignored, and the frame starts at selecting codes[0]. */
+    int32_t         skip_talker;
+    const float *   text;           /* [M][hidden] the frame's text-side input row             */
+    const int32_t * prev;           /* [M][G] the previous frame's codes                        */
+    const int32_t * pos;            /* [M] the talker position of this frame's token            */
+    const int32_t * slots;          /* [M] stream slots (both caches and the history); NULL: m  */
+    const int32_t * replay;         /* [M][G] codes to take instead of choosing; NULL: greedy   */
+    int32_t *       codes;          /* [M][G] out                                               */
+    float *         hidden;         /* [M][hidden] talker hidden: out (in when skip_talker); may be NULL unless skip_talker */
+    float *         talker_logits;  /* [M][talker vocab]: same                                  */
+} b200q8_frame_args;
+
+b200q8_status_t b200q8_frame_run(b200q8_frame * frame, const b200q8_frame_args * args, b200q8_stream_t stream);
+
+/* Forgets the chosen-code history of one slot (slot < 0: every slot), as a
+ * new utterance starts with an empty history.  Enqueued on `stream`. */
+b200q8_status_t b200q8_frame_reset_history(b200q8_frame * frame, int32_t slot, b200q8_stream_t stream);
+
+void b200q8_frame_destroy(b200q8_frame * frame);
 
 /* Fault injection for tests (host side; no GPU fault): skew != 0 shifts the
  * persistent step's launch counter by `skew`, so that (unless skew is a

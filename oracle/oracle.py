@@ -88,8 +88,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_attend.argtypes = [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p]
         L.oracle_decoder_chain_attn.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                                 c_int64, c_int64, ctypes.c_float, ctypes.c_float, c_void_p, c_int64,
-                                                c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
-                                                c_void_p, c_int, c_int]
+                                                c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                                c_void_p, c_void_p, c_void_p, c_int, c_int]
+        L.oracle_rms_norm_rows.argtypes = [c_void_p, c_void_p, c_void_p, c_int64, c_int64, ctypes.c_float]
         _lib = L
     return _lib
 
@@ -235,26 +236,123 @@ def attend(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, npos: int, n_head: int
     return out
 
 
-def decoder_chain_attn(weights_q, norms: np.ndarray, qk_norms: np.ndarray, table_q: np.ndarray, ids: np.ndarray,
-                       x_in: np.ndarray, pos: np.ndarray, kcache: np.ndarray, vcache: np.ndarray, *, hidden: int,
-                       n_head: int, n_kv: int, head_dim: int, inter: int, eps: float = 1e-6, theta: float = 1e6,
-                       mode: int = QUANT_REF, threads: int = 0) -> np.ndarray:
-    """The decode step with the reference's attention; kcache/vcache [n_layers, M, n_ctx, n_kv*head_dim] float32,
-    updated in place (token m uses slot m at position pos[m])."""
+def decoder_chain_attn(weights_q, norms: np.ndarray, qk_norms: np.ndarray, table_q: np.ndarray | None,
+                       ids: np.ndarray | None, x_in: np.ndarray, pos: np.ndarray, kcache: np.ndarray,
+                       vcache: np.ndarray, *, hidden: int, n_head: int, n_kv: int, head_dim: int, inter: int,
+                       eps: float = 1e-6, theta: float = 1e6, mode: int = QUANT_REF, threads: int = 0,
+                       slots: np.ndarray | None = None) -> np.ndarray:
+    """The decode step with the reference's attention; kcache/vcache [n_layers, n_slots, n_ctx, n_kv*head_dim]
+    float32, updated in place (token m uses slot slots[m], default m, at position pos[m]).  table_q None: h = x_in."""
     n_layers = len(weights_q) // 7
     ptrs = (ctypes.c_void_p * len(weights_q))(*[_ptr(np.ascontiguousarray(w)) for w in weights_q])
     norms = np.ascontiguousarray(norms, dtype=np.float32)
     qk_norms = np.ascontiguousarray(qk_norms, dtype=np.float32)
-    ids = np.ascontiguousarray(ids, dtype=np.int32)
     pos = np.ascontiguousarray(pos, dtype=np.int32)
     x_in = np.ascontiguousarray(x_in, dtype=np.float32).reshape(-1, hidden)
     assert kcache.flags.c_contiguous and vcache.flags.c_contiguous and kcache.dtype == np.float32
     m = x_in.shape[0]
+    if slots is not None:
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        assert slots.min() >= 0 and slots.max() < kcache.shape[1]
+    else:
+        assert m <= kcache.shape[1]
+    if table_q is not None:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
     h = np.empty((m, hidden), dtype=np.float32)
     lib().oracle_decoder_chain_attn(n_layers, ptrs, _ptr(norms), _ptr(qk_norms), hidden, n_head, n_kv, head_dim,
-                                    inter, eps, theta, _ptr(table_q), table_q.shape[0], _ptr(ids), _ptr(x_in),
-                                    _ptr(pos), m, kcache.shape[2], _ptr(kcache), _ptr(vcache), _ptr(h), mode, threads)
+                                    inter, eps, theta, _ptr(table_q) if table_q is not None else None,
+                                    table_q.shape[0] if table_q is not None else 0,
+                                    _ptr(ids) if table_q is not None else None, _ptr(x_in), _ptr(pos),
+                                    _ptr(slots) if slots is not None else None, m, kcache.shape[1], kcache.shape[2],
+                                    _ptr(kcache), _ptr(vcache), _ptr(h), mode, threads)
     return h
+
+
+def rms_norm_rows(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """rms_norm(x) * w per row (ggml_rms_norm: sum of squares in double, scale 1/sqrtf(mean + eps))."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, n = x.reshape(-1, x.shape[-1]).shape
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    y = np.empty((rows, n), dtype=np.float32)
+    lib().oracle_rms_norm_rows(_ptr(x), _ptr(w), _ptr(y), rows, n, eps)
+    return y
+
+
+def select_code(logits: np.ndarray, history: set | None = None, penalty: float = 1.0) -> int:
+    """The reference's greedy choice (sample == false): std::max_element over the logits after the repetition
+    penalty (src/arch/qwen3-tts/code-predictor-host.cpp:45-49,51-69,71-80), in float32, sequentially."""
+    v = np.array(logits, dtype=np.float32)
+    if history and penalty > 1.0:
+        p = np.float32(penalty)
+        for c in history:
+            if 0 <= c < v.size:
+                v[c] = v[c] / p if v[c] > 0 else v[c] * p
+    best = 0
+    for i in range(1, v.size):
+        if v[best] < v[i]:
+            best = i
+    return best
+
+
+def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.ndarray | None, prev: np.ndarray | None,
+          pos: np.ndarray, slots: np.ndarray, state: dict, *, replay: np.ndarray | None = None, penalty: float = 1.0,
+          hidden_in: np.ndarray | None = None, logits_in: np.ndarray | None = None, mode: int = QUANT_REF):
+    """One decode frame for M streams (src/arch/qwen3-tts/model.cpp:1310-1489 with request.sample == false or
+    replay codes): talker step on sum(code embeddings) + text, greedy/replayed code 0, predictor prefill over
+    [hidden, ttable[code 0]] at positions 0, 1 and G-2 single-position predictor steps.  talker / predictor: dicts
+    with mats, norms, qkn, table (talker only), out_norm, heads (list of Q8_0 arrays), hidden, n_head, n_kv,
+    head_dim, inter, eps, theta, vocab.  state: {"tk", "tv", "pk", "pv" caches, "history": {slot: set}} updated in
+    place.  hidden_in / logits_in: the talker's outputs when its step already ran (the prompt pass).
+    Returns (codes [M, G] int32, talker hidden [M, H], talker logits [M, V], predictor logits: a list of G-1
+    arrays [M, V_p], the one each acoustic code was chosen from)."""
+    T, P = talker, predictor
+    H = T["hidden"]
+    M = pos.shape[0]
+    dims = lambda c: dict(hidden=c["hidden"], n_head=c["n_head"], n_kv=c["n_kv"], head_dim=c["head_dim"],
+                          inter=c["inter"], eps=c["eps"], theta=c["theta"], mode=mode)
+    if hidden_in is None:
+        x = np.empty((M, H), np.float32)
+        for m in range(M):
+            acc = get_rows(ptables[0], H, prev[m, 1:2])[0][0]
+            for g in range(2, groups):
+                acc = (acc + get_rows(ptables[g - 1], H, prev[m, g:g + 1])[0][0]).astype(np.float32)
+            acc = (acc + get_rows(T["table"], H, prev[m, 0:1])[0][0]).astype(np.float32)
+            x[m] = (acc + text[m]).astype(np.float32)
+        h = decoder_chain_attn(T["mats"], T["norms"], T["qkn"], None, None, x, pos, state["tk"], state["tv"],
+                               slots=slots, **dims(T))
+        hid = rms_norm_rows(h, T["out_norm"], T["eps"])
+        logits = mul_mat(T["heads"][0], H, hid, mode, want_bound=False)[0]
+    else:
+        hid, logits = hidden_in, logits_in
+    codes = np.zeros((M, groups), np.int32)
+    for m in range(M):
+        if replay is not None:
+            codes[m, 0] = replay[m, 0]
+        else:
+            hist = state["history"].setdefault(int(slots[m]), set())
+            codes[m, 0] = select_code(logits[m], hist, penalty)
+            hist.add(int(codes[m, 0]))
+    # predictor prefill: two positions per stream
+    xp = np.empty((2 * M, H), np.float32)
+    xp[0::2] = hid
+    xp[1::2] = get_rows(T["table"], H, codes[:, 0])[0]
+    pp = np.tile(np.array([0, 1], np.int32), M)
+    ps = np.repeat(np.asarray(slots, np.int32), 2)
+    h = decoder_chain_attn(P["mats"], P["norms"], P["qkn"], None, None, xp, pp, state["pk"], state["pv"], slots=ps,
+                           **dims(P))
+    lg = mul_mat(P["heads"][0], H, rms_norm_rows(h[1::2], P["out_norm"], P["eps"]), mode, want_bound=False)[0]
+    plogits = [lg]
+    for m in range(M):
+        codes[m, 1] = replay[m, 1] if replay is not None else select_code(lg[m])
+    for g in range(1, groups - 1):
+        x = get_rows(ptables[g - 1], H, codes[:, g])[0]
+        h = decoder_chain_attn(P["mats"], P["norms"], P["qkn"], None, None, x, np.full(M, g + 1, np.int32),
+                               state["pk"], state["pv"], slots=slots, **dims(P))
+        lg = mul_mat(P["heads"][g], H, rms_norm_rows(h, P["out_norm"], P["eps"]), mode, want_bound=False)[0]
+        plogits.append(lg)
+        for m in range(M):
+            codes[m, g + 1] = replay[m, g + 1] if replay is not None else select_code(lg[m])
+    return codes, hid, logits, plogits
 
 
 # ---------------------------------------------------- numpy / Python restatements

@@ -488,16 +488,28 @@ void oracle_decoder_chain(int n_layers, const void * const * weights, const floa
     free(s);
 }
 
+/* Final RMS norm of each of `rows` rows (talker.cpp:169, code-predictor.cpp:66:
+ * rms_norm(hidden, model.norm.weight)). */
+void oracle_rms_norm_rows(const float * x, const float * w, float * y, int64_t rows, int64_t n, float eps) {
+    for (int64_t r = 0; r < rows; ++r) {
+        rms_norm_mul(x + r * n, w, y + r * n, n, eps);
+    }
+}
+
 /* oracle_decoder_chain with the reference's attention: per layer the q and k
  * heads are RMS-normed (qk_norms: per layer q_norm then k_norm, head_dim
  * floats each) and rotated at pos[m]; k and v go into the caches at pos[m] of
- * slot m (kcache / vcache: [n_layers][M][n_ctx][n_kv * head_dim], updated in
- * place); token m attends over cached positions 0..pos[m]. */
+ * slot slots[m] (slots == NULL: slot m; kcache / vcache:
+ * [n_layers][n_slots][n_ctx][n_kv * head_dim], updated in place); token m
+ * attends over cached positions 0..pos[m] of its slot.  Tokens are processed
+ * in order, so tokens of one slot at increasing positions see each other
+ * causally, as ggml's masked block does.  table == NULL: h = x_in. */
 void oracle_decoder_chain_attn(int n_layers, const void * const * weights, const float * norms,
                                const float * qk_norms, int64_t hidden, int64_t n_head, int64_t n_kv, int64_t head_dim,
                                int64_t inter, float eps, float rope_theta, const void * table, int64_t table_rows,
-                               const int32_t * ids, const float * x_in, const int32_t * pos, int64_t M, int64_t n_ctx,
-                               float * kcache, float * vcache, float * h_out, int mode, int threads) {
+                               const int32_t * ids, const float * x_in, const int32_t * pos, const int32_t * slots,
+                               int64_t M, int64_t n_slots, int64_t n_ctx, float * kcache, float * vcache, float * h_out,
+                               int mode, int threads) {
     const int64_t q_dim  = n_head * head_dim;
     const int64_t kv_dim = n_kv * head_dim;
     const size_t  rb_h   = (size_t) (hidden / ORACLE_QK8_0) * ORACLE_BLOCK_BYTES;
@@ -513,9 +525,13 @@ void oracle_decoder_chain_attn(int n_layers, const void * const * weights, const
     float *       g      = (float *) malloc(sizeof(float) * (size_t) (M * inter));
     float *       u      = (float *) malloc(sizeof(float) * (size_t) (M * inter));
     float *       s      = (float *) malloc(sizeof(float) * (size_t) (M * inter));
-    oracle_get_rows_q8_0(table, hidden, table_rows, ids, M, h);
-    for (int64_t i = 0; i < M * hidden; ++i) {
-        h[i] = x_in[i] + h[i];
+    if (table != NULL) {
+        oracle_get_rows_q8_0(table, hidden, table_rows, ids, M, h);
+        for (int64_t i = 0; i < M * hidden; ++i) {
+            h[i] = x_in[i] + h[i];
+        }
+    } else {
+        memcpy(h, x_in, sizeof(float) * (size_t) (M * hidden));
     }
     for (int l = 0; l < n_layers; ++l) {
         const void * const * W      = weights + 7 * l;
@@ -532,8 +548,9 @@ void oracle_decoder_chain_attn(int n_layers, const void * const * weights, const
         for (int64_t m = 0; m < M; ++m) {
             oracle_head_norm_rope(q + m * q_dim, n_head, head_dim, qn, eps, pos[m], rope_theta, 1);
             oracle_head_norm_rope(k + m * kv_dim, n_kv, head_dim, kn, eps, pos[m], rope_theta, 1);
-            float * kc = kcache + (((size_t) l * M + m) * n_ctx) * kv_dim;
-            float * vc = vcache + (((size_t) l * M + m) * n_ctx) * kv_dim;
+            const int64_t slot = slots != NULL ? slots[m] : m;
+            float * kc = kcache + (((size_t) l * n_slots + slot) * n_ctx) * kv_dim;
+            float * vc = vcache + (((size_t) l * n_slots + slot) * n_ctx) * kv_dim;
             memcpy(kc + (size_t) pos[m] * kv_dim, k + m * kv_dim, sizeof(float) * (size_t) kv_dim);
             memcpy(vc + (size_t) pos[m] * kv_dim, v + m * kv_dim, sizeof(float) * (size_t) kv_dim);
             oracle_attend(q + m * q_dim, kc, vc, (int64_t) pos[m] + 1, n_head, n_kv, head_dim, a + m * q_dim);

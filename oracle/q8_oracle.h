@@ -104,8 +104,10 @@ void oracle_attend(const float * q, const float * kc, const float * vc, int64_t 
 void oracle_decoder_chain_attn(int n_layers, const void * const * weights, const float * norms,
                                const float * qk_norms, int64_t hidden, int64_t n_head, int64_t n_kv, int64_t head_dim,
                                int64_t inter, float eps, float rope_theta, const void * table, int64_t table_rows,
-                               const int32_t * ids, const float * x_in, const int32_t * pos, int64_t M, int64_t n_ctx,
-                               float * kcache, float * vcache, float * h_out, int mode, int threads);
+                               const int32_t * ids, const float * x_in, const int32_t * pos, const int32_t * slots,
+                               int64_t M, int64_t n_slots, int64_t n_ctx, float * kcache, float * vcache, float * h_out,
+                               int mode, int threads);
+void oracle_rms_norm_rows(const float * x, const float * w, float * y, int64_t rows, int64_t n, float eps);
 int oracle_max_threads(void);
 
 #ifdef __cplusplus

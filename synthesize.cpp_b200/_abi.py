@@ -47,12 +47,37 @@ class AttentionDesc(ctypes.Structure):
                 ("q_norm", ctypes.POINTER(ctypes.c_void_p)), ("k_norm", ctypes.POINTER(ctypes.c_void_p))]
 
 
+class OutputDesc(ctypes.Structure):
+    _fields_ = [("norm", ctypes.c_void_p), ("heads", ctypes.POINTER(ctypes.c_void_p)), ("n_heads", ctypes.c_int32),
+                ("vocab", ctypes.c_int64)]
+
+
 class ChainDesc(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int32), ("hidden", ctypes.c_int64), ("n_head", ctypes.c_int64),
                 ("n_kv", ctypes.c_int64), ("head_dim", ctypes.c_int64), ("inter", ctypes.c_int64),
                 ("eps", ctypes.c_float), ("max_m", ctypes.c_int64), ("mode", ctypes.c_int32),
                 ("layers", ctypes.POINTER(Layer)), ("table", ctypes.c_void_p), ("table_rows", ctypes.c_int64),
-                ("attention", ctypes.POINTER(AttentionDesc))]
+                ("attention", ctypes.POINTER(AttentionDesc)), ("output", ctypes.POINTER(OutputDesc))]
+
+
+class StepArgs(ctypes.Structure):
+    _fields_ = [("M", ctypes.c_int64), ("ids", ctypes.c_void_p), ("table", ctypes.c_void_p),
+                ("table_rows", ctypes.c_int64), ("x_in", ctypes.c_void_p), ("pos", ctypes.c_void_p),
+                ("slots", ctypes.c_void_p), ("h_out", ctypes.c_void_p), ("hidden_out", ctypes.c_void_p),
+                ("logits", ctypes.c_void_p), ("head", ctypes.c_int32)]
+
+
+class FrameDesc(ctypes.Structure):
+    _fields_ = [("talker", ctypes.c_void_p), ("predictor", ctypes.c_void_p), ("groups", ctypes.c_int32),
+                ("tables", ctypes.POINTER(ctypes.c_void_p)), ("table_rows", ctypes.c_int64),
+                ("repetition_penalty", ctypes.c_float)]
+
+
+class FrameArgs(ctypes.Structure):
+    _fields_ = [("M", ctypes.c_int64), ("skip_talker", ctypes.c_int32), ("text", ctypes.c_void_p),
+                ("prev", ctypes.c_void_p), ("pos", ctypes.c_void_p), ("slots", ctypes.c_void_p),
+                ("replay", ctypes.c_void_p), ("codes", ctypes.c_void_p), ("hidden", ctypes.c_void_p),
+                ("talker_logits", ctypes.c_void_p)]
 
 
 def header_symbols(header: str = HEADER) -> list[str]:
@@ -108,6 +133,16 @@ def lib() -> ctypes.CDLL:
     L.b200q8_chain_buffer.restype = i32
     L.b200q8_chain_destroy.argtypes = [vp]
     L.b200q8_chain_destroy.restype = None
+    L.b200q8_chain_step.argtypes = [vp, ctypes.POINTER(StepArgs), vp]
+    L.b200q8_chain_step.restype = i32
+    L.b200q8_frame_create.argtypes = [ctypes.POINTER(FrameDesc), ctypes.POINTER(vp)]
+    L.b200q8_frame_create.restype = i32
+    L.b200q8_frame_run.argtypes = [vp, ctypes.POINTER(FrameArgs), vp]
+    L.b200q8_frame_run.restype = i32
+    L.b200q8_frame_reset_history.argtypes = [vp, i32, vp]
+    L.b200q8_frame_reset_history.restype = i32
+    L.b200q8_frame_destroy.argtypes = [vp]
+    L.b200q8_frame_destroy.restype = None
     _lib = L
     return L
 

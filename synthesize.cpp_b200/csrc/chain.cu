@@ -10,14 +10,17 @@
 //               gu   = W_gu * Q(rms_norm(h1) * norm_post)    (one GEMV, 6144 rows)
 //               h    = h1 + W_d * Q(silu(g) * u)             (GEMV + residual)
 //
-// where attend is attention over a single cached position: the softmax of
-// one score is 1, so query head j reads kv head j / (n_head / n_kv).  The
-// norms, the GQA expansion and SwiGLU are folded into the prologue of the
-// GEMV that consumes them, the residual adds into its epilogue, so the step
-// is 1 + 4 * n_layers kernels.  They are launched with programmatic
-// dependent launch (each GEMV streams its weights into shared memory before
-// waiting on its predecessor) and captured once per (M, pointer set) into a
-// CUDA graph that run() replays.
+// where attend is either attention over a single cached position (the
+// softmax of one score is 1, so query head j reads kv head j / (n_head /
+// n_kv)) or, for chains built with an attention desc, the reference's
+// attention over a per-slot KV cache (attention.cu).  The norms, the GQA
+// expansion and SwiGLU are folded into the prologue of the GEMV that consumes
+// them, the residual adds into its epilogue, so the step is 1 + 4 * n_layers
+// kernels (+ 2 per layer with attention, + 1 with an output head).  They are
+// launched with programmatic dependent launch (each GEMV streams its weights
+// into shared memory before waiting on its predecessor) and captured once per
+// argument set into a CUDA graph that run() replays.
+#include "chain.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -34,6 +37,8 @@ int             current_sm_count();
 
 namespace {
 
+// h = x_in + get_rows(table, ids); a NULL ids or x_in drops that term (the
+// other is copied exactly).
 __global__ void embed_add_kernel(const uint8_t * __restrict__ table, size_t table_stride, int64_t table_rows,
                                  const int32_t * __restrict__ ids, const float * __restrict__ x_in,
                                  float * __restrict__ h, int64_t M, int64_t H) {
@@ -41,6 +46,10 @@ __global__ void embed_add_kernel(const uint8_t * __restrict__ table, size_t tabl
     for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t) gridDim.x * blockDim.x) {
         const int64_t m = i / H;
         const int64_t k = i % H;
+        if (ids == nullptr) {
+            h[i] = x_in[i];
+            continue;
+        }
         const int64_t r = ids[m];
         float         e = 0.0f;
         if (r < 0 || r >= table_rows) {
@@ -52,7 +61,7 @@ __global__ void embed_add_kernel(const uint8_t * __restrict__ table, size_t tabl
             const float     d   = __half2float(__ushort_as_half((unsigned short) (blk[0] | (blk[1] << 8))));
             e                   = __fmul_rn((float) (int8_t) blk[2 + k % kQK], d);
         }
-        h[i] = __fadd_rn(x_in[i], e);
+        h[i] = x_in != nullptr ? __fadd_rn(x_in[i], e) : e;
     }
 }
 
@@ -96,14 +105,17 @@ struct b200q8_chain {
     float *                      q_rot        = nullptr;  // [max_m][Q]
     float *                      attn_partial = nullptr;  // [max_m][n_head][kAttnMaxSplits][head_dim + 2]
     unsigned *                   attn_count   = nullptr;  // [max_m][n_head]
+    // output stage (desc.output != nullptr)
+    int                          n_heads      = 0;
+    const float *                out_norm     = nullptr;
+    std::vector<const uint8_t *> heads;
+    int64_t                      vocab        = 0;
+    float *                      h_last       = nullptr;  // [max_m][hidden] when the caller passes no h_out
+    float *                      hid          = nullptr;  // [max_m][hidden] when the caller passes no hidden_out
+    float *                      lg           = nullptr;  // [max_m][vocab] when the caller passes no logits
 
     struct Graph {
-        int64_t         M;
-        const void *    ids;
-        const void *    x;
-        void *          h;
-        const void *    pos;
-        const void *    slots;
+        StepIO          io;
         cudaGraphExec_t exec;
     };
 
@@ -191,9 +203,11 @@ const uint8_t * contiguous(b200q8_chain * c, const void * a, size_t a_bytes, con
 // M > 8: per op, a per-token prologue kernel (norm / GQA / SwiGLU + residual,
 // quantized into code and scale planes) then the int8 tensor-core GEMM;
 // 2 launches per op with programmatic dependent launch between them.
-cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, int64_t M, const int32_t * pos,
-                                 const int32_t * slots, float * h_out) {
+cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, const StepIO & io) {
     const b200q8_chain_desc & d = c->d;
+    const int64_t   M = io.M;
+    const int32_t * pos = io.pos, * slots = io.slots;
+    float *         h_out = io.h_out;
     const int64_t H = d.hidden, Q = d.n_head * d.head_dim, KV = d.n_kv * d.head_dim, I = d.inter;
     const int     hd = (int) d.head_dim, grp = (int) (d.n_head / d.n_kv);
     uint8_t *     xrec = static_cast<uint8_t *>(c->planes);
@@ -246,25 +260,35 @@ cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, int64_t M, c
         e           = launch_residual_rows(c->buf(L, kH1), c->buf(L, kDown), (size_t) H, h_out, (size_t) H, (int) H, M,
                                            st, true);
     }
+    // output: hidden = rms_norm(h) * norm, logits = head * Q(hidden)
+    if (e == cudaSuccess && io.hidden_out != nullptr) {
+        e = launch_stage_rows(0, h_out, nullptr, (size_t) H, nullptr, 0, c->out_norm, d.eps, (int) H, hd, grp,
+                              io.hidden_out, (size_t) H, M, d.mode, xrec, st, true);
+        if (e == cudaSuccess)
+            e = launch_gemm_staged(c->heads[io.head], c->rb_h, H, c->vocab, xrec, M, io.logits, (size_t) c->vocab, st,
+                                   c->sms, true);
+    }
     return e;
 }
 
-cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, int64_t M, const int32_t * ids, const float * x_in,
-                         const int32_t * pos, const int32_t * slots, float * h_out) {
+cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, const StepIO & io) {
     const b200q8_chain_desc & d = c->d;
     const int64_t H = d.hidden, Q = d.n_head * d.head_dim, KV = d.n_kv * d.head_dim, I = d.inter;
+    const int64_t   M = io.M;
+    const int32_t * pos = io.pos, * slots = io.slots;
+    float *         h_out = io.h_out;
     {
         const int64_t total = M * H;
         const int     grid  = (int) std::min<int64_t>((total + 255) / 256, (int64_t) c->sms * 4);
-        embed_add_kernel<<<grid, 256, 0, st>>>(static_cast<const uint8_t *>(d.table), (size_t) c->rb_h,
-                                                d.table_rows, ids, x_in, c->h0, M, H);
+        embed_add_kernel<<<grid, 256, 0, st>>>(io.table, (size_t) c->rb_h, io.table_rows, io.ids, io.x_in, c->h0, M,
+                                                H);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) {
             return e;
         }
     }
     if (M > 8 && c->planes != nullptr) {
-        return enqueue_step_batched(c, st, M, pos, slots, h_out);
+        return enqueue_step_batched(c, st, io);
     }
     for (int64_t m0 = 0; m0 < M; m0 += 8) {
         const int   mc = (int) std::min<int64_t>(M - m0, 8);
@@ -315,18 +339,32 @@ cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, int64_t M, const int
             if (e != cudaSuccess) return e;
             h = p.y_res;
         }
+        if (io.hidden_out != nullptr) {
+            // hidden = rms_norm(h) * norm (written by the prologue), logits = head * Q(hidden)
+            GemvParams p = {};
+            p.M = mc; p.mode = d.mode; p.eps = d.eps;
+            p.w = c->heads[io.head]; p.row_bytes = c->rb_h; p.K = (int) H; p.N = (int) c->vocab;
+            p.pro = kProRmsNorm; p.x = h; p.x_stride = (size_t) H; p.norm_w = c->out_norm;
+            p.pro_out = io.hidden_out + m0 * H; p.pro_out_stride = (size_t) H;
+            p.y = io.logits + m0 * c->vocab; p.y_stride = (size_t) c->vocab;
+            const cudaError_t e = launch_gemv(p, st, c->sms, true);
+            if (e != cudaSuccess) return e;
+        }
     }
     return cudaSuccess;
 }
 
-// The step as a CUDA graph, captured once per (M, buffers) and replayed.
-b200q8_status_t run_graph(b200q8_chain * c, const int32_t * ids, const float * x_in, const int32_t * pos,
-                          const int32_t * slots, float * h_out, int64_t M, b200q8_stream_t stream) {
+// The step as a CUDA graph, captured once per argument set and replayed
+// (the most recently used kMaxGraphs are kept).
+constexpr size_t kMaxGraphs = 64;
+
+b200q8_status_t run_graph(b200q8_chain * c, const StepIO & io, b200q8_stream_t stream) {
     cudaError_t     e    = cudaSuccess;
     cudaGraphExec_t exec = nullptr;
-    for (auto & g : c->graphs) {
-        if (g.M == M && g.ids == ids && g.x == x_in && g.h == h_out && g.pos == pos && g.slots == slots) {
-            exec = g.exec;
+    for (size_t i = 0; i < c->graphs.size(); ++i) {
+        if (same_io(c->graphs[i].io, io)) {
+            exec = c->graphs[i].exec;
+            std::rotate(c->graphs.begin() + i, c->graphs.begin() + i + 1, c->graphs.end());  // most recent last
             break;
         }
     }
@@ -334,7 +372,7 @@ b200q8_status_t run_graph(b200q8_chain * c, const int32_t * ids, const float * x
         cudaGraph_t graph = nullptr;
         e                 = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal);
         if (e == cudaSuccess) {
-            cudaError_t e2 = enqueue_step(c, c->cap_stream, M, ids, x_in, pos, slots, h_out);
+            cudaError_t e2 = enqueue_step(c, c->cap_stream, io);
             e              = cudaStreamEndCapture(c->cap_stream, &graph);
             if (e2 != cudaSuccess) {
                 e = e2;
@@ -349,11 +387,11 @@ b200q8_status_t run_graph(b200q8_chain * c, const int32_t * ids, const float * x
         if (e != cudaSuccess) {
             return cuda_error(e, "chain_run: graph capture");
         }
-        if (c->graphs.size() >= 8) {
+        if (c->graphs.size() >= kMaxGraphs) {
             cudaGraphExecDestroy(c->graphs.front().exec);
             c->graphs.erase(c->graphs.begin());
         }
-        c->graphs.push_back({ M, ids, x_in, h_out, pos, slots, exec });
+        c->graphs.push_back({ io, exec });
     }
     e = cudaGraphLaunch(exec, reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_run: graph launch");
@@ -396,9 +434,29 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
             }
         }
     }
+    if (d.output != nullptr) {
+        const b200q8_output_desc & od = *d.output;
+        if (od.norm == nullptr || od.heads == nullptr || od.n_heads < 1 || od.vocab < 16 || od.vocab > (1 << 24)) {
+            return set_error(B200Q8_ERR_INVALID_ARG, "chain_create: bad output desc (norm, heads, n_heads >= 1, "
+                                                     "vocab in [16, 2^24])");
+        }
+        for (int i = 0; i < od.n_heads; ++i) {
+            if (od.heads[i] == nullptr) {
+                return set_error(B200Q8_ERR_INVALID_ARG, "chain_create: output head %d is null", i);
+            }
+        }
+    }
     b200q8_chain * c = new (std::nothrow) b200q8_chain();
     if (c == nullptr) {
         return set_error(B200Q8_ERR_OOM, "chain_create: out of host memory");
+    }
+    if (d.output != nullptr) {
+        c->n_heads  = d.output->n_heads;
+        c->out_norm = d.output->norm;
+        c->vocab    = d.output->vocab;
+        for (int i = 0; i < c->n_heads; ++i) {
+            c->heads.push_back(static_cast<const uint8_t *>(d.output->heads[i]));
+        }
     }
     if (d.attention != nullptr) {
         c->attn = true;
@@ -413,6 +471,7 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
     c->layers.assign(d.layers, d.layers + d.n_layers);
     c->d.layers    = nullptr;
     c->d.attention = nullptr;
+    c->d.output    = nullptr;
     int prev    = 0;
     cudaGetDevice(&prev);
     cudaError_t e = cudaSetDevice(device);
@@ -460,7 +519,24 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
     if (e == cudaSuccess) {
         e = cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking);
     }
+    // default output buffers: [max_m][hidden] twice, [max_m][vocab]
+    if (e == cudaSuccess) {
+        const size_t hm = (size_t) (H * d.max_m + 63) / 64 * 64;
+        const size_t vm = c->n_heads > 0 ? (size_t) (c->vocab * d.max_m + 63) / 64 * 64 : 0;
+        void *       p  = nullptr;
+        e               = cudaMalloc(&p, (2 * hm + vm) * sizeof(float));
+        if (e == cudaSuccess) {
+            c->owned.push_back(p);
+            c->h_last = static_cast<float *>(p);
+            c->hid    = c->h_last + hm;
+            c->lg     = vm ? c->hid + hm : nullptr;
+            e         = cudaMemset(p, 0, (2 * hm + vm) * sizeof(float));
+        }
+    }
     bool batched_ok = d.max_m > 8 && d.head_dim % 4 == 0;
+    for (int i = 0; i < c->n_heads && batched_ok; ++i) {
+        batched_ok = gemm_supported(c->heads[i], c->rb_h, H, c->vocab, d.max_m);
+    }
     for (int l = 0; l < d.n_layers && batched_ok; ++l) {
         batched_ok = gemm_supported(c->w_qkv[l], c->rb_h, H, c->qkv_dim, d.max_m) &&
                      gemm_supported(c->w_o[l], c->rb_q, Q, H, d.max_m) &&
@@ -529,6 +605,10 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
         p.w = c->w_gu[l]; p.N = (int) (2 * I); ok = ok && gemv_supported(p);
         p.w = c->w_o[l]; p.row_bytes = c->rb_q; p.K = (int) Q; p.N = (int) H; ok = ok && gemv_supported(p);
         p.w = c->w_d[l]; p.row_bytes = c->rb_i; p.K = (int) I; ok = ok && gemv_supported(p);
+        for (int i = 0; i < c->n_heads && l == 0; ++i) {
+            p.w = c->heads[i]; p.row_bytes = c->rb_h; p.K = (int) H; p.N = (int) c->vocab;
+            ok = ok && gemv_supported(p);
+        }
         if (!ok) {
             cudaSetDevice(prev);
             chain_free(c);
@@ -588,7 +668,10 @@ b200q8_status_t b200q8_chain_run(b200q8_chain * c, const int32_t * ids, const fl
             return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_run: persistent step launch");
         }
     }
-    const b200q8_status_t st = run_graph(c, ids, x_in, nullptr, nullptr, h_out, M, stream);
+    StepIO io;
+    io.M = M; io.ids = ids; io.x_in = x_in; io.h_out = h_out;
+    io.table = static_cast<const uint8_t *>(c->d.table); io.table_rows = c->d.table_rows;
+    const b200q8_status_t st = run_graph(c, io, stream);
     cudaSetDevice(prev);
     return st;
 }
@@ -612,7 +695,30 @@ b200q8_status_t b200q8_chain_run_at(b200q8_chain * c, const int32_t * ids, const
     if (e != cudaSuccess) {
         return cuda_error(e, "chain_run_at: cudaSetDevice");
     }
-    const b200q8_status_t st = run_graph(c, ids, x_in, pos, slots, h_out, M, stream);
+    StepIO io;
+    io.M = M; io.ids = ids; io.x_in = x_in; io.pos = pos; io.slots = slots; io.h_out = h_out;
+    io.table = static_cast<const uint8_t *>(c->d.table); io.table_rows = c->d.table_rows;
+    const b200q8_status_t st = run_graph(c, io, stream);
+    cudaSetDevice(prev);
+    return st;
+}
+
+b200q8_status_t b200q8_chain_step(b200q8_chain * c, const b200q8_step_args * a, b200q8_stream_t stream) {
+    if (c == nullptr || a == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_step: null argument");
+    }
+    StepIO                io;
+    const b200q8_status_t v = chain_resolve(c, *a, io);
+    if (v != B200Q8_OK) {
+        return v;
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) {
+        return cuda_error(e, "chain_step: cudaSetDevice");
+    }
+    const b200q8_status_t st = run_graph(c, io, stream);
     cudaSetDevice(prev);
     return st;
 }
@@ -675,3 +781,74 @@ void b200q8_chain_destroy(b200q8_chain * c) {
 }
 
 }  // extern "C"
+
+namespace b200q8 {
+
+ChainInfo chain_info(const b200q8_chain * c) {
+    ChainInfo i  = {};
+    i.device     = c->device;
+    i.sms        = c->sms;
+    i.hidden     = c->d.hidden;
+    i.max_m      = c->d.max_m;
+    i.attn       = c->attn;
+    i.n_ctx      = c->attn ? c->ad.n_ctx : 0;
+    i.n_slots    = c->attn ? c->ad.n_slots : 0;
+    i.n_heads    = c->n_heads;
+    i.vocab      = c->vocab;
+    i.table      = static_cast<const uint8_t *>(c->d.table);
+    i.table_rows = c->d.table_rows;
+    return i;
+}
+
+b200q8_status_t chain_resolve(b200q8_chain * c, const b200q8_step_args & a, StepIO & io) {
+    if (a.M < 1 || a.M > c->d.max_m) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_step: M (%lld) must be in [1, max_m]", (long long) a.M);
+    }
+    if (a.ids == nullptr && a.x_in == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_step: needs ids, x_in or both");
+    }
+    if (a.ids != nullptr && a.table != nullptr && a.table_rows < 1) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_step: a table needs table_rows >= 1");
+    }
+    if (a.table != nullptr && reinterpret_cast<uintptr_t>(a.table) % 2 != 0) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_step: table must be 2-byte aligned");
+    }
+    if (c->attn != (a.pos != nullptr)) {
+        return set_error(B200Q8_ERR_INVALID_ARG, c->attn ? "chain_step: this chain has attention and needs pos"
+                                                         : "chain_step: pos given to a chain without attention");
+    }
+    if (c->attn && a.slots == nullptr && a.M > c->ad.n_slots) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_step: M (%lld) tokens need explicit slots beyond n_slots",
+                         (long long) a.M);
+    }
+    const bool out = a.hidden_out != nullptr || a.logits != nullptr;
+    if (out && c->n_heads == 0) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_step: the chain was built without an output desc");
+    }
+    if (out && (a.head < 0 || a.head >= c->n_heads)) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "chain_step: head %d outside [0, %d)", a.head, c->n_heads);
+    }
+    io            = StepIO();
+    io.M          = a.M;
+    io.ids        = a.ids;
+    io.table      = a.ids == nullptr ? nullptr
+                    : a.table != nullptr ? static_cast<const uint8_t *>(a.table)
+                                         : static_cast<const uint8_t *>(c->d.table);
+    io.table_rows = a.ids == nullptr ? 0 : a.table != nullptr ? a.table_rows : c->d.table_rows;
+    io.x_in       = a.x_in;
+    io.pos        = a.pos;
+    io.slots      = a.slots;
+    io.h_out      = a.h_out != nullptr ? a.h_out : c->h_last;
+    if (out) {
+        io.hidden_out = a.hidden_out != nullptr ? a.hidden_out : c->hid;
+        io.logits     = a.logits != nullptr ? a.logits : c->lg;
+        io.head       = a.head;
+    }
+    return B200Q8_OK;
+}
+
+cudaError_t chain_enqueue(b200q8_chain * c, cudaStream_t st, const StepIO & io) {
+    return enqueue_step(c, st, io);
+}
+
+}  // namespace b200q8

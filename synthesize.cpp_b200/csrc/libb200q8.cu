@@ -10,3 +10,4 @@
 #include "pack_host.cu"
 #include "noalloc.cu"
 #include "gguf.cu"
+#include "frame.cu"

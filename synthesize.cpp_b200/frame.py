@@ -1,0 +1,56 @@
+"""One decode frame of Qwen3-TTS (talker + code predictor) on the device (b200q8_frame_*).
+
+Mirrors the reference's per-frame loop (src/arch/qwen3-tts/model.cpp:1310-1489) with greedy selection
+(request.sample == false) or replayed codes: one run() is the talker step and the code predictor's
+code_group_count - 1 calls for M streams, replayed as one CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._abi import FrameArgs, FrameDesc, check, lib
+from .chain import DecodeChain
+from .q8 import stream_ptr
+
+
+class Frame:
+    """talker / predictor: DecodeChain objects built with attention and output descs; tables: the predictor's
+    G-1 codec tables (uint8 Q8_0 [rows, hidden/32*34] CUDA tensors)."""
+
+    def __init__(self, talker: DecodeChain, predictor: DecodeChain, tables: list[torch.Tensor], *,
+                 repetition_penalty: float = 1.0):
+        self._keep = (talker, predictor, tables)
+        self.groups = len(tables) + 1
+        arr = (ctypes.c_void_p * len(tables))(*[t.data_ptr() for t in tables])
+        desc = FrameDesc(talker._h, predictor._h, self.groups, ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)),
+                         tables[0].shape[0], repetition_penalty)
+        handle = ctypes.c_void_p()
+        check(lib().b200q8_frame_create(ctypes.byref(desc), ctypes.byref(handle)))
+        self._h = handle
+
+    def run(self, codes: torch.Tensor, *, text: torch.Tensor | None = None, prev: torch.Tensor | None = None,
+            pos: torch.Tensor | None = None, slots: torch.Tensor | None = None, replay: torch.Tensor | None = None,
+            hidden: torch.Tensor | None = None, talker_logits: torch.Tensor | None = None,
+            skip_talker: bool = False) -> torch.Tensor:
+        """codes: int32 [M, G] out.  Without skip_talker: text [M, hidden], prev [M, G], pos [M]."""
+        p = lambda t: t.data_ptr() if t is not None else None
+        a = FrameArgs(codes.shape[0], 1 if skip_talker else 0, p(text), p(prev), p(pos), p(slots), p(replay),
+                      p(codes), p(hidden), p(talker_logits))
+        check(lib().b200q8_frame_run(self._h, ctypes.byref(a), stream_ptr()))
+        return codes
+
+    def reset_history(self, slot: int = -1) -> None:
+        check(lib().b200q8_frame_reset_history(self._h, slot, stream_ptr()))
+
+    def close(self) -> None:
+        if self._h:
+            lib().b200q8_frame_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -46,6 +46,13 @@ def chain_mod(pkg):
 
 
 @pytest.fixture(scope="session")
+def frame_mod(pkg):
+    import importlib
+
+    return importlib.import_module(__graft_entry__.PKG_NAME + ".frame")
+
+
+@pytest.fixture(scope="session")
 def dev():
     import torch
 
