@@ -41,7 +41,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b", "gemv", "gemv-large", "mul-mat"],
+    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b", "gemv", "gemv-large", "mul-mat",
+                             "frame"],
                     help="talker: BASELINE config 2 (config 3 with --batch 16/64/256); talker-1.7b: config 4 shapes; "
                          "dp-sweep: config 5, 512 streams split over the ranks in M=64 batches; "
                          "pack-1.7b: config 4 packing of all 1.4 B weights (synthesize-quantize); "
@@ -163,9 +164,232 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
+def frame_positions(i: int, prompt: int, window: int) -> int:
+    """Talker position of frame i in the frame workload: frames cycle over positions prompt .. prompt+window-1."""
+    return prompt + i % window
+
+
+FRAME_PROMPT, FRAME_WINDOW = 64, 256
+
+
+def oracle_frames_per_s(O, tref, pref, ptables, fs, m, threads, budget_s, max_frames):
+    """Greedy frames of the oracle restatement (ggml-cpu's Q8_0 arithmetic and the reference's attention in C) on
+    the host cores, at talker positions cycling like the GPU arm's; returns (frames/s, frames, seconds)."""
+    import numpy as np
+
+    KV, G = fs.talker.kv_dim, fs.groups
+    n_ctx = FRAME_PROMPT + FRAME_WINDOW
+    state = dict(tk=np.zeros((fs.talker.n_layers, m, n_ctx, KV), np.float32),
+                 tv=np.zeros((fs.talker.n_layers, m, n_ctx, KV), np.float32),
+                 pk=np.zeros((fs.predictor.n_layers, m, G, KV), np.float32),
+                 pv=np.zeros((fs.predictor.n_layers, m, G, KV), np.float32), history={})
+    rng = np.random.default_rng(0)
+    text = rng.standard_normal((m, fs.talker.hidden)).astype(np.float32)
+    prev = np.zeros((m, G), np.int32)
+    slots = np.arange(m, dtype=np.int32)
+
+    def one(i):
+        nonlocal prev
+        pos = np.full(m, frame_positions(i, FRAME_PROMPT, FRAME_WINDOW), np.int32)
+        prev = O.frame(tref, pref, ptables, G, text, prev, pos, slots, state, threads=threads)[0]
+
+    one(0)
+    t0 = time.perf_counter()
+    one(1)
+    per = time.perf_counter() - t0
+    n = max(1, min(max_frames, int(budget_s / max(per, 1e-6))))
+    t0 = time.perf_counter()
+    for i in range(n):
+        one(2 + i)
+    dt = time.perf_counter() - t0
+    return n * m / dt, n, dt
+
+
+def run_reference_frame(args, rank):
+    """Reference arm of the frame workload: the oracle's greedy frames (the reference's own CPU code path for a
+    frame is ggml-cpu, absent from its tree) on all host threads, rank 0 only."""
+    import torch
+
+    import __graft_entry__ as g
+
+    g.load_package()
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from synthesize_cpp_b200.workloads import FRAME_06B, build_frame_model, frame_host_copy
+
+    if not torch.cuda.is_available():
+        raise RuntimeError("the frame workload builds its weights on the device")
+    fm = build_frame_model(FRAME_06B, torch.device("cuda", 0))
+    tref, pref, ptables = frame_host_copy(fm)
+    threads = host_threads()
+    value, n, dt = oracle_frames_per_s(O, tref, pref, ptables, FRAME_06B, args.batch, threads, 120.0, args.steps)
+    sample = (f"{n} of {args.steps} greedy frames at M={args.batch} (28-layer talker + 15 predictor calls; oracle C "
+              f"port, OpenMP {threads} threads)")
+    line = {
+        "impl": "reference", "metric": "Qwen3-TTS decode frames (talker + code predictor, greedy)", "value": value,
+        "unit": "frames/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * dt / n, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8xint8->int32, f32 scale; f32 attention",
+        "data": "synthetic (seeded N(0,1) stream of src/random-stream.cpp)",
+        "config": {"workload": f"qwen3-tts-0.6b decode frame, M={args.batch}", "batch": args.batch},
+        "cpu_baseline": {"value": value, "unit": "frames/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_frame(args, rank, local_rank):
+    """A Qwen3-TTS decode frame on the device (b200q8_frame_run): the 28-layer talker step with the reference's
+    attention, its codec head and greedy choice, then the code predictor's prefill and 14 steps (5 layers each,
+    one head and one codec table per group), for M streams per GPU; replicas across GPUs."""
+    import torch
+
+    import __graft_entry__ as g
+
+    g.load_package()
+    from synthesize_cpp_b200 import chain as chain_mod
+    from synthesize_cpp_b200 import dp as dpu
+    from synthesize_cpp_b200 import frame as frame_mod
+    from synthesize_cpp_b200 import q8
+    from synthesize_cpp_b200.workloads import FRAME_06B, build_frame_model, frame_host_copy
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dpu.init("nccl", timeout_s=300.0, device=dev)
+    fs, m = FRAME_06B, args.batch
+    fm = build_frame_model(fs, dev)
+    n_ctx = FRAME_PROMPT + FRAME_WINDOW
+    mk = lambda dm, out, max_m, ctx: chain_mod.DecodeChain(
+        dm.layers, dm.table, hidden=dm.shape.hidden, n_head=dm.shape.n_head, n_kv=dm.shape.n_kv,
+        head_dim=dm.shape.head_dim, inter=dm.shape.inter, eps=dm.shape.eps, max_m=max_m,
+        attention=dict(rope_theta=fs.rope_theta, n_ctx=ctx, n_slots=m), output=out)
+    talker = mk(fm.talker, fm.t_out, max(8, m), n_ctx)
+    pred = mk(fm.predictor, fm.p_out, max(8, 2 * m), fs.groups)
+    fr = frame_mod.Frame(talker, pred, fm.ptables)
+    G, H = fs.groups, fs.talker.hidden
+    rng = torch.Generator().manual_seed(1234 + rank)
+    text_host = torch.randn((m, H), generator=rng).pin_memory()
+    text = text_host.to(dev)
+    codes = [torch.zeros((m, G), dtype=torch.int32, device=dev) for _ in range(2)]
+    codes_host = torch.empty((m, G), dtype=torch.int32).pin_memory()
+    pos = torch.full((m,), FRAME_PROMPT, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    state = {"i": 0}
+
+    def frame(e2e=False):
+        i = state["i"]
+        if i % FRAME_WINDOW == 0:
+            pos.fill_(FRAME_PROMPT)
+        else:
+            pos.add_(1)
+        if e2e:
+            text.copy_(text_host, non_blocking=True)
+        fr.run(codes[(i + 1) & 1], text=text, prev=codes[i & 1], pos=pos)
+        if e2e:
+            codes_host.copy_(codes[(i + 1) & 1], non_blocking=True)
+        state["i"] = i + 1
+
+    def barrier_sync():
+        torch.cuda.synchronize(dev)
+        dpu.barrier(dev)
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        frame()
+    barrier_sync()
+    if q8.device_status(local_rank) != 0:
+        raise RuntimeError("device status set during warm-up")
+    first = state["i"]
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    time.sleep(0.3)
+    barrier_sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        frame()
+    e1.record(stream)
+    barrier_sync()
+    t_dev = dpu.max_over_ranks(e0.elapsed_time(e1) / 1e3, dev)
+    clocks = sampler.stop()
+    barrier_sync()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        frame(e2e=True)
+    f1.record(stream)
+    barrier_sync()
+    t_e2e = dpu.max_over_ranks(f0.elapsed_time(f1) / 1e3, dev)
+    if q8.device_status(local_rank) != 0:
+        raise RuntimeError("device status set during the timed region")
+
+    positions = [frame_positions(i, FRAME_PROMPT, FRAME_WINDOW) for i in range(first, first + args.steps)]
+    mean_pos = sum(positions) / len(positions)
+    frames = world * m * args.steps
+    frame_s = t_dev / args.steps
+    peaks, peak_kind = measured_peaks()
+    fbytes = fs.frame_bytes(m, mean_pos)
+    achieved = fbytes / frame_s / 1e9
+
+    def chain_launches(layers, mm):
+        return 1 + (6 * layers + 1 if mm <= 8 else 10 * layers + 3)
+
+    per_frame = (2 + chain_launches(fs.talker.n_layers, m) + 2 + chain_launches(fs.predictor.n_layers, 2 * m) + 1 +
+                 (G - 2) * (chain_launches(fs.predictor.n_layers, m) + 1))
+    line = {
+        "metric": "Qwen3-TTS decode frames (talker + code predictor, greedy)", "value": frames / t_dev,
+        "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": 1e3 * frame_s, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8xint8->int32, f32 scale (Q8_0 x F32); f32 attention",
+        "data": "synthetic (seeded N(0,1) stream of src/random-stream.cpp; weights 0.02*N, packed on device)",
+        "config": {"workload": f"qwen3-tts-0.6b decode frame: 28-layer talker + {G - 1} code-predictor calls "
+                               f"(5 layers), greedy, M={m} streams per GPU, talker positions "
+                               f"{FRAME_PROMPT}..{FRAME_PROMPT + FRAME_WINDOW - 1} cycling (mean {mean_pos:.0f})",
+                   "batch_per_gpu": m, "global_batch": world * m, "groups": G,
+                   "parallelism": f"replicas x{world} (no collectives)",
+                   "l2": "inputs larger than L2: 1.76 GB of weights streamed per frame",
+                   "weight_bytes_per_frame": fs.weight_bytes(), "algorithmic_bytes_per_frame": fbytes,
+                   "int8_ops_per_frame": fs.frame_ops(m),
+                   "position_update": "one torch fill_/add_ of the [M] position vector per frame"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic(f"frame-m{m}"),
+                     "kernel": "the frame's CUDA graph (GEMV/GEMM + attention + selection kernels)",
+                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                     "int8_tops": fs.frame_ops(m) / frame_s / 1e12},
+        "e2e": {"value": frames / t_e2e, "unit": "frames/s", "h2d_bytes_per_step": m * H * 4,
+                "d2h_bytes_per_step": m * G * 4},
+        "gpu_launches": per_frame * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+
+        tref, pref, ptables = frame_host_copy(fm)
+        threads = host_threads()
+        v, n, dt = oracle_frames_per_s(O, tref, pref, ptables, fs, min(m, 8), threads, 12.0, 400)
+        line["cpu_baseline"] = {"value": v, "unit": "frames/s", "cores": threads, "kind": "port",
+                                "sample": f"{n} greedy frames at M={min(m, 8)} ({dt:.1f} s; oracle C port, OpenMP)"}
+    fr.close()
+    talker.close()
+    pred.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_reference(args, rank):
     """The reference's CPU path for the same step: rank 0 only, all host threads."""
     if rank != 0:
+        return
+    if args.workload == "frame":
+        run_reference_frame(args, rank)
         return
     import numpy as np
     import torch  # noqa: F401  (keeps the same import cost profile as our arm)
@@ -447,6 +671,9 @@ def main():
         return
     if args.workload in ("gemv", "gemv-large", "mul-mat"):
         run_mul_mat(args, rank, local_rank)
+        return
+    if args.workload == "frame":
+        run_frame(args, rank, local_rank)
         return
 
     import torch

@@ -296,7 +296,8 @@ def select_code(logits: np.ndarray, history: set | None = None, penalty: float =
 
 def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.ndarray | None, prev: np.ndarray | None,
           pos: np.ndarray, slots: np.ndarray, state: dict, *, replay: np.ndarray | None = None, penalty: float = 1.0,
-          hidden_in: np.ndarray | None = None, logits_in: np.ndarray | None = None, mode: int = QUANT_REF):
+          hidden_in: np.ndarray | None = None, logits_in: np.ndarray | None = None, mode: int = QUANT_REF,
+          threads: int = 0):
     """One decode frame for M streams (src/arch/qwen3-tts/model.cpp:1310-1489 with request.sample == false or
     replay codes): talker step on sum(code embeddings) + text, greedy/replayed code 0, predictor prefill over
     [hidden, ttable[code 0]] at positions 0, 1 and G-2 single-position predictor steps.  talker / predictor: dicts
@@ -309,7 +310,7 @@ def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.nd
     H = T["hidden"]
     M = pos.shape[0]
     dims = lambda c: dict(hidden=c["hidden"], n_head=c["n_head"], n_kv=c["n_kv"], head_dim=c["head_dim"],
-                          inter=c["inter"], eps=c["eps"], theta=c["theta"], mode=mode)
+                          inter=c["inter"], eps=c["eps"], theta=c["theta"], mode=mode, threads=threads)
     if hidden_in is None:
         x = np.empty((M, H), np.float32)
         for m in range(M):
@@ -321,7 +322,7 @@ def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.nd
         h = decoder_chain_attn(T["mats"], T["norms"], T["qkn"], None, None, x, pos, state["tk"], state["tv"],
                                slots=slots, **dims(T))
         hid = rms_norm_rows(h, T["out_norm"], T["eps"])
-        logits = mul_mat(T["heads"][0], H, hid, mode, want_bound=False)[0]
+        logits = mul_mat(T["heads"][0], H, hid, mode, threads, want_bound=False)[0]
     else:
         hid, logits = hidden_in, logits_in
     codes = np.zeros((M, groups), np.int32)
@@ -340,7 +341,7 @@ def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.nd
     ps = np.repeat(np.asarray(slots, np.int32), 2)
     h = decoder_chain_attn(P["mats"], P["norms"], P["qkn"], None, None, xp, pp, state["pk"], state["pv"], slots=ps,
                            **dims(P))
-    lg = mul_mat(P["heads"][0], H, rms_norm_rows(h[1::2], P["out_norm"], P["eps"]), mode, want_bound=False)[0]
+    lg = mul_mat(P["heads"][0], H, rms_norm_rows(h[1::2], P["out_norm"], P["eps"]), mode, threads, want_bound=False)[0]
     plogits = [lg]
     for m in range(M):
         codes[m, 1] = replay[m, 1] if replay is not None else select_code(lg[m])
@@ -348,7 +349,7 @@ def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.nd
         x = get_rows(ptables[g - 1], H, codes[:, g])[0]
         h = decoder_chain_attn(P["mats"], P["norms"], P["qkn"], None, None, x, np.full(M, g + 1, np.int32),
                                state["pk"], state["pv"], slots=slots, **dims(P))
-        lg = mul_mat(P["heads"][g], H, rms_norm_rows(h, P["out_norm"], P["eps"]), mode, want_bound=False)[0]
+        lg = mul_mat(P["heads"][g], H, rms_norm_rows(h, P["out_norm"], P["eps"]), mode, threads, want_bound=False)[0]
         plogits.append(lg)
         for m in range(M):
             codes[m, g + 1] = replay[m, g + 1] if replay is not None else select_code(lg[m])

@@ -11,7 +11,8 @@
 // theta_{i+1} = theta_i * base^(-2/head_dim) in fp32, cos/sin of each; NEOX
 // pairs element i with i + head_dim/2.  Attention runs split over positions
 // (online softmax per warp, fixed-order merge of the warps, then of the
-// splits by the last CTA of each (token, head) to finish): deterministic.
+// splits by the last CTA of each (token, head) to finish; the split count
+// follows the token's position): deterministic.
 // Scores, softmax and the V sum are fp32 -- ggml-cpu's are fp32 in its own
 // SIMD order -- so parity with the oracle is to a tolerance.
 #include "common.cuh"
@@ -22,7 +23,8 @@
 namespace b200q8 {
 namespace {
 
-constexpr int kAttnThreads = 128;  // 4 warps
+constexpr int kAttnThreads  = 256;  // 8 warps
+constexpr int kPosPerSplit = 64;   // fewest cached positions a split CTA takes
 constexpr int kAttnWarps   = kAttnThreads / 32;
 constexpr int kMaxHeadDim  = 256;
 
@@ -100,20 +102,27 @@ __global__ void __launch_bounds__(kMaxHeadDim) qk_rope_cache_kernel(const AttnAr
     }
 }
 
-// One CTA per (head, token, split): positions [j0, j1) of the token's cached
-// prefix 0..pos.  Each warp keeps an online softmax (running max, sum and
-// weighted V) over its positions; lanes hold head_dim/32 elements.
+// One CTA per (head, token, split).  A token at position pos attends over
+// npos = pos + 1 cached positions, split into ns_eff = ceil(npos /
+// kPosPerSplit) parts (at most the launch's gridDim.z); CTAs beyond ns_eff
+// leave at once, so short prefixes cost one CTA per head.  Each warp keeps an
+// online softmax (running max, sum and weighted V) over its positions; lanes
+// hold head_dim/32 elements.  The warps merge in a fixed order; with several
+// splits, the last split CTA of a (token, head) to finish merges the splits'
+// partials in split order.  ns_eff depends only on pos, so the result is
+// deterministic.
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
     __shared__ float sq[kMaxHeadDim];
     __shared__ float wm[kAttnWarps], wl[kAttnWarps];
     __shared__ float wo[kAttnWarps][kMaxHeadDim];
+    __shared__ float sw[kAttnMaxSplits];
+    __shared__ float sL;
     __shared__ int   last;
     pdl_launch_dependents();
     pdl_wait_primary();
     const int h     = blockIdx.x;
     const int m     = blockIdx.y;
     const int split = blockIdx.z;
-    const int ns    = gridDim.z;
     const int hd    = a.head_dim;
     const int warp  = threadIdx.x >> 5;
     const int lane  = threadIdx.x & 31;
@@ -121,10 +130,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     const int slot  = a.slots ? a.slots[m] : a.slot_base + m;
     const bool ok   = pos >= 0 && pos < a.n_ctx && slot >= 0 && slot < a.n_slots;
     const int npos  = ok ? pos + 1 : 0;
-    const int per   = (npos + ns - 1) / ns;
-    const int j0    = min(npos, split * per);
-    const int j1    = min(npos, j0 + per);
-    const int kvh   = h / (a.n_head / a.n_kv);
+    const int ns    = max(1, min((int) gridDim.z, (npos + kPosPerSplit - 1) / kPosPerSplit));
+    if (split >= ns) {
+        return;
+    }
+    const int per = (npos + ns - 1) / ns;
+    const int j0  = min(npos, split * per);
+    const int j1  = min(npos, j0 + per);
+    const int kvh = h / (a.n_head / a.n_kv);
     for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
         sq[d] = ok ? a.q_rot[(size_t) m * a.n_head * hd + h * hd + d] : 0.0f;
     }
@@ -137,16 +150,25 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     for (int e = 0; e < kMaxHeadDim / 32; ++e) {
         o[e] = 0.0f;
     }
-    const size_t row = (size_t) a.n_kv * hd;
-    const float * kb = a.k_cache + ((size_t) slot * a.n_ctx) * row + (size_t) kvh * hd;
-    const float * vb = a.v_cache + ((size_t) slot * a.n_ctx) * row + (size_t) kvh * hd;
+    const size_t  row = (size_t) a.n_kv * hd;
+    const float * kb  = a.k_cache + ((size_t) slot * a.n_ctx) * row + (size_t) kvh * hd;
+    const float * vb  = a.v_cache + ((size_t) slot * a.n_ctx) * row + (size_t) kvh * hd;
     for (int j = j0 + warp; j < j1; j += kAttnWarps) {
-        const float * kj  = kb + (size_t) j * row;
-        float         dot = 0.0f;
+        const float * kj = kb + (size_t) j * row;
+        const float * vj = vb + (size_t) j * row;
+        float         kv[kMaxHeadDim / 32], vv[kMaxHeadDim / 32];
 #pragma unroll
         for (int e = 0; e < kMaxHeadDim / 32; ++e) {
             if (e < E) {
-                dot = __fmaf_rn(sq[lane + 32 * e], kj[lane + 32 * e], dot);
+                kv[e] = kj[lane + 32 * e];
+                vv[e] = vj[lane + 32 * e];
+            }
+        }
+        float dot = 0.0f;
+#pragma unroll
+        for (int e = 0; e < kMaxHeadDim / 32; ++e) {
+            if (e < E) {
+                dot = __fmaf_rn(sq[lane + 32 * e], kv[e], dot);
             }
         }
 #pragma unroll
@@ -158,11 +180,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
         const float f  = expf(mx - nm);  // 0 on the first position (mx = -inf)
         const float p  = expf(s - nm);
         l              = __fmaf_rn(l, f, p);
-        const float * vj = vb + (size_t) j * row;
 #pragma unroll
         for (int e = 0; e < kMaxHeadDim / 32; ++e) {
             if (e < E) {
-                o[e] = __fmaf_rn(o[e], f, __fmul_rn(p, vj[lane + 32 * e]));
+                o[e] = __fmaf_rn(o[e], f, __fmul_rn(p, vv[e]));
             }
         }
         mx = nm;
@@ -179,37 +200,45 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
         }
     }
     __syncthreads();
-    float * part = a.partial + (((size_t) m * a.n_head + h) * ns + split) * (hd + 2);
-    if (warp == 0) {
-        float M_ = -INFINITY;
-        for (int w = 0; w < kAttnWarps; ++w) {
-            M_ = fmaxf(M_, wm[w]);
-        }
-        float L = 0.0f;
-        for (int w = 0; w < kAttnWarps; ++w) {
-            if (wm[w] != -INFINITY) {
-                L = __fmaf_rn(wl[w], expf(wm[w] - M_), L);
-            }
-        }
-        for (int d = lane; d < hd; d += 32) {
+    float M_ = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) {
+        M_ = fmaxf(M_, wm[w]);
+    }
+    if (threadIdx.x < kAttnWarps) {
+        sw[threadIdx.x] = wm[threadIdx.x] != -INFINITY ? expf(wm[threadIdx.x] - M_) : 0.0f;
+    }
+    __syncthreads();
+    float L = 0.0f;
+    for (int w = 0; w < kAttnWarps; ++w) {
+        L = __fmaf_rn(wl[w], sw[w], L);
+    }
+    if (ns == 1) {
+        for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
             float acc = 0.0f;
             for (int w = 0; w < kAttnWarps; ++w) {
-                if (wm[w] != -INFINITY) {
-                    acc = __fmaf_rn(wo[w][d], expf(wm[w] - M_), acc);
-                }
+                acc = __fmaf_rn(wo[w][d], sw[w], acc);
             }
-            part[d] = acc;
+            a.out[(size_t) m * a.out_stride + h * hd + d] = ok ? __fdiv_rn(acc, L) : 0.0f;
         }
-        if (lane == 0) {
-            part[hd]     = M_;
-            part[hd + 1] = L;
+        return;
+    }
+    float * part = a.partial + (((size_t) m * a.n_head + h) * kAttnMaxSplits + split) * (hd + 2);
+    for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
+        float acc = 0.0f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            acc = __fmaf_rn(wo[w][d], sw[w], acc);
         }
+        part[d] = acc;
+    }
+    if (threadIdx.x == 0) {
+        part[hd]     = M_;
+        part[hd + 1] = L;
     }
     // the last split of this (token, head) to finish merges all splits in order
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-        unsigned * cnt = a.counters + (size_t) m * a.n_head + h;
+        unsigned *     cnt  = a.counters + (size_t) m * a.n_head + h;
         const unsigned prev = atomicAdd(cnt, 1u);
         last                = prev == (unsigned) ns - 1;
         if (last) {
@@ -221,27 +250,31 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
         return;
     }
     __threadfence();
-    const float * base = a.partial + ((size_t) m * a.n_head + h) * ns * (hd + 2);
-    float         M_   = -INFINITY;
-    for (int s = 0; s < ns; ++s) {
-        M_ = fmaxf(M_, ((volatile const float *) base)[s * (hd + 2) + hd]);
+    const float * base = a.partial + ((size_t) m * a.n_head + h) * kAttnMaxSplits * (hd + 2);
+    if (threadIdx.x < ns) {
+        sw[threadIdx.x] = __ldcg(base + threadIdx.x * (hd + 2) + hd);
     }
-    float L = 0.0f;
-    for (int s = 0; s < ns; ++s) {
-        const float ms = ((volatile const float *) base)[s * (hd + 2) + hd];
-        if (ms != -INFINITY) {
-            L = __fmaf_rn(((volatile const float *) base)[s * (hd + 2) + hd + 1], expf(ms - M_), L);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mx2 = -INFINITY;
+        for (int s = 0; s < ns; ++s) {
+            mx2 = fmaxf(mx2, sw[s]);
         }
+        float L2 = 0.0f;
+        for (int s = 0; s < ns; ++s) {
+            const float ws = sw[s] != -INFINITY ? expf(sw[s] - mx2) : 0.0f;
+            L2             = __fmaf_rn(__ldcg(base + s * (hd + 2) + hd + 1), ws, L2);
+            sw[s]          = ws;
+        }
+        sL = L2;
     }
+    __syncthreads();
     for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
         float acc = 0.0f;
         for (int s = 0; s < ns; ++s) {
-            const float ms = ((volatile const float *) base)[s * (hd + 2) + hd];
-            if (ms != -INFINITY) {
-                acc = __fmaf_rn(((volatile const float *) base)[s * (hd + 2) + d], expf(ms - M_), acc);
-            }
+            acc = __fmaf_rn(__ldcg(base + s * (hd + 2) + d), sw[s], acc);
         }
-        a.out[(size_t) m * a.out_stride + h * hd + d] = ok ? __fdiv_rn(acc, L) : 0.0f;
+        a.out[(size_t) m * a.out_stride + h * hd + d] = ok ? __fdiv_rn(acc, sL) : 0.0f;
     }
 }
 
