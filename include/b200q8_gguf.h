@@ -55,6 +55,26 @@ b200q8_status_t b200q8_gguf_get_str(const b200q8_gguf * g, const char * key, cha
 b200q8_status_t b200q8_gguf_talker_chain(const b200q8_gguf * g, int32_t device, int64_t max_m, int32_t mode,
                                          b200q8_chain ** out);
 
+/* Everything one decode frame needs, from a package, on `device`:
+ *   *talker     the talker step with the reference's attention (per-layer
+ *               self_attn.q_norm / k_norm, talker.rope_theta; n_ctx cached
+ *               positions for each of n_slots streams) and output stage
+ *               (talker.model.norm, talker.codec_head);
+ *   *predictor  the code predictor (talker.code_predictor.model.layers.*,
+ *               its norm and lm_head.{g}; cache of code_group_count
+ *               positions; max_m = max(8, 2 * max_m)) with its codec tables;
+ *   *frame      (optional: frame may be NULL) b200q8_frame_create over both,
+ *               with sampling.repetition_penalty (1 when the key is absent).
+ * Hyperparameters follow weights.cpp:128-212 (the predictor's
+ * intermediate_size falls back to the talker's; eps and rope_theta are the
+ * talker's, model.cpp:315-322).  A predictor wider or narrower than the talker
+ * (small_to_mtp_projection) or a tensor not in Q8_0 / F32 as the step needs is
+ * B200Q8_ERR_UNSUPPORTED.  Each chain owns its weights; destroy the frame
+ * before the chains. */
+b200q8_status_t b200q8_gguf_decoder(const b200q8_gguf * g, int32_t device, int64_t max_m, int32_t mode,
+                                    int64_t n_ctx, int64_t n_slots, b200q8_chain ** talker,
+                                    b200q8_chain ** predictor, b200q8_frame ** frame);
+
 #ifdef __cplusplus
 }
 #endif

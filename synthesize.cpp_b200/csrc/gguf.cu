@@ -330,130 +330,318 @@ b200q8_status_t b200q8_gguf_get_str(const b200q8_gguf * g, const char * key, cha
     return B200Q8_OK;
 }
 
-b200q8_status_t b200q8_gguf_talker_chain(const b200q8_gguf * g, int32_t device, int64_t max_m, int32_t mode,
-                                         b200q8_chain ** out) {
-    if (g == nullptr || out == nullptr) {
-        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: null argument");
-    }
-    *out = nullptr;
-    // hyperparameters (src/arch/qwen3-tts/weights.cpp:128-138)
-    const std::string p = "synthesize.qwen3-tts.talker.";
-    uint32_t layers = 0, hidden = 0, heads = 0, kv_heads = 0, head_dim = 0, inter = 0, vocab = 0;
-    float    eps    = 0.0f;
-    const struct {
-        const char * k;
-        uint32_t *   v;
-    } u32s[] = { { "layer_count", &layers },       { "hidden_size", &hidden },
-                 { "attention_head_count", &heads }, { "key_value_head_count", &kv_heads },
-                 { "head_dim", &head_dim },          { "intermediate_size", &inter },
-                 { "codec_vocab_size", &vocab } };
-    for (const auto & e : u32s) {
-        if (b200q8_gguf_get_u32(g, (p + e.k).c_str(), e.v) != B200Q8_OK) {
-            return B200Q8_ERR_INVALID_ARG;
-        }
-    }
-    if (b200q8_gguf_get_f32(g, (p + "rms_norm_eps").c_str(), &eps) != B200Q8_OK) {
-        return B200Q8_ERR_INVALID_ARG;
-    }
-    if (layers == 0 || hidden == 0 || heads == 0 || kv_heads == 0 || head_dim == 0 || inter == 0 || vocab == 0) {
-        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: zero hyperparameter");
-    }
-    // tensors (src/arch/qwen3-tts/catalog.cpp:239-281), expected type and ne
-    struct Need {
-        std::string name;
-        int32_t     type;
-        int64_t     ne0, ne1;
-    };
-    const int64_t     q_out = (int64_t) heads * head_dim, kv_out = (int64_t) kv_heads * head_dim;
-    std::vector<Need> need;
-    for (uint32_t l = 0; l < layers; ++l) {
-        const std::string b = "talker.model.layers." + std::to_string(l) + ".";
-        need.push_back({ b + "self_attn.q_proj.weight", 8, hidden, q_out });
-        need.push_back({ b + "self_attn.k_proj.weight", 8, hidden, kv_out });
-        need.push_back({ b + "self_attn.v_proj.weight", 8, hidden, kv_out });
-        need.push_back({ b + "self_attn.o_proj.weight", 8, q_out, hidden });
-        need.push_back({ b + "mlp.gate_proj.weight", 8, hidden, inter });
-        need.push_back({ b + "mlp.up_proj.weight", 8, hidden, inter });
-        need.push_back({ b + "mlp.down_proj.weight", 8, inter, hidden });
-        need.push_back({ b + "input_layernorm.weight", 0, hidden, 1 });
-        need.push_back({ b + "post_attn_norm.weight", 0, hidden, 1 });
-    }
-    need.push_back({ "talker.model.codec_embedding.weight", 8, hidden, vocab });
-    std::vector<const Tensor *> found;
-    size_t                      total = 0;
+}  // extern "C"
+
+namespace {
+
+struct Need {
+    std::string name;
+    int32_t     type;  // ggml type id: 0 F32, 8 Q8_0
+    int64_t     ne0, ne1;
+};
+
+// Finds every tensor of `need` (shape and type checked; host only).
+b200q8_status_t find_tensors(const b200q8_gguf * g, const std::vector<Need> & need, const char * who,
+                             std::vector<const Tensor *> & found) {
+    found.clear();
     for (const Need & n : need) {
         const int64_t i = b200q8_gguf_find_tensor(g, n.name.c_str());
         if (i < 0) {
-            return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: tensor %s is missing", n.name.c_str());
+            return set_error(B200Q8_ERR_INVALID_ARG, "%s: tensor %s is missing", who, n.name.c_str());
         }
         const Tensor & t = g->tensors[(size_t) i];
         if (t.ne[0] != n.ne0 || t.ne[1] != n.ne1 || t.ne[2] != 1 || t.ne[3] != 1) {
-            return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: %s has shape [%lld, %lld], expected [%lld, %lld]",
+            return set_error(B200Q8_ERR_INVALID_ARG, "%s: %s has shape [%lld, %lld], expected [%lld, %lld]", who,
                              n.name.c_str(), (long long) t.ne[0], (long long) t.ne[1], (long long) n.ne0,
                              (long long) n.ne1);
         }
         if (t.type != n.type) {
-            return set_error(B200Q8_ERR_UNSUPPORTED, "gguf_talker_chain: %s is ggml type %d, the step needs %s",
+            return set_error(B200Q8_ERR_UNSUPPORTED, "%s: %s is ggml type %d, the step needs %s", who,
                              n.name.c_str(), t.type, n.type == 8 ? "Q8_0" : "F32");
         }
         found.push_back(&t);
-        total += (t.nbytes + 15) & ~(size_t) 15;
+    }
+    return B200Q8_OK;
+}
+
+// Uploads the found tensors into one device buffer (current device) at
+// 16-byte steps, so q|k|v and gate|up stay adjacent and the chain uses them in
+// place; returns their device pointers.
+b200q8_status_t upload_tensors(const b200q8_gguf * g, const std::vector<const Tensor *> & found, uint8_t ** buf,
+                               std::vector<const void *> & ptr) {
+    size_t total = 0;
+    for (const Tensor * t : found) {
+        total += (t->nbytes + 15) & ~(size_t) 15;
+    }
+    uint8_t *   dev = nullptr;
+    cudaError_t e   = cudaMalloc(&dev, std::max<size_t>(total, 16));
+    if (e != cudaSuccess) {
+        return cuda_error(e, "gguf: weight buffer");
+    }
+    ptr.assign(found.size(), nullptr);
+    size_t off = 0;
+    for (size_t i = 0; i < found.size() && e == cudaSuccess; ++i) {
+        ptr[i] = dev + off;
+        e      = cudaMemcpy(dev + off, g->map + g->data_start + found[i]->offset, found[i]->nbytes,
+                            cudaMemcpyHostToDevice);
+        off += (found[i]->nbytes + 15) & ~(size_t) 15;
+    }
+    if (e != cudaSuccess) {
+        cudaFree(dev);
+        return cuda_error(e, "gguf: weight upload");
+    }
+    *buf = dev;
+    return B200Q8_OK;
+}
+
+// One decoder stack of the package (the talker's or the code predictor's: the
+// same block, src/arch/qwen3-tts/catalog.cpp:234-262).
+struct StackSpec {
+    std::string              prefix;  // "talker.model.layers." or "talker.code_predictor.model.layers."
+    uint32_t                 layers = 0, hidden = 0, heads = 0, kv = 0, head_dim = 0, inter = 0;
+    float                    eps = 0.0f, rope_theta = 0.0f;
+    bool                     attention = false;
+    int64_t                  n_ctx = 0, n_slots = 0;
+    std::vector<std::string> tables;  // Q8_0 [table_hidden, table_rows]; the first is the chain's table
+    uint32_t                 table_hidden = 0;
+    int64_t                  table_rows   = 0;
+    std::string              norm;    // final norm; empty: no output stage
+    std::vector<std::string> head_names;
+    int64_t                  vocab = 0;
+};
+
+b200q8_status_t build_stack(const b200q8_gguf * g, const StackSpec & s, int32_t device, int64_t max_m,
+                            int32_t mode, const char * who, b200q8_chain ** out, std::vector<const void *> * tables) {
+    const int64_t     Q = (int64_t) s.heads * s.head_dim, KV = (int64_t) s.kv * s.head_dim;
+    const int         per_layer = s.attention ? 11 : 9;
+    std::vector<Need> need;
+    for (uint32_t l = 0; l < s.layers; ++l) {
+        const std::string b = s.prefix + std::to_string(l) + ".";
+        need.push_back({ b + "self_attn.q_proj.weight", 8, s.hidden, Q });
+        need.push_back({ b + "self_attn.k_proj.weight", 8, s.hidden, KV });
+        need.push_back({ b + "self_attn.v_proj.weight", 8, s.hidden, KV });
+        need.push_back({ b + "self_attn.o_proj.weight", 8, Q, s.hidden });
+        need.push_back({ b + "mlp.gate_proj.weight", 8, s.hidden, s.inter });
+        need.push_back({ b + "mlp.up_proj.weight", 8, s.hidden, s.inter });
+        need.push_back({ b + "mlp.down_proj.weight", 8, s.inter, s.hidden });
+        need.push_back({ b + "input_layernorm.weight", 0, s.hidden, 1 });
+        need.push_back({ b + "post_attn_norm.weight", 0, s.hidden, 1 });
+        if (s.attention) {
+            need.push_back({ b + "self_attn.q_norm.weight", 0, s.head_dim, 1 });
+            need.push_back({ b + "self_attn.k_norm.weight", 0, s.head_dim, 1 });
+        }
+    }
+    const size_t t0 = need.size();
+    for (const std::string & t : s.tables) {
+        need.push_back({ t, 8, s.table_hidden, s.table_rows });
+    }
+    const size_t n0 = need.size();
+    if (!s.norm.empty()) {
+        need.push_back({ s.norm, 0, s.hidden, 1 });
+        for (const std::string & h : s.head_names) {
+            need.push_back({ h, 8, s.hidden, s.vocab });
+        }
+    }
+    std::vector<const Tensor *> found;
+    b200q8_status_t             st = find_tensors(g, need, who, found);
+    if (st != B200Q8_OK) {
+        return st;
     }
     int prev = 0;
     cudaGetDevice(&prev);
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) {
-        return cuda_error(e, "gguf_talker_chain: cudaSetDevice");
+        return cuda_error(e, "gguf: cudaSetDevice");
     }
-    uint8_t * dev = nullptr;
-    e             = cudaMalloc(&dev, total);
-    if (e != cudaSuccess) {
+    uint8_t *                 dev = nullptr;
+    std::vector<const void *> ptr;
+    st = upload_tensors(g, found, &dev, ptr);
+    if (st != B200Q8_OK) {
         cudaSetDevice(prev);
-        return cuda_error(e, "gguf_talker_chain: weight buffer");
+        return st;
     }
-    std::vector<const void *> ptr(found.size());
-    size_t                    off = 0;
-    for (size_t i = 0; i < found.size() && e == cudaSuccess; ++i) {
-        ptr[i] = dev + off;
-        e      = cudaMemcpy(dev + off, g->map + g->data_start + found[i]->offset, found[i]->nbytes,
-                            cudaMemcpyHostToDevice);
-        // 16-byte steps keep q|k|v and gate|up adjacent, so the chain uses them in place
-        off += (found[i]->nbytes + 15) & ~(size_t) 15;
+    std::vector<b200q8_layer>  ls(s.layers);
+    std::vector<const float *> qn(s.layers), kn(s.layers);
+    for (uint32_t l = 0; l < s.layers; ++l) {
+        const void * const * q = &ptr[(size_t) l * per_layer];
+        ls[l] = { q[0], q[1], q[2], q[3], q[4], q[5], q[6], static_cast<const float *>(q[7]),
+                  static_cast<const float *>(q[8]) };
+        if (s.attention) {
+            qn[l] = static_cast<const float *>(q[9]);
+            kn[l] = static_cast<const float *>(q[10]);
+        }
     }
-    if (e != cudaSuccess) {
-        cudaFree(dev);
-        cudaSetDevice(prev);
-        return cuda_error(e, "gguf_talker_chain: weight upload");
-    }
-    std::vector<b200q8_layer> ls(layers);
-    for (uint32_t l = 0; l < layers; ++l) {
-        const void * const * q = &ptr[(size_t) l * 9];
-        ls[l]                  = { q[0], q[1], q[2], q[3], q[4], q[5], q[6], static_cast<const float *>(q[7]),
-                                   static_cast<const float *>(q[8]) };
-    }
+    b200q8_attention_desc ad = { s.rope_theta, s.n_ctx, s.n_slots, qn.data(), kn.data() };
+    std::vector<const void *> heads(ptr.begin() + (std::ptrdiff_t) std::min(n0 + 1, ptr.size()), ptr.end());
+    b200q8_output_desc        od = { s.norm.empty() ? nullptr : static_cast<const float *>(ptr[n0]), heads.data(),
+                                     (int32_t) heads.size(), s.vocab };
     b200q8_chain_desc d = {};
-    d.n_layers          = (int32_t) layers;
-    d.hidden            = hidden;
-    d.n_head            = heads;
-    d.n_kv              = kv_heads;
-    d.head_dim          = head_dim;
-    d.inter             = inter;
-    d.eps               = eps;
+    d.n_layers          = (int32_t) s.layers;
+    d.hidden            = s.hidden;
+    d.n_head            = s.heads;
+    d.n_kv              = s.kv;
+    d.head_dim          = s.head_dim;
+    d.inter             = s.inter;
+    d.eps               = s.eps;
     d.max_m             = max_m;
     d.mode              = mode;
     d.layers            = ls.data();
-    d.table             = ptr.back();
-    d.table_rows        = vocab;
-    b200q8_chain *        c  = nullptr;
-    const b200q8_status_t st = b200q8_chain_create(&d, device, &c);
+    d.table             = ptr[t0];
+    d.table_rows        = s.table_rows;
+    d.attention         = s.attention ? &ad : nullptr;
+    d.output            = s.norm.empty() ? nullptr : &od;
+    b200q8_chain * c    = nullptr;
+    st                  = b200q8_chain_create(&d, device, &c);
     if (st != B200Q8_OK) {
         cudaFree(dev);
         cudaSetDevice(prev);
         return st;
     }
     c->owned.push_back(dev);  // the chain frees the weights with its own buffers
+    if (tables != nullptr) {
+        tables->assign(ptr.begin() + (std::ptrdiff_t) t0, ptr.begin() + (std::ptrdiff_t) n0);
+    }
     cudaSetDevice(prev);
     *out = c;
+    return B200Q8_OK;
+}
+
+// The decoder block's hyperparameters under `p` (weights.cpp:128-138 for the
+// talker, 168-212 for the code predictor).
+b200q8_status_t read_block(const b200q8_gguf * g, const std::string & p, const char * vocab_key, StackSpec & s,
+                           uint32_t & vocab, const char * who) {
+    const struct {
+        const char * k;
+        uint32_t *   v;
+    } u32s[] = { { "layer_count", &s.layers }, { "hidden_size", &s.hidden }, { "attention_head_count", &s.heads },
+                 { "key_value_head_count", &s.kv }, { "head_dim", &s.head_dim }, { vocab_key, &vocab } };
+    for (const auto & e : u32s) {
+        if (b200q8_gguf_get_u32(g, (p + e.k).c_str(), e.v) != B200Q8_OK) {
+            return B200Q8_ERR_INVALID_ARG;
+        }
+    }
+    if (s.layers == 0 || s.hidden == 0 || s.heads == 0 || s.kv == 0 || s.head_dim == 0 || vocab == 0 ||
+        s.heads % s.kv != 0) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "%s: zero hyperparameter or heads not a multiple of kv heads", who);
+    }
+    return B200Q8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+b200q8_status_t b200q8_gguf_talker_chain(const b200q8_gguf * g, int32_t device, int64_t max_m, int32_t mode,
+                                         b200q8_chain ** out) {
+    if (g == nullptr || out == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: null argument");
+    }
+    *out = nullptr;
+    const std::string p = "synthesize.qwen3-tts.talker.";
+    StackSpec         s;
+    uint32_t          vocab = 0;
+    b200q8_status_t   st    = read_block(g, p, "codec_vocab_size", s, vocab, "gguf_talker_chain");
+    if (st == B200Q8_OK) st = b200q8_gguf_get_u32(g, (p + "intermediate_size").c_str(), &s.inter);
+    if (st == B200Q8_OK) st = b200q8_gguf_get_f32(g, (p + "rms_norm_eps").c_str(), &s.eps);
+    if (st != B200Q8_OK) {
+        return st;
+    }
+    if (s.inter == 0) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_talker_chain: zero hyperparameter");
+    }
+    s.prefix       = "talker.model.layers.";
+    s.tables       = { "talker.model.codec_embedding.weight" };
+    s.table_hidden = s.hidden;
+    s.table_rows   = vocab;
+    return build_stack(g, s, device, max_m, mode, "gguf_talker_chain", out, nullptr);
+}
+
+b200q8_status_t b200q8_gguf_decoder(const b200q8_gguf * g, int32_t device, int64_t max_m, int32_t mode,
+                                    int64_t n_ctx, int64_t n_slots, b200q8_chain ** talker,
+                                    b200q8_chain ** predictor, b200q8_frame ** frame) {
+    if (g == nullptr || talker == nullptr || predictor == nullptr || max_m < 1 || n_ctx < 1 || n_slots < 1) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "gguf_decoder: null argument or non-positive size");
+    }
+    *talker    = nullptr;
+    *predictor = nullptr;
+    if (frame != nullptr) {
+        *frame = nullptr;
+    }
+    const char *      who = "gguf_decoder";
+    const std::string tp = "synthesize.qwen3-tts.talker.", pp = "synthesize.qwen3-tts.code_predictor.";
+    StackSpec         ts, ps;
+    uint32_t          t_vocab = 0, p_vocab = 0, t_groups = 0, p_groups = 0;
+    b200q8_status_t   st = read_block(g, tp, "codec_vocab_size", ts, t_vocab, who);
+    if (st == B200Q8_OK) st = read_block(g, pp, "vocab_size", ps, p_vocab, who);
+    if (st == B200Q8_OK) st = b200q8_gguf_get_u32(g, (tp + "intermediate_size").c_str(), &ts.inter);
+    if (st == B200Q8_OK) st = b200q8_gguf_get_f32(g, (tp + "rms_norm_eps").c_str(), &ts.eps);
+    if (st == B200Q8_OK) st = b200q8_gguf_get_f32(g, (tp + "rope_theta").c_str(), &ts.rope_theta);
+    if (st == B200Q8_OK) st = b200q8_gguf_get_u32(g, (tp + "code_group_count").c_str(), &t_groups);
+    if (st == B200Q8_OK) st = b200q8_gguf_get_u32(g, (pp + "code_group_count").c_str(), &p_groups);
+    if (st != B200Q8_OK) {
+        return st;
+    }
+    // optional: packages converted before the key carry the talker's width (weights.cpp:178-193)
+    if (b200q8_gguf_get_u32(g, (pp + "intermediate_size").c_str(), &ps.inter) != B200Q8_OK) {
+        ps.inter = ts.inter;
+    }
+    char rope_type[16] = {};
+    if (b200q8_gguf_get_str(g, (tp + "rope_type").c_str(), rope_type, sizeof(rope_type)) == B200Q8_OK &&
+        std::strcmp(rope_type, "1d") != 0) {
+        return set_error(B200Q8_ERR_UNSUPPORTED, "%s: rope type %s (only 1d is defined)", who, rope_type);
+    }
+    float penalty = 1.0f;
+    if (b200q8_gguf_get_f32(g, "synthesize.qwen3-tts.sampling.repetition_penalty", &penalty) != B200Q8_OK) {
+        penalty = 1.0f;
+    }
+    if (ts.inter == 0 || ps.inter == 0 || !(ts.eps > 0.0f) || !(ts.rope_theta > 0.0f) || t_groups < 2 ||
+        t_groups != p_groups) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "%s: bad hyperparameters (intermediate sizes, eps, rope_theta, "
+                                                 "code groups >= 2 and equal for both heads)", who);
+    }
+    if (ps.hidden != ts.hidden) {
+        return set_error(B200Q8_ERR_UNSUPPORTED, "%s: the predictor's width differs from the talker's "
+                                                 "(small_to_mtp_projection is not supported)", who);
+    }
+    ts.prefix       = "talker.model.layers.";
+    ts.attention    = true;
+    ts.n_ctx        = n_ctx;
+    ts.n_slots      = n_slots;
+    ts.tables       = { "talker.model.codec_embedding.weight" };
+    ts.table_hidden = ts.hidden;
+    ts.table_rows   = t_vocab;
+    ts.norm         = "talker.model.norm.weight";
+    ts.head_names   = { "talker.codec_head.weight" };
+    ts.vocab        = t_vocab;
+    ps.prefix       = "talker.code_predictor.model.layers.";
+    ps.eps          = ts.eps;  // the predictor shares the talker's eps and rope (model.cpp:315-322)
+    ps.rope_theta   = ts.rope_theta;
+    ps.attention    = true;
+    ps.n_ctx        = t_groups;
+    ps.n_slots      = n_slots;
+    for (uint32_t k = 0; k + 1 < t_groups; ++k) {
+        ps.tables.push_back("talker.code_predictor.model.codec_embedding." + std::to_string(k) + ".weight");
+        ps.head_names.push_back("talker.code_predictor.lm_head." + std::to_string(k) + ".weight");
+    }
+    ps.table_hidden = ts.hidden;
+    ps.table_rows   = p_vocab;
+    ps.norm         = "talker.code_predictor.model.norm.weight";
+    ps.vocab        = p_vocab;
+    b200q8_chain *            tc = nullptr, *pc = nullptr;
+    std::vector<const void *> ptables;
+    st = build_stack(g, ts, device, max_m, mode, who, &tc, nullptr);
+    if (st == B200Q8_OK) st = build_stack(g, ps, device, std::max<int64_t>(8, 2 * max_m), mode, who, &pc, &ptables);
+    if (st == B200Q8_OK && frame != nullptr) {
+        const b200q8_frame_desc fd = { tc, pc, (int32_t) t_groups, ptables.data(), p_vocab, penalty };
+        st                         = b200q8_frame_create(&fd, frame);
+    }
+    if (st != B200Q8_OK) {
+        b200q8_chain_destroy(tc);
+        b200q8_chain_destroy(pc);
+        return st;
+    }
+    *talker    = tc;
+    *predictor = pc;
     return B200Q8_OK;
 }
 

@@ -30,6 +30,16 @@ class Frame:
         check(lib().b200q8_frame_create(ctypes.byref(desc), ctypes.byref(handle)))
         self._h = handle
 
+    @classmethod
+    def from_handle(cls, handle: ctypes.c_void_p, talker: DecodeChain, predictor: DecodeChain, *,
+                    groups: int) -> "Frame":
+        """Wraps a frame the library already built (b200q8_gguf_decoder); keeps the chains alive while it lives."""
+        self = cls.__new__(cls)
+        self._keep = (talker, predictor)
+        self.groups = groups
+        self._h = handle
+        return self
+
     def run(self, codes: torch.Tensor, *, text: torch.Tensor | None = None, prev: torch.Tensor | None = None,
             pos: torch.Tensor | None = None, slots: torch.Tensor | None = None, replay: torch.Tensor | None = None,
             hidden: torch.Tensor | None = None, talker_logits: torch.Tensor | None = None,

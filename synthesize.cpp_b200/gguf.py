@@ -48,6 +48,9 @@ def _bind():
     L.b200q8_gguf_get_str.restype = i32
     L.b200q8_gguf_talker_chain.argtypes = [vp, i32, i64, i32, ctypes.POINTER(vp)]
     L.b200q8_gguf_talker_chain.restype = i32
+    L.b200q8_gguf_decoder.argtypes = [vp, i32, i64, i32, i64, i64, ctypes.POINTER(vp), ctypes.POINTER(vp),
+                                      ctypes.POINTER(vp)]
+    L.b200q8_gguf_decoder.restype = i32
     L._gguf_bound = True
     return L
 
@@ -103,6 +106,27 @@ class Package:
         return DecodeChain.from_handle(h, hidden=self.get_u32(p + "hidden_size"),
                                        n_layers=self.get_u32(p + "layer_count"),
                                        device=torch.device("cuda", device))
+
+    def decoder(self, device: int = 0, max_m: int = 8, n_ctx: int = 4096, n_slots: int = 8,
+                mode: int = QUANT_REF):
+        """(talker, predictor, frame): the package's talker step with attention and codec head, its code predictor
+        and the decode frame over both (b200q8_gguf_decoder)."""
+        from .chain import DecodeChain
+        from .frame import Frame
+
+        t, pr, f = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        check(_bind().b200q8_gguf_decoder(self._h, device, max_m, mode, n_ctx, n_slots, ctypes.byref(t),
+                                          ctypes.byref(pr), ctypes.byref(f)))
+        dev = torch.device("cuda", device)
+        tp, pp = "synthesize.qwen3-tts.talker.", "synthesize.qwen3-tts.code_predictor."
+        talker = DecodeChain.from_handle(t, hidden=self.get_u32(tp + "hidden_size"),
+                                         n_layers=self.get_u32(tp + "layer_count"), device=dev)
+        talker.vocab = self.get_u32(tp + "codec_vocab_size")
+        predictor = DecodeChain.from_handle(pr, hidden=self.get_u32(pp + "hidden_size"),
+                                            n_layers=self.get_u32(pp + "layer_count"), device=dev)
+        predictor.vocab = self.get_u32(pp + "vocab_size")
+        frame = Frame.from_handle(f, talker, predictor, groups=self.get_u32(tp + "code_group_count"))
+        return talker, predictor, frame
 
     def close(self) -> None:
         if self._h:

@@ -30,7 +30,8 @@ def test_gguf_header_is_exported(pkg):
 
     hdr = os.path.join(os.path.dirname(_abi.HEADER), "b200q8_gguf.h")
     declared = _abi.header_symbols(hdr)
-    assert declared == ["b200q8_gguf_close", "b200q8_gguf_find_tensor", "b200q8_gguf_get_f32", "b200q8_gguf_get_str",
+    assert declared == ["b200q8_gguf_close", "b200q8_gguf_decoder", "b200q8_gguf_find_tensor", "b200q8_gguf_get_f32",
+                        "b200q8_gguf_get_str",
                         "b200q8_gguf_get_u32", "b200q8_gguf_open", "b200q8_gguf_talker_chain", "b200q8_gguf_tensor",
                         "b200q8_gguf_tensor_count"]
     out = subprocess.run(["nm", "-D", "--defined-only", _abi.LIB_PATH], capture_output=True, text=True).stdout

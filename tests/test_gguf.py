@@ -108,3 +108,36 @@ def test_talker_chain_reports_missing_tensors_without_a_gpu(pkg_mod, tmp_path):
         with pytest.raises(B200Q8Error) as e:
             pk.talker_chain()
         assert e.value.status == 1
+
+
+def _decoder_meta(p_hidden=256, with_pred=True):
+    kv = {}
+    t, pp = "synthesize.qwen3-tts.talker.", "synthesize.qwen3-tts.code_predictor."
+    kv.update({t + "layer_count": ("uint32", 1), t + "hidden_size": ("uint32", 256),
+               t + "attention_head_count": ("uint32", 4), t + "key_value_head_count": ("uint32", 2),
+               t + "head_dim": ("uint32", 64), t + "intermediate_size": ("uint32", 512),
+               t + "codec_vocab_size": ("uint32", 64), t + "rms_norm_eps": ("float32", 1e-6),
+               t + "rope_theta": ("float32", 1e4), t + "code_group_count": ("uint32", 4)})
+    if with_pred:
+        kv.update({pp + "layer_count": ("uint32", 1), pp + "hidden_size": ("uint32", p_hidden),
+                   pp + "attention_head_count": ("uint32", 4), pp + "key_value_head_count": ("uint32", 2),
+                   pp + "head_dim": ("uint32", 64), pp + "vocab_size": ("uint32", 32),
+                   pp + "code_group_count": ("uint32", 4)})
+    return kv
+
+
+@pytest.mark.parametrize("case,status", [("width", 8), ("no_predictor", 1)])
+def test_decoder_refusals_before_any_upload(pkg_mod, tmp_path, case, status):
+    """b200q8_gguf_decoder refuses a predictor of another width (small_to_mtp_projection) as UNSUPPORTED and a
+    package without the predictor's keys as INVALID_ARG, before touching a device."""
+    import ctypes
+
+    path = tmp_path / f"{case}.gguf"
+    write_package(path, _decoder_meta(p_hidden=512 if case == "width" else 256, with_pred=case != "no_predictor"),
+                  [("talker.model.norm.weight", np.ones(256, np.float32), None, None)])
+    with pkg_mod.Package(path) as p:
+        L = pkg_mod._bind()
+        t, pr, f = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        st = L.b200q8_gguf_decoder(p._h, 0, 2, 0, 8, 2, ctypes.byref(t), ctypes.byref(pr), ctypes.byref(f))
+        assert st == status
+        assert not t.value and not pr.value and not f.value
