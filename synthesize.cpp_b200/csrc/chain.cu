@@ -95,6 +95,7 @@ struct b200q8_chain {
     size_t                       ll_layer     = 0;
     unsigned *                   sync         = nullptr;
     bool                         persistent   = false;
+    bool                         persistent_in_graph = true;  // cleared if a graph cannot hold its launch
     void *                       timeline     = nullptr;  // B200Q8_TIMELINE analysis builds only
     void *                       planes       = nullptr;  // batched path (M > 8): GEMM code/scale planes
     // attention with a KV cache (desc.attention != nullptr)
@@ -200,6 +201,48 @@ const uint8_t * contiguous(b200q8_chain * c, const void * a, size_t a_bytes, con
     return o;
 }
 
+// The persistent single-launch step's arguments for io; false when the step
+// cannot run it (M > 2, a shape or head it does not support, or disabled).
+bool persistent_args(b200q8_chain * c, const StepIO & io, StepArgs & a) {
+    if (!c->persistent || io.M > 2) {
+        return false;
+    }
+    const b200q8_chain_desc & d = c->d;
+    a = StepArgs();
+    a.layers = c->step_layers; a.n_layers = d.n_layers;
+    a.H = (int) d.hidden; a.Q = (int) (d.n_head * d.head_dim); a.KV = (int) (d.n_kv * d.head_dim);
+    a.I = (int) d.inter; a.head_dim = (int) d.head_dim; a.group = (int) (d.n_head / d.n_kv); a.eps = d.eps;
+    while ((1 << a.lg_head_dim) < a.head_dim) ++a.lg_head_dim;
+    while ((1 << a.lg_group) < a.group) ++a.lg_group;
+    a.rb_h = c->rb_h; a.rb_q = c->rb_q; a.rb_i = c->rb_i;
+    a.table = io.table; a.table_rows = io.table_rows;
+    a.ids = io.ids; a.x_in = io.x_in; a.h_out = io.h_out; a.M = (int) io.M; a.mode = d.mode;
+    a.ll = c->ll; a.ll_layer = c->ll_layer; a.ll_m = 2;
+    a.trace = c->act; a.trace_layer = c->layer_floats;
+    for (int i = 0; i < kNumBufs; ++i) a.trace_off[i] = c->buf_off[i];
+    a.sync = c->sync;
+    if (c->attn) {
+        a.attn = 1; a.rope_theta = c->ad.rope_theta; a.pos = io.pos; a.slots = io.slots;
+        a.n_ctx = (int) c->ad.n_ctx; a.n_cache_slots = (int) c->ad.n_slots;
+        const size_t layer = (size_t) c->ad.n_slots * c->ad.n_ctx * (d.n_kv * d.head_dim);
+        a.k_cache = c->kv_cache;
+        a.v_cache = c->kv_cache + (size_t) d.n_layers * layer;
+    }
+    if (io.hidden_out != nullptr) {
+        a.out_norm = c->out_norm; a.head = c->heads[io.head]; a.vocab = (int) c->vocab;
+        a.hidden_out = io.hidden_out; a.logits = io.logits;
+    }
+#ifdef B200Q8_TIMELINE
+    if (c->timeline == nullptr) {
+        cudaMalloc(&c->timeline, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms);
+        cudaMemset(c->timeline, 0, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms);
+        c->owned.push_back(c->timeline);
+    }
+    a.timeline = static_cast<unsigned long long *>(c->timeline);
+#endif
+    return decode_step_supported(a, c->sms);
+}
+
 // M > 8: per op, a per-token prologue kernel (norm / GQA / SwiGLU + residual,
 // quantized into code and scale planes) then the int8 tensor-core GEMM;
 // 2 launches per op with programmatic dependent launch between them.
@@ -277,6 +320,10 @@ cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, const StepIO & io) {
     const int64_t   M = io.M;
     const int32_t * pos = io.pos, * slots = io.slots;
     float *         h_out = io.h_out;
+    StepArgs        sa;
+    if (c->persistent_in_graph && persistent_args(c, io, sa)) {
+        return launch_decode_step(sa, c->sms, st);
+    }
     {
         const int64_t total = M * H;
         const int     grid  = (int) std::min<int64_t>((total + 255) / 256, (int64_t) c->sms * 4);
@@ -369,20 +416,30 @@ b200q8_status_t run_graph(b200q8_chain * c, const StepIO & io, b200q8_stream_t s
         }
     }
     if (exec == nullptr) {
-        cudaGraph_t graph = nullptr;
-        e                 = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal);
-        if (e == cudaSuccess) {
-            cudaError_t e2 = enqueue_step(c, c->cap_stream, io);
-            e              = cudaStreamEndCapture(c->cap_stream, &graph);
-            if (e2 != cudaSuccess) {
-                e = e2;
+        for (int attempt = 0; attempt < 2; ++attempt) {
+            cudaGraph_t graph = nullptr;
+            exec              = nullptr;
+            e                 = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal);
+            if (e == cudaSuccess) {
+                cudaError_t e2 = enqueue_step(c, c->cap_stream, io);
+                e              = cudaStreamEndCapture(c->cap_stream, &graph);
+                if (e2 != cudaSuccess) {
+                    e = e2;
+                }
             }
-        }
-        if (e == cudaSuccess) {
-            e = cudaGraphInstantiate(&exec, graph, 0);
-        }
-        if (graph) {
-            cudaGraphDestroy(graph);
+            if (e == cudaSuccess) {
+                e = cudaGraphInstantiate(&exec, graph, 0);
+            }
+            if (graph) {
+                cudaGraphDestroy(graph);
+            }
+            StepArgs probe;
+            if (e == cudaSuccess || attempt > 0 || !c->persistent_in_graph || !persistent_args(c, io, probe)) {
+                break;
+            }
+            // a graph that cannot hold the cooperative launch: capture the per-op form instead
+            cudaGetLastError();
+            c->persistent_in_graph = false;
         }
         if (e != cudaSuccess) {
             return cuda_error(e, "chain_run: graph capture");
@@ -570,16 +627,17 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
             c->attn_count   = static_cast<unsigned *>(p4);
         }
     }
-    // persistent step (single-position attention only): per-layer weight
-    // table, LL hand-off words, sync words
+    // persistent step (M <= 2): per-layer weight table, LL hand-off words,
+    // sync words
     const char * per_op = getenv("B200Q8_CHAIN_PER_OP");
-    if (e == cudaSuccess && !c->attn && !(per_op && per_op[0] == '1')) {
+    if (e == cudaSuccess && !(per_op && per_op[0] == '1')) {
         std::vector<StepLayerDev> host_layers(d.n_layers);
         for (int l = 0; l < d.n_layers; ++l) {
             host_layers[l] = { c->w_qkv[l], c->w_o[l], c->w_gu[l], c->w_gu[l] + (size_t) I * c->rb_h, c->w_d[l],
-                               c->layers[l].norm_in, c->layers[l].norm_post };
+                               c->layers[l].norm_in, c->layers[l].norm_post,
+                               c->attn ? c->q_norm[l] : nullptr, c->attn ? c->k_norm[l] : nullptr };
         }
-        c->ll_layer  = (size_t) 2 * (KV + H + I + H);
+        c->ll_layer  = (size_t) 2 * (c->qkv_dim + Q + H + I + H);
         void * p1 = nullptr, * p2 = nullptr, * p3 = nullptr;
         e = cudaMalloc(&p1, sizeof(StepLayerDev) * d.n_layers);
         if (e == cudaSuccess) { c->owned.push_back(p1); e = cudaMalloc(&p2, sizeof(unsigned long long) * c->ll_layer * d.n_layers); }
@@ -595,7 +653,7 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
         if (e == cudaSuccess) e = cudaMemset(p3, 0, 64);
         StepArgs probe = {};
         probe.H = (int) H; probe.Q = (int) (d.n_head * d.head_dim); probe.KV = (int) KV; probe.I = (int) I;
-        probe.mode = d.mode;
+        probe.mode = d.mode; probe.attn = c->attn ? 1 : 0; probe.head_dim = (int) d.head_dim;
         c->persistent = e == cudaSuccess && decode_step_fits(probe);
     }
     for (int l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
@@ -639,38 +697,15 @@ b200q8_status_t b200q8_chain_run(b200q8_chain * c, const int32_t * ids, const fl
     if (e != cudaSuccess) {
         return cuda_error(e, "chain_run: cudaSetDevice");
     }
-    if (c->persistent && M <= 2) {
-        const b200q8_chain_desc & d = c->d;
-        StepArgs a = {};
-        a.layers = c->step_layers; a.n_layers = d.n_layers;
-        a.H = (int) d.hidden; a.Q = (int) (d.n_head * d.head_dim); a.KV = (int) (d.n_kv * d.head_dim);
-        a.I = (int) d.inter; a.head_dim = (int) d.head_dim; a.group = (int) (d.n_head / d.n_kv); a.eps = d.eps;
-        while ((1 << a.lg_head_dim) < a.head_dim) ++a.lg_head_dim;
-        while ((1 << a.lg_group) < a.group) ++a.lg_group;
-        a.rb_h = c->rb_h; a.rb_q = c->rb_q; a.rb_i = c->rb_i;
-        a.table = static_cast<const uint8_t *>(d.table); a.table_rows = d.table_rows;
-        a.ids = ids; a.x_in = x_in; a.h_out = h_out; a.M = (int) M; a.mode = d.mode;
-        a.ll = c->ll; a.ll_layer = c->ll_layer; a.ll_m = 2;
-        a.trace = c->act; a.trace_layer = c->layer_floats;
-        for (int i = 0; i < kNumBufs; ++i) a.trace_off[i] = c->buf_off[i];
-        a.sync = c->sync;
-#ifdef B200Q8_TIMELINE
-        if (c->timeline == nullptr) {
-            cudaMalloc(&c->timeline, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms);
-            cudaMemset(c->timeline, 0, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms);
-            c->owned.push_back(c->timeline);
-        }
-        a.timeline = static_cast<unsigned long long *>(c->timeline);
-#endif
-        if (decode_step_supported(a, c->sms)) {
-            e = launch_decode_step(a, c->sms, reinterpret_cast<cudaStream_t>(stream));
-            cudaSetDevice(prev);
-            return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_run: persistent step launch");
-        }
-    }
     StepIO io;
     io.M = M; io.ids = ids; io.x_in = x_in; io.h_out = h_out;
     io.table = static_cast<const uint8_t *>(c->d.table); io.table_rows = c->d.table_rows;
+    StepArgs a;
+    if (persistent_args(c, io, a)) {
+        e = launch_decode_step(a, c->sms, reinterpret_cast<cudaStream_t>(stream));
+        cudaSetDevice(prev);
+        return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "chain_run: persistent step launch");
+    }
     const b200q8_status_t st = run_graph(c, io, stream);
     cudaSetDevice(prev);
     return st;
@@ -849,6 +884,14 @@ b200q8_status_t chain_resolve(b200q8_chain * c, const b200q8_step_args & a, Step
 
 cudaError_t chain_enqueue(b200q8_chain * c, cudaStream_t st, const StepIO & io) {
     return enqueue_step(c, st, io);
+}
+
+bool chain_persistent_in_graph(b200q8_chain * c, bool disable) {
+    const bool was = c->persistent && c->persistent_in_graph;
+    if (disable) {
+        c->persistent_in_graph = false;
+    }
+    return was;
 }
 
 }  // namespace b200q8

@@ -53,4 +53,8 @@ b200q8_status_t chain_resolve(b200q8_chain * c, const b200q8_step_args & a, Step
 // Enqueues the step's kernels on st (which may be capturing).
 cudaError_t chain_enqueue(b200q8_chain * c, cudaStream_t st, const StepIO & io);
 
+// Whether the chain puts its persistent single-launch step into captured
+// graphs; disable = true turns that off (the per-op form is captured then).
+bool chain_persistent_in_graph(b200q8_chain * c, bool disable);
+
 }  // namespace b200q8

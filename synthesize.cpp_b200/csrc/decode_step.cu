@@ -128,8 +128,15 @@ struct Smem {
     float *    ybuf;       // [M_T][2*kStepYMax]
     uint8_t *  xc[2];      // staged codes [M_T][Kmax], double buffered by op parity
     float *    xd[2];      // staged scales [M_T][Kmax/32]
+    float *    att;        // attention scratch (attention steps): q, 2 k, 2 v rows, per-warp partials
     uint8_t *  ring;
 };
+
+// Floats of attention scratch: q [hd], k and v of up to 2 in-launch tokens
+// [2][hd] each, per-warp weighted V [warps][hd], per-warp max and sum.
+__host__ __device__ constexpr size_t att_scratch_floats(int hd) {
+    return (size_t) hd * (1 + 2 + 2 + kStepConsumerWarps) + 2 * kStepConsumerWarps;
+}
 
 // This CTA's row slices and tile sizes, the same for every layer; computed
 // once per launch (each holds runtime divisions).
@@ -158,6 +165,12 @@ __device__ __forceinline__ void layer_segs(const StepArgs & a, const Plan & p, i
     segs[2] = { L.w_gate + (size_t) p.pi.r0 * a.rb_h, a.rb_h, p.pi.n, p.sr_h };
     segs[3] = { L.w_up + (size_t) p.pi.r0 * a.rb_h, a.rb_h, p.pi.n, p.sr_h };
     segs[4] = { L.w_down + (size_t) p.ph.r0 * a.rb_i, a.rb_i, p.ph.n, p.sr_i };
+}
+
+// This CTA's rows of the output head.
+__device__ __forceinline__ Seg head_seg(const StepArgs & a, const Plan & p, int c, int G) {
+    const Part pv = part(a.vocab, G, c);
+    return { a.head + (size_t) pv.r0 * a.rb_h, a.rb_h, pv.n, p.sr_h };
 }
 
 // The global abort word holds the epoch of the launch that raised it, so an
@@ -534,7 +547,227 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
     }
 }
 
-template <int M_T, int MODE>
+// Qwen3's per-head RMS norm then NEOX RoPE for one head held by one warp:
+// lane holds elements lane + 32 e (e < E), so the NEOX pair (i, i + hd/2)
+// is (x[e], x[e + E/2]) of one lane.  The same arithmetic as
+// qk_rope_cache_kernel (attention.cu): fp64 sum of fp32 squares, scale
+// 1/sqrtf(mean + eps), (x * scale) * w, then the angle recurrence
+// theta_0 = pos, theta_{i+1} = theta_i * base^(-2/hd) in fp32.
+template <int E>
+__device__ __forceinline__ void warp_head_norm_rope(float (&x)[E], const float * w, float eps, int pos,
+                                                    float theta_base, int lane) {
+    constexpr int hd = 32 * E;
+    double        ss = 0.0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        ss += (double) __fmul_rn(x[e], x[e]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    }
+    const float mean  = (float) (ss / (double) hd);
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, eps)));
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        x[e] = __fmul_rn(__fmul_rn(x[e], scale), w[lane + 32 * e]);
+    }
+    const float ts    = powf(theta_base, __fdiv_rn(-2.0f, (float) hd));
+    float       theta = (float) pos;
+    int         done  = 0;
+#pragma unroll
+    for (int e = 0; e < E / 2; ++e) {
+        const int i = lane + 32 * e;
+        for (; done < i; ++done) {
+            theta = __fmul_rn(theta, ts);
+        }
+        const float c  = cosf(theta);
+        const float sn = sinf(theta);
+        const float x0 = x[e];
+        const float x1 = x[e + E / 2];
+        x[e]           = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+        x[e + E / 2]   = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+}
+
+// Waits for this lane's E LL words of one head (elements lane + 32 e) and
+// returns their values.
+template <int E>
+__device__ __forceinline__ bool ll_head(const StepArgs & a, const Smem & s, const unsigned long long * base, int lane,
+                                        unsigned epoch, float (&x)[E]) {
+    const unsigned long long * src[E];
+    unsigned long long         w[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        src[e] = base + lane + 32 * e;
+        w[e]   = ld_ll(src[e]);
+    }
+    const bool ok = ll_settle<E>(a, s, src, w, E, epoch);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        x[e] = __uint_as_float((unsigned) (w[e] & 0xffffffffu));
+    }
+    return ok;
+}
+
+// The attention of one (query head h, token m) inside the step, by this
+// CTA's consumer warps (src/arch/qwen3-tts/operations.cpp:86-135): q and the
+// kv head's k are RMS-normed and rotated at their positions; the token's k
+// and v go to its cache row (written by the group's first query head); the
+// softmax runs over cached positions 0..pos, where positions of tokens of the
+// same slot in this launch come from their freshly computed rows, never from
+// the cache (another CTA may still be writing them).  Per-warp online
+// softmax, fixed-order merge; the head's output is published as LL words.
+template <int E>
+__device__ void attention_phase(const StepArgs & a, const Smem & s, int l, const unsigned long long * ll_qkv,
+                                unsigned long long * ll_att, size_t qkv_dim, int h, int m, int M, unsigned epoch,
+                                bool & fail) {
+    constexpr int hd    = 32 * E;
+    const int     warp  = threadIdx.x >> 5;
+    const int     lane  = threadIdx.x & 31;
+    const int     kvh   = h >> a.lg_group;
+    const int     pos   = a.pos[m];
+    const int     slot  = a.slots ? a.slots[m] : m;
+    const bool    ok    = pos >= 0 && pos < a.n_ctx && slot >= 0 && slot < a.n_cache_slots;
+    float *       sq    = s.att;
+    float *       kr    = sq + hd;          // [2][hd]
+    float *       vr    = kr + 2 * hd;      // [2][hd]
+    float *       wo    = vr + 2 * hd;      // [warps][hd]
+    float *       wm    = wo + kStepConsumerWarps * hd;
+    float *       wl    = wm + kStepConsumerWarps;
+    // tokens of this launch whose rows this token reads: same slot, position <= pos
+    int in_m[2] = { 0, 0 }, in_pos[2] = { -1, -1 }, n_in = 0;
+    for (int t = 0; t < M && ok; ++t) {
+        const int pt = a.pos[t];
+        const int st = a.slots ? a.slots[t] : t;
+        if (st == slot && pt >= 0 && pt <= pos && n_in < 2) {
+            in_m[n_in]   = t;
+            in_pos[n_in] = pt;
+            ++n_in;
+        }
+    }
+    const size_t layer_rows = (size_t) a.n_cache_slots * a.n_ctx;
+    const size_t cache_row0 = ((size_t) l * layer_rows + (size_t) (ok ? slot : 0) * a.n_ctx) * a.KV + (size_t) kvh * hd;
+    if (!ok) {
+        if (h == 0 && threadIdx.x == 0) {
+            record_device_error((unsigned) B200Q8_ERR_INVALID_ARG);
+        }
+    } else if (warp == 0) {
+        float x[E];
+        if (!ll_head<E>(a, s, ll_qkv + (size_t) m * qkv_dim + (size_t) h * hd, lane, epoch, x)) {
+            fail = true;
+        }
+        warp_head_norm_rope<E>(x, a.layers[l].q_norm, a.eps, pos, a.rope_theta, lane);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            sq[lane + 32 * e] = x[e];
+        }
+    } else if (warp <= n_in) {
+        const int t   = in_m[warp - 1];
+        float     k[E], v[E];
+        const unsigned long long * row = ll_qkv + (size_t) t * qkv_dim;
+        bool good = ll_head<E>(a, s, row + a.Q + (size_t) kvh * hd, lane, epoch, k);
+        good      = ll_head<E>(a, s, row + a.Q + a.KV + (size_t) kvh * hd, lane, epoch, v) && good;
+        if (!good) {
+            fail = true;
+        }
+        warp_head_norm_rope<E>(k, a.layers[l].k_norm, a.eps, in_pos[warp - 1], a.rope_theta, lane);
+        const bool writer = t == m && (h & ((1 << a.lg_group) - 1)) == 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            kr[(warp - 1) * hd + lane + 32 * e] = k[e];
+            vr[(warp - 1) * hd + lane + 32 * e] = v[e];
+            if (writer && good) {
+                a.k_cache[cache_row0 + (size_t) pos * a.KV + lane + 32 * e] = k[e];
+                a.v_cache[cache_row0 + (size_t) pos * a.KV + lane + 32 * e] = v[e];
+            }
+        }
+    }
+    if (fail) {
+        raise_abort(a, s);
+    }
+    if (consumers_any(fail)) {  // every consumer takes the same decision
+        fail = true;
+        return;
+    }
+    // online softmax over this warp's positions (one position per iteration)
+    const float scale = __fdiv_rn(1.0f, sqrtf((float) hd));
+    float       mx = -INFINITY, lsum = 0.0f, o[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        o[e] = 0.0f;
+    }
+    const int npos = ok ? pos + 1 : 0;
+    for (int j = warp; j < npos; j += kStepConsumerWarps) {
+        const float * kj;
+        const float * vj;
+        if (j == in_pos[0]) {  // n_in >= 1 whenever npos > 0: the token's own position
+            kj = kr;
+            vj = vr;
+        } else if (n_in > 1 && j == in_pos[1]) {
+            kj = kr + hd;
+            vj = vr + hd;
+        } else {
+            kj = a.k_cache + cache_row0 + (size_t) j * a.KV;
+            vj = a.v_cache + cache_row0 + (size_t) j * a.KV;
+        }
+        float kv[E], vv[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            kv[e] = kj[lane + 32 * e];
+            vv[e] = vj[lane + 32 * e];
+        }
+        float dot = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            dot = __fmaf_rn(sq[lane + 32 * e], kv[e], dot);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        }
+        const float sc = __fmul_rn(dot, scale);
+        const float nm = fmaxf(mx, sc);
+        const float f  = expf(mx - nm);
+        const float p  = expf(sc - nm);
+        lsum           = __fmaf_rn(lsum, f, p);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            o[e] = __fmaf_rn(o[e], f, __fmul_rn(p, vv[e]));
+        }
+        mx = nm;
+    }
+    if (lane == 0) {
+        wm[warp] = mx;
+        wl[warp] = lsum;
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        wo[warp * hd + lane + 32 * e] = o[e];
+    }
+    named_barrier_sync(1, kStepConsumers);
+    if (threadIdx.x < hd) {
+        const int d  = threadIdx.x;
+        float     M_ = -INFINITY;
+        for (int w = 0; w < kStepConsumerWarps; ++w) {
+            M_ = fmaxf(M_, wm[w]);
+        }
+        float L = 0.0f, acc = 0.0f;
+        for (int w = 0; w < kStepConsumerWarps; ++w) {
+            if (wm[w] != -INFINITY) {
+                const float f = expf(wm[w] - M_);
+                L             = __fmaf_rn(wl[w], f, L);
+                acc           = __fmaf_rn(wo[w * hd + d], f, acc);
+            }
+        }
+        st_ll(ll_att + (size_t) m * a.Q + (size_t) h * hd + d, npos > 0 ? __fdiv_rn(acc, L) : 0.0f, epoch);
+    }
+}
+
+// ATTN: the reference's attention over the KV cache (a.attn), else the
+// single cached position; a compile-time switch so the benchmark step's
+// kernel carries none of the attention code.
+template <int M_T, int MODE, bool ATTN>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int G = gridDim.x;
@@ -565,6 +798,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         s.xd[i] = reinterpret_cast<float *>(smem + off);
         off += (size_t) M_T * (Kmax / kQK) * 4;
     }
+    s.att = reinterpret_cast<float *>(smem + off);
+    if (ATTN) {
+        off += att_scratch_floats(a.head_dim) * 4;
+    }
     off    = (off + 127) & ~(size_t) 127;
     s.ring = smem + off;
     const int S = a.n_slots;
@@ -593,12 +830,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             int            sl      = 0;  // slot of tile t
             uint32_t       ph      = 0;  // fill round of slot sl, mod 2
             bool           stop    = false;
-            for (int l = 0; l < a.n_layers && !stop; ++l) {
+            for (int l = 0; l <= a.n_layers && !stop; ++l) {
                 Seg segs[5];
-                layer_segs(a, plan, l, segs);
-                for (int g = 0; g < 5 && !stop; ++g) {
+                int nsegs = 5;
+                if (l < a.n_layers) {
+                    layer_segs(a, plan, l, segs);
+                } else if (a.head != nullptr) {  // the output head after the last layer
+                    segs[0] = head_seg(a, plan, c, G);
+                    nsegs   = 1;
+                } else {
+                    break;
+                }
+                for (int g = 0; g < nsegs && !stop; ++g) {
 #ifdef B200Q8_TIMELINE
-                    if (a.timeline != nullptr && g != 3) {
+                    if (a.timeline != nullptr && g != 3 && l < a.n_layers) {
                         unsigned long long gt;
                         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
                         a.timeline[((size_t) blockIdx.x * (4 * a.n_layers) + 4 * l + (g < 3 ? g : 3)) * 8 + 5] = gt;
@@ -644,10 +889,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     // ----------------------------------------------------------- consumers
     const int t_id = threadIdx.x;
     // step input: h = x_in + get_rows(table, ids), every CTA for itself
+    // (either term may be absent: ids == nullptr or x_in == nullptr)
     for (int m = 0; m < M; ++m) {
-        const int64_t r     = a.ids[m];
+        const int64_t r     = a.ids != nullptr ? a.ids[m] : -1;
         const bool    in_tb = r >= 0 && r < a.table_rows;
-        if (!in_tb && c == 0 && t_id == 0) {
+        if (a.ids != nullptr && !in_tb && c == 0 && t_id == 0) {
             record_device_error((unsigned) B200Q8_ERR_INVALID_ARG);
         }
         for (int k = t_id; k < H; k += kStepConsumers) {
@@ -657,7 +903,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                 const float     d   = __half2float(__ushort_as_half((unsigned short) (blk[0] | (blk[1] << 8))));
                 ev                  = __fmul_rn((float) (int8_t) blk[2 + (k & 31)], d);
             }
-            s.hbuf[m * H + k] = __fadd_rn(a.x_in[(size_t) m * H + k], ev);
+            s.hbuf[m * H + k] = a.ids == nullptr  ? a.x_in[(size_t) m * H + k]
+                                : a.x_in == nullptr ? ev
+                                                    : __fadd_rn(a.x_in[(size_t) m * H + k], ev);
         }
     }
     named_barrier_sync(1, kStepConsumers);
@@ -673,13 +921,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     const Part   pq  = plan.pq;
     const Part   po  = plan.ph;
     const Part   pg  = plan.pi;
+    bool         stopped = false;
 
     for (int l = 0; l < a.n_layers; ++l) {
         const StepLayerDev &       L    = a.layers[l];
-        unsigned long long * const ll_v = a.ll + (size_t) l * a.ll_layer;
-        unsigned long long * const ll_o = ll_v + llm * a.KV;
-        unsigned long long * const ll_s = ll_o + llm * a.H;
-        unsigned long long * const ll_d = ll_s + llm * a.I;
+        unsigned long long * const ll_qkv = a.ll + (size_t) l * a.ll_layer;
+        unsigned long long * const ll_att = ll_qkv + llm * qkv_dim;
+        unsigned long long * const ll_o   = ll_att + llm * a.Q;
+        unsigned long long * const ll_s   = ll_o + llm * a.H;
+        unsigned long long * const ll_d   = ll_s + llm * a.I;
         Seg                        segs[5];
         layer_segs(a, plan, l, segs);
 
@@ -692,14 +942,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         float scale[M_T];
         // ---- qkv = W_qkv * Q(rms_norm(h) * norm_in), h = h1 + d(l-1); v published
         TL(4 * l + 0, 0);
-        const unsigned long long * prev_d = l > 0 ? a.ll + (size_t) (l - 1) * a.ll_layer + llm * (a.KV + a.H + a.I)
-                                                  : nullptr;
+        const unsigned long long * prev_d =
+            l > 0 ? a.ll + (size_t) (l - 1) * a.ll_layer + llm * (qkv_dim + a.Q + a.H + a.I) : nullptr;
         residual_and_rms<M_T>(a, s, prev_d, s.h1buf, s.hbuf, M, epoch, (l > 0 && c == 0) ? trace(l - 1, 9) : nullptr,
                               L.norm_in, fail, scale);
         TL(4 * l + 0, 1);
         if (stage_activations<M_T, MODE>(a, s, H, M, 0, s.hbuf, s.normbuf, scale, nullptr, 0, false, epoch,
                                          c == 0 ? trace(l, 0) : nullptr, (size_t) H, s.xc[0], s.xd[0], fail)) {
             stop_producer(s);
+            stopped = true;
             break;
         }
         TL(4 * l + 0, 2);
@@ -711,8 +962,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
 #pragma unroll
                                 for (int m = 0; m < M_T; ++m) {
                                     if (m < M) {
-                                        if (row >= a.Q + a.KV) {
-                                            st_ll(ll_v + (size_t) m * a.KV + (row - a.Q - a.KV), y[m], epoch);
+                                        if (ATTN || row >= a.Q + a.KV) {
+                                            st_ll(ll_qkv + (size_t) m * qkv_dim + row, y[m], epoch);
                                         }
                                         if (tq) {
                                             tq[(size_t) m * qkv_dim + row] = y[m];
@@ -726,14 +977,35 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
             stop_producer(s);
+            stopped = true;
             break;
         }
-        // ---- o = W_o * Q(attend(v)); attention over one cached position; o published
+        // ---- attention: one CTA per (query head, token) publishes the head's output
+        if (ATTN) {
+            const int n_head = a.Q >> a.lg_head_dim;
+            if (c < n_head * M) {
+                const int hh = c % n_head, mm = c / n_head;
+                switch (a.head_dim) {
+                    case 64: attention_phase<2>(a, s, l, ll_qkv, ll_att, qkv_dim, hh, mm, M, epoch, fail); break;
+                    case 128: attention_phase<4>(a, s, l, ll_qkv, ll_att, qkv_dim, hh, mm, M, epoch, fail); break;
+                    case 192: attention_phase<6>(a, s, l, ll_qkv, ll_att, qkv_dim, hh, mm, M, epoch, fail); break;
+                    default: attention_phase<8>(a, s, l, ll_qkv, ll_att, qkv_dim, hh, mm, M, epoch, fail); break;
+                }
+                if (consumers_any(fail || aborted(a, s))) {
+                    stop_producer(s);
+                    stopped = true;
+                    break;
+                }
+            }
+        }
+        // ---- o = W_o * Q(attend); attention over the cache, or over one cached position; o published
         TL(4 * l + 1, 0);
-        if (stage_activations<M_T, MODE>(a, s, a.Q, M, 1, nullptr, nullptr, no_scale, ll_v, (size_t) a.KV, true,
-                                         epoch, c == 0 ? trace(l, 2) : nullptr, (size_t) a.Q, s.xc[1], s.xd[1],
-                                         fail)) {
+        const unsigned long long * o_src = ATTN ? ll_att : ll_qkv + a.Q + a.KV;
+        if (stage_activations<M_T, MODE>(a, s, a.Q, M, 1, nullptr, nullptr, no_scale, o_src,
+                                         ATTN ? (size_t) a.Q : (size_t) qkv_dim, !ATTN, epoch,
+                                         c == 0 ? trace(l, 2) : nullptr, (size_t) a.Q, s.xc[1], s.xd[1], fail)) {
             stop_producer(s);
+            stopped = true;
             break;
         }
         TL(4 * l + 1, 2);
@@ -757,6 +1029,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
             stop_producer(s);
+            stopped = true;
             break;
         }
         // ---- g|u = W_gate|W_up * Q(rms_norm(h1) * norm_post), h1 = h + o; s = silu(g)*u published
@@ -767,6 +1040,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (stage_activations<M_T, MODE>(a, s, H, M, 0, s.h1buf, s.normbuf, scale, nullptr, 0, false, epoch,
                                          c == 0 ? trace(l, 5) : nullptr, (size_t) H, s.xc[0], s.xd[0], fail)) {
             stop_producer(s);
+            stopped = true;
             break;
         }
         TL(4 * l + 2, 2);
@@ -796,6 +1070,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
             stop_producer(s);
+            stopped = true;
             break;
         }
         // ---- d = W_down * Q(s); d published (the last layer writes h_out = h1 + d)
@@ -803,6 +1078,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (stage_activations<M_T, MODE>(a, s, a.I, M, 1, nullptr, nullptr, no_scale, ll_s, (size_t) a.I, false,
                                          epoch, nullptr, 0, s.xc[1], s.xd[1], fail)) {
             stop_producer(s);
+            stopped = true;
             break;
         }
         TL(4 * l + 3, 2);
@@ -815,7 +1091,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
 #pragma unroll
                                 for (int m = 0; m < M_T; ++m) {
                                     if (m < M) {
-                                        if (last) {
+                                        if (last && a.head == nullptr) {
                                             a.h_out[(size_t) m * H + row] = __fadd_rn(s.h1buf[m * H + row], y[m]);
                                         } else {
                                             st_ll(ll_d + (size_t) m * a.H + row, y[m], epoch);
@@ -832,7 +1108,39 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || aborted(a, s))) {
             stop_producer(s);
+            stopped = true;
             break;
+        }
+    }
+    if (stopped || fail || a.head == nullptr) {
+        return;
+    }
+    // ---- output: h = h1 + d (CTA 0 writes h_out), hidden = rms_norm(h) * out_norm
+    // (CTA 0 writes hidden_out), logits = head * Q(hidden)
+    {
+        const unsigned long long * last_d =
+            a.ll + (size_t) (a.n_layers - 1) * a.ll_layer + llm * (qkv_dim + a.Q + a.H + a.I);
+        float scale[M_T];
+        residual_and_rms<M_T>(a, s, last_d, s.h1buf, s.hbuf, M, epoch, c == 0 ? a.h_out : nullptr, a.out_norm, fail,
+                              scale);
+        if (stage_activations<M_T, MODE>(a, s, H, M, 0, s.hbuf, s.normbuf, scale, nullptr, 0, false, epoch,
+                                         c == 0 ? a.hidden_out : nullptr, (size_t) H, s.xc[0], s.xd[0], fail)) {
+            stop_producer(s);
+            return;
+        }
+        const Seg  hs = head_seg(a, plan, c, G);
+        const Part pv = part(a.vocab, G, c);
+        consume_op<M_T>(a, s, S, sl, ph, &hs, 1, false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 0,
+                        [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
+#pragma unroll
+                            for (int m = 0; m < M_T; ++m) {
+                                if (m < M) {
+                                    a.logits[(size_t) m * a.vocab + pv.r0 + u] = y[m];
+                                }
+                            }
+                        });
+        if (consumers_any(fail || aborted(a, s))) {
+            stop_producer(s);
         }
     }
 }
@@ -847,6 +1155,9 @@ size_t decode_step_smem_bytes(const StepArgs & a, int mt, int & n_slots) {
     off += (size_t) mt * 2 * kStepYMax * 4;
     off += 2 * (size_t) mt * Kmax;
     off += 2 * (size_t) mt * (Kmax / kQK) * 4;
+    if (a.attn) {
+        off += att_scratch_floats(a.head_dim) * 4;
+    }
     off                   = (off + 127) & ~(size_t) 127;
     const size_t limit    = 227 * 1024;
     if (off + kStepSlotBytes * 2 > limit) {
@@ -872,6 +1183,16 @@ bool decode_step_supported(const StepArgs & a, int G) {
     if (a.rb_i > (size_t) kStepSlotBytes || a.rb_q > (size_t) kStepSlotBytes || a.rb_h > (size_t) kStepSlotBytes) {
         return false;
     }
+    // attention: one CTA per (query head, token); a warp holds a head in
+    // lanes of head_dim/32 elements whose NEOX pairs stay in one lane
+    if (a.attn && (a.head_dim % 64 != 0 || a.head_dim > 256 || (a.Q / a.head_dim) * a.M > G ||
+                   a.pos == nullptr || a.k_cache == nullptr || a.v_cache == nullptr || !(a.rope_theta > 0.0f))) {
+        return false;
+    }
+    if (a.head != nullptr && (a.vocab < 1 || (a.vocab + G - 1) / G > kStepYMax || a.logits == nullptr ||
+                              a.hidden_out == nullptr || a.out_norm == nullptr)) {
+        return false;
+    }
     int slots = 0;
     if (decode_step_smem_bytes(a, a.M <= 1 ? 1 : 2, slots) == 0 || slots < 2) {
         return false;
@@ -882,23 +1203,31 @@ bool decode_step_supported(const StepArgs & a, int G) {
         const int sr   = std::max(1, (int) (kStepSlotBytes / rb));
         return (rows + sr - 1) / sr;
     };
-    const int worst = std::max(std::max(tiles(qkv, a.rb_h), tiles(a.H, a.rb_q)),
-                               std::max(2 * tiles(a.I, a.rb_h), tiles(a.H, a.rb_i)));
+    const int worst = std::max(std::max(std::max(tiles(qkv, a.rb_h), tiles(a.H, a.rb_q)),
+                                        std::max(2 * tiles(a.I, a.rb_h), tiles(a.H, a.rb_i))),
+                               a.head != nullptr ? tiles(a.vocab, a.rb_h) : 0);
     return worst <= std::min(slots, 16);
 }
 
 namespace {
 using StepFn = void (*)(const StepArgs);
 
-StepFn pick_step_kernel(int mode, int mt) {
+template <bool ATTN>
+StepFn pick_step_kernel_t(int mode, int mt) {
     switch (mode) {
         case B200Q8_QUANT_CPU_X86:
-            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_X86> : decode_step_kernel<2, B200Q8_QUANT_CPU_X86>;
+            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_X86, ATTN>
+                           : decode_step_kernel<2, B200Q8_QUANT_CPU_X86, ATTN>;
         case B200Q8_QUANT_CPU_ARM:
-            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_ARM> : decode_step_kernel<2, B200Q8_QUANT_CPU_ARM>;
+            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_ARM, ATTN>
+                           : decode_step_kernel<2, B200Q8_QUANT_CPU_ARM, ATTN>;
         default:
-            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_REF> : decode_step_kernel<2, B200Q8_QUANT_REF>;
+            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_REF, ATTN> : decode_step_kernel<2, B200Q8_QUANT_REF, ATTN>;
     }
+}
+
+StepFn pick_step_kernel(int mode, int mt, bool attn) {
+    return attn ? pick_step_kernel_t<true>(mode, mt) : pick_step_kernel_t<false>(mode, mt);
 }
 }  // namespace
 
@@ -908,7 +1237,7 @@ bool decode_step_fits(const StepArgs & a) {
     for (int mt = 1; mt <= 2; ++mt) {
         int          slots = 0;
         const size_t smem  = decode_step_smem_bytes(a, mt, slots);
-        StepFn       fn    = pick_step_kernel(a.mode, mt);
+        StepFn       fn    = pick_step_kernel(a.mode, mt, a.attn != 0);
         if (smem == 0 || cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess) {
             cudaGetLastError();
             return false;
@@ -927,7 +1256,7 @@ cudaError_t launch_decode_step(StepArgs a, int G, cudaStream_t stream) {
     int       slots = 0;
     const size_t smem = decode_step_smem_bytes(a, mt, slots);
     a.n_slots         = slots;
-    StepFn fn = pick_step_kernel(a.mode, mt);
+    StepFn fn = pick_step_kernel(a.mode, mt, a.attn != 0);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     if (e != cudaSuccess) {
         return e;

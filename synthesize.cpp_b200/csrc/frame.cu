@@ -450,20 +450,32 @@ b200q8_status_t b200q8_frame_run(b200q8_frame * f, const b200q8_frame_args * a, 
         }
     }
     if (exec == nullptr) {
-        cudaGraph_t graph = nullptr;
-        e                 = cudaStreamBeginCapture(f->cap, cudaStreamCaptureModeThreadLocal);
-        if (e == cudaSuccess) {
-            const cudaError_t e2 = enqueue_frame(f, f->cap, key);
-            e                    = cudaStreamEndCapture(f->cap, &graph);
-            if (e2 != cudaSuccess) {
-                e = e2;
+        for (int attempt = 0; attempt < 2; ++attempt) {
+            cudaGraph_t graph = nullptr;
+            exec              = nullptr;
+            e                 = cudaStreamBeginCapture(f->cap, cudaStreamCaptureModeThreadLocal);
+            if (e == cudaSuccess) {
+                const cudaError_t e2 = enqueue_frame(f, f->cap, key);
+                e                    = cudaStreamEndCapture(f->cap, &graph);
+                if (e2 != cudaSuccess) {
+                    e = e2;
+                }
             }
-        }
-        if (e == cudaSuccess) {
-            e = cudaGraphInstantiate(&exec, graph, 0);
-        }
-        if (graph) {
-            cudaGraphDestroy(graph);
+            if (e == cudaSuccess) {
+                e = cudaGraphInstantiate(&exec, graph, 0);
+            }
+            if (graph) {
+                cudaGraphDestroy(graph);
+            }
+            const bool persistent = chain_persistent_in_graph(f->talker, false) ||
+                                    chain_persistent_in_graph(f->predictor, false);
+            if (e == cudaSuccess || attempt > 0 || !persistent) {
+                break;
+            }
+            // a graph that cannot hold the persistent steps' cooperative launches: per-op steps instead
+            cudaGetLastError();
+            chain_persistent_in_graph(f->talker, true);
+            chain_persistent_in_graph(f->predictor, true);
         }
         if (e != cudaSuccess) {
             cudaSetDevice(prev);

@@ -137,6 +137,8 @@ struct StepLayerDev {
     const uint8_t * w_down;  // [H rows] of K = I
     const float *   norm_in;
     const float *   norm_post;
+    const float *   q_norm;  // [head_dim] (attention steps only)
+    const float *   k_norm;
 };
 
 struct StepArgs {
@@ -153,9 +155,26 @@ struct StepArgs {
     float *              h_out;
     int                  M;
     int                  mode;
-    unsigned long long * ll;        // LL words, per layer [v | o | s | d], each [ll_m][width]
+    // LL words, per layer [qkv | att | o | s | d], each [ll_m][width]
+    // (width Q + 2 KV, Q, H, I, H)
+    unsigned long long * ll;
     size_t               ll_layer;  // words per layer
     int                  ll_m;      // token stride of the LL buffers
+    // attention over the KV cache (attn != 0; else the single cached position)
+    int                  attn;
+    float                rope_theta;
+    const int32_t *      pos;       // [M]
+    const int32_t *      slots;     // [M] or nullptr: slot m
+    int                  n_ctx, n_cache_slots;
+    float *              k_cache;   // [n_layers][n_cache_slots][n_ctx][KV]
+    float *              v_cache;
+    // output stage (head != nullptr): hidden_out = rms_norm(h) * out_norm,
+    // logits = head * Q(hidden_out); h_out is written in full either way
+    const float *        out_norm;
+    const uint8_t *      head;      // [vocab rows] of K = H
+    int                  vocab;
+    float *              hidden_out;
+    float *              logits;
     float *              trace;     // optional per-layer activation copies (chain buffer layout)
     size_t               trace_layer;
     size_t               trace_off[10];
