@@ -185,6 +185,14 @@ __device__ void raise_abort(const StepArgs & a, const Smem & s) {
     atomicExch(&a.sync[1], *(volatile unsigned *) s.epoch);
 }
 
+// This CTA's own stop flag (set by raise_abort and stop_producer).  The
+// barriers between ops check only this: another CTA's abort reaches this one
+// through the global word, which every bounded wait polls, so a barrier need
+// not pay an L2 round trip for it.
+__device__ __forceinline__ bool local_stop(const Smem & s) {
+    return *(volatile int *) s.abort_local != 0;
+}
+
 // Consumers that stop early tell their producer, which then stops waiting
 // for slots to be released.
 __device__ __forceinline__ void stop_producer(const Smem & s) {
@@ -406,7 +414,7 @@ __device__ bool stage_activations_t(const StepArgs & a, const Smem & s, int K, i
             }
         }
     }
-    return consumers_any(fail || aborted(a, s));
+    return consumers_any(fail || local_stop(s));
 }
 
 // One round per token whatever K is: 8 lanes per block up to 32*kStepConsumerWarps/8
@@ -690,18 +698,32 @@ __device__ void attention_phase(const StepArgs & a, const Smem & s, int l, const
         fail = true;
         return;
     }
-    // online softmax over this warp's positions (one position per iteration)
-    const float scale = __fdiv_rn(1.0f, sqrtf((float) hd));
-    float       mx = -INFINITY, lsum = 0.0f, o[E];
+    // Online softmax over this warp's positions: a group of LPP = hd/16 lanes
+    // takes one position (lane gl of the group holds elements 16 gl .. 16 gl
+    // + 15, read as four 16-byte words), so a warp covers 32/LPP positions per
+    // round and every warp is busy even for a short prefix.
+    constexpr int LPP  = hd / 16;
+    constexpr int PPW  = 32 / LPP;
+    const int     grp  = lane / LPP;
+    const int     gl   = lane % LPP;
+    const float   scale = __fdiv_rn(1.0f, sqrtf((float) hd));
+    float         mx = -INFINITY, lsum = 0.0f, o[16];
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
+    for (int e = 0; e < 16; ++e) {
         o[e] = 0.0f;
     }
     const int npos = ok ? pos + 1 : 0;
-    for (int j = warp; j < npos; j += kStepConsumerWarps) {
+    float     qv[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        qv[e] = sq[16 * gl + e];
+    }
+    for (int base = warp * PPW; base < npos; base += kStepConsumerWarps * PPW) {  // warp-uniform
+        const int  j      = base + grp;
+        const bool active = j < npos;
         const float * kj;
         const float * vj;
-        if (j == in_pos[0]) {  // n_in >= 1 whenever npos > 0: the token's own position
+        if (!active || j == in_pos[0]) {  // n_in >= 1 whenever npos > 0: the token's own position
             kj = kr;
             vj = vr;
         } else if (n_in > 1 && j == in_pos[1]) {
@@ -711,29 +733,55 @@ __device__ void attention_phase(const StepArgs & a, const Smem & s, int l, const
             kj = a.k_cache + cache_row0 + (size_t) j * a.KV;
             vj = a.v_cache + cache_row0 + (size_t) j * a.KV;
         }
-        float kv[E], vv[E];
+        const float4 * k4 = reinterpret_cast<const float4 *>(kj + 16 * gl);
+        const float4 * v4 = reinterpret_cast<const float4 *>(vj + 16 * gl);
+        float4         kk[4], vv[4];
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-            kv[e] = kj[lane + 32 * e];
-            vv[e] = vj[lane + 32 * e];
+        for (int q = 0; q < 4; ++q) {
+            kk[q] = k4[q];
+            vv[q] = v4[q];
         }
         float dot = 0.0f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-            dot = __fmaf_rn(sq[lane + 32 * e], kv[e], dot);
+        for (int q = 0; q < 4; ++q) {
+            dot = __fmaf_rn(qv[4 * q + 0], kk[q].x, dot);
+            dot = __fmaf_rn(qv[4 * q + 1], kk[q].y, dot);
+            dot = __fmaf_rn(qv[4 * q + 2], kk[q].z, dot);
+            dot = __fmaf_rn(qv[4 * q + 3], kk[q].w, dot);
         }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
+        for (int off = LPP / 2; off > 0; off >>= 1) {
             dot += __shfl_xor_sync(0xffffffffu, dot, off);
         }
-        const float sc = __fmul_rn(dot, scale);
-        const float nm = fmaxf(mx, sc);
-        const float f  = expf(mx - nm);
-        const float p  = expf(sc - nm);
-        lsum           = __fmaf_rn(lsum, f, p);
+        if (active) {
+            const float sc = __fmul_rn(dot, scale);
+            const float nm = fmaxf(mx, sc);
+            const float f  = expf(mx - nm);  // 0 on the group's first position (mx = -inf)
+            const float p  = expf(sc - nm);
+            lsum           = __fmaf_rn(lsum, f, p);
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-            o[e] = __fmaf_rn(o[e], f, __fmul_rn(p, vv[e]));
+            for (int q = 0; q < 4; ++q) {
+                o[4 * q + 0] = __fmaf_rn(o[4 * q + 0], f, __fmul_rn(p, vv[q].x));
+                o[4 * q + 1] = __fmaf_rn(o[4 * q + 1], f, __fmul_rn(p, vv[q].y));
+                o[4 * q + 2] = __fmaf_rn(o[4 * q + 2], f, __fmul_rn(p, vv[q].z));
+                o[4 * q + 3] = __fmaf_rn(o[4 * q + 3], f, __fmul_rn(p, vv[q].w));
+            }
+            mx = nm;
+        }
+    }
+    // merge the warp's groups (butterfly over the lanes holding the same elements)
+#pragma unroll
+    for (int off = LPP; off < 32; off <<= 1) {
+        const float omx = __shfl_xor_sync(0xffffffffu, mx, off);
+        const float ol  = __shfl_xor_sync(0xffffffffu, lsum, off);
+        const float nm  = fmaxf(mx, omx);
+        const float f1  = mx == -INFINITY ? 0.0f : expf(mx - nm);
+        const float f2  = omx == -INFINITY ? 0.0f : expf(omx - nm);
+        lsum            = __fmaf_rn(lsum, f1, __fmul_rn(ol, f2));
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const float oo = __shfl_xor_sync(0xffffffffu, o[e], off);
+            o[e]           = __fmaf_rn(o[e], f1, __fmul_rn(oo, f2));
         }
         mx = nm;
     }
@@ -741,9 +789,11 @@ __device__ void attention_phase(const StepArgs & a, const Smem & s, int l, const
         wm[warp] = mx;
         wl[warp] = lsum;
     }
+    if (grp == 0) {
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-        wo[warp * hd + lane + 32 * e] = o[e];
+        for (int e = 0; e < 16; ++e) {
+            wo[warp * hd + 16 * gl + e] = o[e];
+        }
     }
     named_barrier_sync(1, kStepConsumers);
     if (threadIdx.x < hd) {
@@ -975,7 +1025,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 0, 3);
         // park warps that are done until the whole op is: a warp polling the
         // next op's inputs would steal issue slots from warps still computing
-        if (consumers_any(fail || aborted(a, s))) {
+        if (consumers_any(fail || local_stop(s))) {
             stop_producer(s);
             stopped = true;
             break;
@@ -988,10 +1038,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                 switch (a.head_dim) {
                     case 64: attention_phase<2>(a, s, l, ll_qkv, ll_att, qkv_dim, hh, mm, M, epoch, fail); break;
                     case 128: attention_phase<4>(a, s, l, ll_qkv, ll_att, qkv_dim, hh, mm, M, epoch, fail); break;
-                    case 192: attention_phase<6>(a, s, l, ll_qkv, ll_att, qkv_dim, hh, mm, M, epoch, fail); break;
                     default: attention_phase<8>(a, s, l, ll_qkv, ll_att, qkv_dim, hh, mm, M, epoch, fail); break;
                 }
-                if (consumers_any(fail || aborted(a, s))) {
+                if (consumers_any(fail || local_stop(s))) {
                     stop_producer(s);
                     stopped = true;
                     break;
@@ -1027,7 +1076,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 1, 3);
         // park warps that are done until the whole op is: a warp polling the
         // next op's inputs would steal issue slots from warps still computing
-        if (consumers_any(fail || aborted(a, s))) {
+        if (consumers_any(fail || local_stop(s))) {
             stop_producer(s);
             stopped = true;
             break;
@@ -1068,7 +1117,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 2, 3);
         // park warps that are done until the whole op is: a warp polling the
         // next op's inputs would steal issue slots from warps still computing
-        if (consumers_any(fail || aborted(a, s))) {
+        if (consumers_any(fail || local_stop(s))) {
             stop_producer(s);
             stopped = true;
             break;
@@ -1106,7 +1155,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 3, 3);
         // park warps that are done until the whole op is: a warp polling the
         // next op's inputs would steal issue slots from warps still computing
-        if (consumers_any(fail || aborted(a, s))) {
+        if (consumers_any(fail || local_stop(s))) {
             stop_producer(s);
             stopped = true;
             break;
@@ -1139,7 +1188,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                                 }
                             }
                         });
-        if (consumers_any(fail || aborted(a, s))) {
+        if (consumers_any(fail || local_stop(s))) {
             stop_producer(s);
         }
     }
@@ -1184,8 +1233,9 @@ bool decode_step_supported(const StepArgs & a, int G) {
         return false;
     }
     // attention: one CTA per (query head, token); a warp holds a head in
-    // lanes of head_dim/32 elements whose NEOX pairs stay in one lane
-    if (a.attn && (a.head_dim % 64 != 0 || a.head_dim > 256 || (a.Q / a.head_dim) * a.M > G ||
+    // lanes of head_dim/32 elements whose NEOX pairs stay in one lane, and
+    // head_dim/16 lanes share a cached position (head_dim 64, 128 or 256)
+    if (a.attn && ((a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) || (a.Q / a.head_dim) * a.M > G ||
                    a.pos == nullptr || a.k_cache == nullptr || a.v_cache == nullptr || !(a.rope_theta > 0.0f))) {
         return false;
     }
