@@ -115,6 +115,13 @@ __device__ __forceinline__ int seg_tiles(const Seg & s) {
     return t;
 }
 
+// Token facts the attention CTAs keep for the whole launch (header words).
+struct AttTok {
+    int pos[2];
+    int slot[2];
+    int ok[2];
+};
+
 struct Smem {
     uint64_t * full;
     uint64_t * empty;
@@ -129,14 +136,27 @@ struct Smem {
     uint8_t *  xc[2];      // staged codes [M_T][Kmax], double buffered by op parity
     float *    xd[2];      // staged scales [M_T][Kmax/32]
     float *    att;        // attention scratch (attention steps): q, 2 k, 2 v rows, per-warp partials
+    AttTok *   tok;        // attention steps: positions and slots of the launch's tokens
     uint8_t *  ring;
 };
 
 // Floats of attention scratch: q [hd], k and v of up to 2 in-launch tokens
-// [2][hd] each, per-warp weighted V [warps][hd], per-warp max and sum.
+// [2][hd] each, per-warp weighted V [warps][hd], per-warp max and sum, the
+// layer's q_norm and k_norm [hd] each, and per token of the launch the RoPE
+// cos and sin at its position [2][hd] (cos at i, sin at hd/2 + i).
 __host__ __device__ constexpr size_t att_scratch_floats(int hd) {
+    return (size_t) hd * (1 + 2 + 2 + kStepConsumerWarps) + 2 * kStepConsumerWarps + 2 * (size_t) hd + 2 * (size_t) hd;
+}
+
+// Offsets (floats) in the attention scratch of q_norm / k_norm and of the
+// RoPE table.
+__host__ __device__ constexpr size_t att_norm_offset(int hd) {
     return (size_t) hd * (1 + 2 + 2 + kStepConsumerWarps) + 2 * kStepConsumerWarps;
 }
+__host__ __device__ constexpr size_t att_rope_offset(int hd) {
+    return att_norm_offset(hd) + 2 * (size_t) hd;
+}
+
 
 // This CTA's row slices and tile sizes, the same for every layer; computed
 // once per launch (each holds runtime divisions).
@@ -559,11 +579,25 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
 // lane holds elements lane + 32 e (e < E), so the NEOX pair (i, i + hd/2)
 // is (x[e], x[e + E/2]) of one lane.  The same arithmetic as
 // qk_rope_cache_kernel (attention.cu): fp64 sum of fp32 squares, scale
-// 1/sqrtf(mean + eps), (x * scale) * w, then the angle recurrence
-// theta_0 = pos, theta_{i+1} = theta_i * base^(-2/hd) in fp32.
+// 1/sqrtf(mean + eps), (x * scale) * w, then the rotation by cs (cos and
+// sin of the angles at the token's position, from rope_table).
+
+// cos and sin of the RoPE angles of position pos, for i < hd/2: the angle
+// recurrence theta_0 = pos, theta_{i+1} = theta_i * base^(-2/hd) in fp32 (as
+// qk_rope_cache_kernel computes it), then cosf / sinf.  cs[i] = cos,
+// cs[hd/2 + i] = sin.
+__device__ __forceinline__ void rope_entry(float * cs, int hd, int i, int pos, float theta_base) {
+    const float ts    = powf(theta_base, __fdiv_rn(-2.0f, (float) hd));
+    float       theta = (float) pos;
+    for (int k = 0; k < i; ++k) {
+        theta = __fmul_rn(theta, ts);
+    }
+    cs[i]          = cosf(theta);
+    cs[hd / 2 + i] = sinf(theta);
+}
 template <int E>
-__device__ __forceinline__ void warp_head_norm_rope(float (&x)[E], const float * w, float eps, int pos,
-                                                    float theta_base, int lane) {
+__device__ __forceinline__ void warp_head_norm_rope(float (&x)[E], const float * w, float eps, const float * cs,
+                                                    int lane) {
     constexpr int hd = 32 * E;
     double        ss = 0.0;
 #pragma unroll
@@ -580,17 +614,11 @@ __device__ __forceinline__ void warp_head_norm_rope(float (&x)[E], const float *
     for (int e = 0; e < E; ++e) {
         x[e] = __fmul_rn(__fmul_rn(x[e], scale), w[lane + 32 * e]);
     }
-    const float ts    = powf(theta_base, __fdiv_rn(-2.0f, (float) hd));
-    float       theta = (float) pos;
-    int         done  = 0;
 #pragma unroll
     for (int e = 0; e < E / 2; ++e) {
-        const int i = lane + 32 * e;
-        for (; done < i; ++done) {
-            theta = __fmul_rn(theta, ts);
-        }
-        const float c  = cosf(theta);
-        const float sn = sinf(theta);
+        const int   i  = lane + 32 * e;
+        const float c  = cs[i];
+        const float sn = cs[hd / 2 + i];
         const float x0 = x[e];
         const float x1 = x[e + E / 2];
         x[e]           = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
@@ -618,6 +646,31 @@ __device__ __forceinline__ bool ll_head(const StepArgs & a, const Smem & s, cons
     return ok;
 }
 
+// Waits for this lane's words of one kv head's k and v together.
+template <int E>
+__device__ __forceinline__ bool ll_head_kv(const StepArgs & a, const Smem & s, const unsigned long long * kbase,
+                                           const unsigned long long * vbase, int lane, unsigned epoch, float (&k)[E],
+                                           float (&v)[E]) {
+    const unsigned long long * src[2 * E];
+    unsigned long long         w[2 * E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        src[e]     = kbase + lane + 32 * e;
+        src[E + e] = vbase + lane + 32 * e;
+    }
+#pragma unroll
+    for (int i = 0; i < 2 * E; ++i) {
+        w[i] = ld_ll(src[i]);
+    }
+    const bool ok = ll_settle<2 * E>(a, s, src, w, 2 * E, epoch);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        k[e] = __uint_as_float((unsigned) (w[e] & 0xffffffffu));
+        v[e] = __uint_as_float((unsigned) (w[E + e] & 0xffffffffu));
+    }
+    return ok;
+}
+
 // The attention of one (query head h, token m) inside the step, by this
 // CTA's consumer warps (src/arch/qwen3-tts/operations.cpp:86-135): q and the
 // kv head's k are RMS-normed and rotated at their positions; the token's k
@@ -634,21 +687,24 @@ __device__ void attention_phase(const StepArgs & a, const Smem & s, int l, const
     const int     warp  = threadIdx.x >> 5;
     const int     lane  = threadIdx.x & 31;
     const int     kvh   = h >> a.lg_group;
-    const int     pos   = a.pos[m];
-    const int     slot  = a.slots ? a.slots[m] : m;
-    const bool    ok    = pos >= 0 && pos < a.n_ctx && slot >= 0 && slot < a.n_cache_slots;
+    const int     pos   = s.tok->pos[m];
+    const int     slot  = s.tok->slot[m];
+    const bool    ok    = s.tok->ok[m] != 0;
     float *       sq    = s.att;
     float *       kr    = sq + hd;          // [2][hd]
     float *       vr    = kr + 2 * hd;      // [2][hd]
     float *       wo    = vr + 2 * hd;      // [warps][hd]
     float *       wm    = wo + kStepConsumerWarps * hd;
     float *       wl    = wm + kStepConsumerWarps;
+    const float * qn    = wl + kStepConsumerWarps;
+    const float * kn    = qn + hd;
+    const float * cs    = kn + hd;          // [2][hd]
     // tokens of this launch whose rows this token reads: same slot, position <= pos
     int in_m[2] = { 0, 0 }, in_pos[2] = { -1, -1 }, n_in = 0;
     for (int t = 0; t < M && ok; ++t) {
-        const int pt = a.pos[t];
-        const int st = a.slots ? a.slots[t] : t;
-        if (st == slot && pt >= 0 && pt <= pos && n_in < 2) {
+        const int pt = s.tok->pos[t];
+        const int st = s.tok->slot[t];
+        if (s.tok->ok[t] && st == slot && pt <= pos && n_in < 2) {
             in_m[n_in]   = t;
             in_pos[n_in] = pt;
             ++n_in;
@@ -665,7 +721,7 @@ __device__ void attention_phase(const StepArgs & a, const Smem & s, int l, const
         if (!ll_head<E>(a, s, ll_qkv + (size_t) m * qkv_dim + (size_t) h * hd, lane, epoch, x)) {
             fail = true;
         }
-        warp_head_norm_rope<E>(x, a.layers[l].q_norm, a.eps, pos, a.rope_theta, lane);
+        warp_head_norm_rope<E>(x, qn, a.eps, cs + m * hd, lane);
 #pragma unroll
         for (int e = 0; e < E; ++e) {
             sq[lane + 32 * e] = x[e];
@@ -674,12 +730,12 @@ __device__ void attention_phase(const StepArgs & a, const Smem & s, int l, const
         const int t   = in_m[warp - 1];
         float     k[E], v[E];
         const unsigned long long * row = ll_qkv + (size_t) t * qkv_dim;
-        bool good = ll_head<E>(a, s, row + a.Q + (size_t) kvh * hd, lane, epoch, k);
-        good      = ll_head<E>(a, s, row + a.Q + a.KV + (size_t) kvh * hd, lane, epoch, v) && good;
+        const bool good = ll_head_kv<E>(a, s, row + a.Q + (size_t) kvh * hd, row + a.Q + a.KV + (size_t) kvh * hd,
+                                        lane, epoch, k, v);
         if (!good) {
             fail = true;
         }
-        warp_head_norm_rope<E>(k, a.layers[l].k_norm, a.eps, in_pos[warp - 1], a.rope_theta, lane);
+        warp_head_norm_rope<E>(k, kn, a.eps, cs + t * hd, lane);
         const bool writer = t == m && (h & ((1 << a.lg_group) - 1)) == 0;
 #pragma unroll
         for (int e = 0; e < E; ++e) {
@@ -833,6 +889,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     s.abort_local = reinterpret_cast<int *>(smem + 260);
     s.rms_scale   = reinterpret_cast<float *>(smem + 264);
     s.rms_part    = reinterpret_cast<double *>(smem + 512);
+    s.tok         = reinterpret_cast<AttTok *>(smem + 1024);
     size_t off    = kStepHeader;
     s.hbuf        = reinterpret_cast<float *>(smem + off);
     off += (size_t) M_T * H * 4;
@@ -958,6 +1015,31 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                                                     : __fadd_rn(a.x_in[(size_t) m * H + k], ev);
         }
     }
+    // attention: the tokens' positions and slots, and (attention CTAs) the
+    // RoPE cos / sin at each token's position, once per launch
+    const bool att_cta = ATTN && c < (a.Q >> a.lg_head_dim) * M;
+    if (ATTN) {
+        if (t_id < 2) {
+            int p = 0, sl = 0, okv = 0;
+            if (t_id < M) {
+                p   = a.pos[t_id];
+                sl  = a.slots ? a.slots[t_id] : t_id;
+                okv = p >= 0 && p < a.n_ctx && sl >= 0 && sl < a.n_cache_slots;
+            }
+            s.tok->pos[t_id]  = p;
+            s.tok->slot[t_id] = sl;
+            s.tok->ok[t_id]   = okv;
+        }
+        if (att_cta) {
+            const int hd = a.head_dim;
+            for (int idx = t_id; idx < M * (hd / 2); idx += kStepConsumers) {
+                const int m = idx / (hd / 2);
+                const int p = a.pos[m];
+                rope_entry(s.att + att_rope_offset(hd) + (size_t) m * hd, hd, idx % (hd / 2),
+                           p >= 0 && p < a.n_ctx ? p : 0, a.rope_theta);
+            }
+        }
+    }
     named_barrier_sync(1, kStepConsumers);
 
     const int qkv_dim = a.Q + 2 * a.KV;
@@ -982,6 +1064,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         unsigned long long * const ll_d   = ll_s + llm * a.I;
         Seg                        segs[5];
         layer_segs(a, plan, l, segs);
+        if (att_cta) {  // this layer's q_norm / k_norm, read after the qkv op
+            float * qk = s.att + att_norm_offset(a.head_dim);
+            for (int i = t_id; i < 2 * a.head_dim; i += kStepConsumers) {
+                qk[i] = i < a.head_dim ? L.q_norm[i] : L.k_norm[i - a.head_dim];
+            }
+        }
 
         // Staged activations alternate between two buffers op by op.
         float no_scale[M_T];
