@@ -233,12 +233,7 @@ bool persistent_args(b200q8_chain * c, const StepIO & io, StepArgs & a) {
         a.hidden_out = io.hidden_out; a.logits = io.logits;
     }
 #ifdef B200Q8_TIMELINE
-    if (c->timeline == nullptr) {
-        cudaMalloc(&c->timeline, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms);
-        cudaMemset(c->timeline, 0, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms);
-        c->owned.push_back(c->timeline);
-    }
-    a.timeline = static_cast<unsigned long long *>(c->timeline);
+    a.timeline = static_cast<unsigned long long *>(c->timeline);  // allocated by chain_create
 #endif
     return decode_step_supported(a, c->sms);
 }
@@ -655,6 +650,14 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
         probe.H = (int) H; probe.Q = (int) (d.n_head * d.head_dim); probe.KV = (int) KV; probe.I = (int) I;
         probe.mode = d.mode; probe.attn = c->attn ? 1 : 0; probe.head_dim = (int) d.head_dim;
         c->persistent = e == cudaSuccess && decode_step_fits(probe);
+#ifdef B200Q8_TIMELINE
+        // analysis builds: the stamp buffer exists before any graph capture
+        if (e == cudaSuccess && cudaMalloc(&c->timeline, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms) ==
+                                    cudaSuccess) {
+            c->owned.push_back(c->timeline);
+            cudaMemset(c->timeline, 0, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms);
+        }
+#endif
     }
     for (int l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
         GemvParams p = {};

@@ -1122,6 +1122,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (ATTN) {
             const int n_head = a.Q >> a.lg_head_dim;
             if (c < n_head * M) {
+                TL(4 * l + 1, 4);
                 const int hh = c % n_head, mm = c / n_head;
                 switch (a.head_dim) {
                     case 64: attention_phase<2>(a, s, l, ll_qkv, ll_att, qkv_dim, hh, mm, M, epoch, fail); break;
@@ -1133,6 +1134,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                     stopped = true;
                     break;
                 }
+                TL(4 * l + 1, 1);
             }
         }
         // ---- o = W_o * Q(attend); attention over the cache, or over one cached position; o published
