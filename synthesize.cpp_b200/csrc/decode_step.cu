@@ -490,21 +490,40 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
 #ifdef B200Q8_TIMELINE
     const long long tc0 = clock64();
 #endif
-    // lane i probes tile i's barrier, so the op's tiles are checked in one go
-    bool bad = fail || nt > kMaxOpTiles || nt > 32;
-    if (!bad && lane < nt) {
-        if (!mbar_wait_bounded(&s.full[t_sl[lane]], t_ph[lane])) {
-            raise_abort(a, s);
-            bad = true;
-        }
-    }
-    bad  = __any_sync(0xffffffffu, bad);
-    fail = fail || bad;
+    // The op is consumed in rounds of tiles.  A single-segment op, or a pair
+    // op whose tiles all fit the ring, is one round.  A pair op (gate, up)
+    // too large for the ring takes R tile pairs per round, R = S - n_r with
+    // n_r tiles per segment: the last fill round 0 needs reuses the slot of a
+    // fill from an earlier op, and each later round's last fill reuses a slot
+    // an earlier round released, so the producer never waits on a slot the
+    // consumers still hold.
+    const int n_r    = pair_units ? seg_first[1] : nt;  // tiles per segment
+    const int per_rd = pair_units && 2 * n_r > S ? min(n_r, S - n_r) : n_r;
+    bool      bad    = fail || nt > kMaxOpTiles || nt > 32 || per_rd < 1;  // warp-uniform
+    fail             = fail || bad;
 #ifdef B200Q8_TIMELINE
     const long long tc1 = clock64();
     long long       tc_pub = 0;
 #endif
-    if (!bad) {
+    for (int k0 = 0; k0 < n_r && !bad; k0 += per_rd) {
+        const int k1  = min(n_r, k0 + per_rd);
+        const int nin = (pair_units ? 2 : 1) * (k1 - k0);  // tiles of this round
+        auto      tile = [&](int i) { return i < k1 - k0 ? k0 + i : seg_first[1] + k0 + (i - (k1 - k0)); };
+        // lane i probes the round's tile i, so its tiles are checked in one go
+        bool rbad = false;
+        if (lane < nin) {
+            const int ti = tile(lane);
+            if (!mbar_wait_bounded(&s.full[t_sl[ti]], t_ph[ti])) {
+                raise_abort(a, s);
+                rbad = true;
+            }
+        }
+        rbad = __any_sync(0xffffffffu, rbad);
+        if (rbad) {
+            bad  = true;
+            fail = true;
+            break;
+        }
         const int      NSB    = K >> 8;  // superblocks per row
         const int      NB     = K >> 5;
         const int      lgs    = min(5, 32 - __clz(2 * NSB - 1));  // ~1 half-superblock per lane
@@ -515,7 +534,8 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
         const uint32_t xc_s   = smem_addr(xc);
         const uint32_t xd_s   = smem_addr(xd);
         const uint32_t ring_s = smem_addr(s.ring);
-        const int      nunit  = segs[0].n;
+        const int      u_lo   = pair_units ? k0 * segs[0].sr : 0;
+        const int      u_hi   = pair_units ? min(segs[0].n, k1 * segs[0].sr) : segs[0].n;
         auto row_addr = [&](int g, int r) -> uint32_t {
             int ti = 0;
             while (r >= segs[g].sr) {
@@ -524,9 +544,9 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
             }
             return ring_s + (uint32_t) (t_sl[seg_first[g] + ti] * kStepSlotBytes) + (uint32_t) (r * segs[g].rb);
         };
-        for (int ub = warp * gpw; ub < nunit; ub += ngroup) {  // warp-uniform
+        for (int ub = u_lo + warp * gpw; ub < u_hi; ub += ngroup) {  // warp-uniform
             const int  u      = ub + (lane >> lgs);
-            const bool active = u < nunit;
+            const bool active = u < u_hi;
             float      acc0[M_T], acc1[M_T];
 #pragma unroll
             for (int m = 0; m < M_T; ++m) {
@@ -554,6 +574,20 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
             tc_pub += clock64() - tp0;
 #endif
         }
+        if (k1 < n_r) {
+            // a later round follows: this round's slots go back to the producer
+            // once every warp is done with them (their data was seen to land)
+            __syncwarp();
+            if (lane == 0) {
+                for (int i = 0; i < nin; ++i) {
+                    mbar_arrive(&s.empty[t_sl[tile(i)]]);
+                }
+            }
+        }
+        if (k1 >= n_r) {
+            // the last round: its tiles are released below with the op's
+            break;
+        }
     }
     __syncwarp();
 #ifdef B200Q8_TIMELINE
@@ -565,12 +599,17 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
             (unsigned long long) (tc2 - tc1 - tc_pub) | ((unsigned long long) tc_pub << 32);
     }
 #endif
-    // Release the op's slots only after their data was seen to land: a slot
+    // Release the op's last-round slots only after their data was seen to land: a slot
     // whose copy may still be in flight must not be handed back to the
     // producer (it then times out instead, and drains before it exits).
     if (lane == 0 && !bad) {
+        const int k0l = n_r > per_rd ? (n_r - 1) / per_rd * per_rd : 0;  // the last round's first tile pair
         for (int i = 0; i < nt; ++i) {
-            mbar_arrive(&s.empty[t_sl[i]]);
+            const int seg_i = pair_units && i >= seg_first[1] ? 1 : 0;
+            const int k     = i - seg_first[seg_i];
+            if (k >= k0l) {
+                mbar_arrive(&s.empty[t_sl[i]]);
+            }
         }
     }
 }
@@ -1343,10 +1382,12 @@ bool decode_step_supported(const StepArgs & a, int G) {
         const int sr   = std::max(1, (int) (kStepSlotBytes / rb));
         return (rows + sr - 1) / sr;
     };
-    const int worst = std::max(std::max(std::max(tiles(qkv, a.rb_h), tiles(a.H, a.rb_q)),
-                                        std::max(2 * tiles(a.I, a.rb_h), tiles(a.H, a.rb_i))),
-                               a.head != nullptr ? tiles(a.vocab, a.rb_h) : 0);
-    return worst <= std::min(slots, 16);
+    // (the gate/up pair op is consumed in rounds: it needs one slot more than
+    // its tiles per segment, and both segments' tiles within consume_op's table)
+    const int worst = std::max(std::max(tiles(qkv, a.rb_h), tiles(a.H, a.rb_q)),
+                               std::max(tiles(a.H, a.rb_i), a.head != nullptr ? tiles(a.vocab, a.rb_h) : 0));
+    const int gu    = tiles(a.I, a.rb_h);
+    return worst <= std::min(slots, 16) && gu + 1 <= slots && 2 * gu <= 16;
 }
 
 namespace {

@@ -182,3 +182,45 @@ def test_chain_rejects_bad_ids(chain_mod, q8, O, dev, path):
     assert q8.device_status(0) == 1
     assert q8.device_status(0) == 0
     ch.close()
+
+
+@pytest.mark.parametrize("m", [1, 2])
+def test_wide_step_persistent_matches_oracle(chain_mod, O, dev, m):
+    """1.7B talker shapes (hidden 2048, intermediate 6144): the persistent step consumes the gate/up op in rounds
+    of tiles (its tiles exceed the ring); it must match the oracle's chain and the per-op kernels."""
+    H2, I2, L2 = 2048, 6144, 2
+    shapes = [(Q, H2), (KV, H2), (KV, H2), (H2, Q), (I2, H2), (I2, H2), (H2, I2)]
+    mats, norms = [], []
+    for l in range(L2):
+        for j, (n, k) in enumerate(shapes):
+            mats.append(O.quantize_rows(O.normal(900 + 16 * l + j, n * k, 0.02).reshape(n, k)))
+        for j in range(2):
+            norms.append((1.0 + 0.1 * O.normal(900 + 16 * l + 8 + j, H2)).astype(np.float32))
+    norms = np.stack(norms)
+    table = O.quantize_rows(O.normal(899, 64 * H2, 0.02).reshape(64, H2))
+    layers, t_table = upload(mats, norms, table, dev)
+    ids = np.arange(m, dtype=np.int32) * 11 % 64
+    x = np.asarray(np.random.default_rng(m + 40).standard_normal((m, H2)), np.float32)
+    outs = {}
+    for path in ("persistent", "per_op"):
+        import os
+
+        old = os.environ.get("B200Q8_CHAIN_PER_OP")
+        os.environ["B200Q8_CHAIN_PER_OP"] = "1" if path == "per_op" else "0"
+        try:
+            ch = chain_mod.DecodeChain(layers, t_table, hidden=H2, n_head=NH, n_kv=NKV, head_dim=HD, inter=I2, eps=EPS,
+                                       max_m=2)
+        finally:
+            if old is None:
+                del os.environ["B200Q8_CHAIN_PER_OP"]
+            else:
+                os.environ["B200Q8_CHAIN_PER_OP"] = old
+        h = torch.empty((m, H2), device=dev)
+        ch.run(torch.from_numpy(ids).to(dev), torch.from_numpy(x).to(dev), h)
+        torch.cuda.synchronize()
+        outs[path] = h.cpu().numpy()
+        ch.close()
+    ref = O.decoder_chain(mats, norms, table, ids, x, hidden=H2, n_head=NH, n_kv=NKV, head_dim=HD, inter=I2, eps=EPS)
+    for path, got in outs.items():
+        rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+        assert rel < 2e-3, (path, rel)
