@@ -493,10 +493,10 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
     // The op is consumed in rounds of tiles.  A single-segment op, or a pair
     // op whose tiles all fit the ring, is one round.  A pair op (gate, up)
     // too large for the ring takes R tile pairs per round, R = S - n_r with
-    // n_r tiles per segment: the last fill round 0 needs reuses the slot of a
-    // fill from an earlier op, and each later round's last fill reuses a slot
-    // an earlier round released, so the producer never waits on a slot the
-    // consumers still hold.
+    // n_r tiles per segment: the last fill the first tile round needs reuses
+    // the slot of a fill from an earlier op, and each later round's last fill
+    // reuses a slot an earlier round released, so the producer never waits on
+    // a slot the consumers still hold.
     const int n_r    = pair_units ? seg_first[1] : nt;  // tiles per segment
     const int per_rd = pair_units && 2 * n_r > S ? min(n_r, S - n_r) : n_r;
     bool      bad    = fail || nt > kMaxOpTiles || nt > 32 || per_rd < 1;  // warp-uniform
