@@ -336,12 +336,19 @@ b200q8_status_t b200q8_chain_step(b200q8_chain * chain, const b200q8_step_args *
 typedef struct b200q8_frame_desc {
     b200q8_chain *       talker;     /* attention + output desc with >= 1 head; its table = ttable  */
     b200q8_chain *       predictor;  /* attention + output desc with >= G-1 heads, n_ctx >= G,
-                                        max_m >= 2 * the frame's M, same device and hidden width   */
+                                        max_m >= 2 * the frame's M, same device; same hidden width
+                                        unless an input projection is given                        */
     int32_t              groups;     /* code_group_count (16)                                       */
     const void * const * tables;     /* G-1 device pointers: predictor codec_embedding.{g}, Q8_0
                                         [talker hidden, table_rows]                                 */
     int64_t              table_rows;
     float                repetition_penalty;  /* the talker's; values <= 1 apply none             */
+    /* A predictor narrower than the talker (the 1.7B packages): every
+     * predictor input row (talker width) is first projected,
+     * x = W * Q(x) + b (small_to_mtp_projection, code-predictor.cpp:49-58).
+     * NULL / NULL when the widths agree. */
+    const void *         input_projection;       /* Q8_0 with ne = [talker hidden, predictor hidden] */
+    const float *        input_projection_bias;  /* F32 [predictor hidden]                          */
 } b200q8_frame_desc;
 
 typedef struct b200q8_frame b200q8_frame;

@@ -67,8 +67,9 @@ b200q8_status_t b200q8_gguf_talker_chain(const b200q8_gguf * g, int32_t device, 
  *               with sampling.repetition_penalty (1 when the key is absent).
  * Hyperparameters follow weights.cpp:128-212 (the predictor's
  * intermediate_size falls back to the talker's; eps and rope_theta are the
- * talker's, model.cpp:315-322).  A predictor wider or narrower than the talker
- * (small_to_mtp_projection) or a tensor not in Q8_0 / F32 as the step needs is
+ * talker's, model.cpp:315-322).  A predictor of another width than the
+ * talker gets its small_to_mtp_projection (Q8_0 weight, F32 bias) uploaded
+ * and handed to the frame.  A tensor not in Q8_0 / F32 as the step needs is
  * B200Q8_ERR_UNSUPPORTED.  Each chain owns its weights; destroy the frame
  * before the chains. */
 b200q8_status_t b200q8_gguf_decoder(const b200q8_gguf * g, int32_t device, int64_t max_m, int32_t mode,

@@ -302,7 +302,7 @@ def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.nd
     replay codes): talker step on sum(code embeddings) + text, greedy/replayed code 0, predictor prefill over
     [hidden, ttable[code 0]] at positions 0, 1 and G-2 single-position predictor steps.  talker / predictor: dicts
     with mats, norms, qkn, table (talker only), out_norm, heads (list of Q8_0 arrays), hidden, n_head, n_kv,
-    head_dim, inter, eps, theta, vocab.  state: {"tk", "tv", "pk", "pv" caches, "history": {slot: set}} updated in
+    head_dim, inter, eps, theta, vocab; the predictor's may hold proj_w / proj_b (its input projection).  state: {"tk", "tv", "pk", "pv" caches, "history": {slot: set}} updated in
     place.  hidden_in / logits_in: the talker's outputs when its step already ran (the prompt pass).
     Returns (codes [M, G] int32, talker hidden [M, H], talker logits [M, V], predictor logits: a list of G-1
     arrays [M, V_p], the one each acoustic code was chosen from)."""
@@ -333,23 +333,30 @@ def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.nd
             hist = state["history"].setdefault(int(slots[m]), set())
             codes[m, 0] = select_code(logits[m], hist, penalty)
             hist.add(int(codes[m, 0]))
+    def project(x):  # a predictor narrower than the talker: x = W * Q(x) + b (code-predictor.cpp:49-58)
+        if "proj_w" not in P:
+            return x
+        return (mul_mat(P["proj_w"], H, x, mode, threads, want_bound=False)[0] + P["proj_b"]).astype(np.float32)
+
     # predictor prefill: two positions per stream
     xp = np.empty((2 * M, H), np.float32)
     xp[0::2] = hid
     xp[1::2] = get_rows(T["table"], H, codes[:, 0])[0]
+    xp = project(xp)
     pp = np.tile(np.array([0, 1], np.int32), M)
     ps = np.repeat(np.asarray(slots, np.int32), 2)
     h = decoder_chain_attn(P["mats"], P["norms"], P["qkn"], None, None, xp, pp, state["pk"], state["pv"], slots=ps,
                            **dims(P))
-    lg = mul_mat(P["heads"][0], H, rms_norm_rows(h[1::2], P["out_norm"], P["eps"]), mode, threads, want_bound=False)[0]
+    Hp = P["hidden"]
+    lg = mul_mat(P["heads"][0], Hp, rms_norm_rows(h[1::2], P["out_norm"], P["eps"]), mode, threads, want_bound=False)[0]
     plogits = [lg]
     for m in range(M):
         codes[m, 1] = replay[m, 1] if replay is not None else select_code(lg[m])
     for g in range(1, groups - 1):
-        x = get_rows(ptables[g - 1], H, codes[:, g])[0]
+        x = project(get_rows(ptables[g - 1], H, codes[:, g])[0])
         h = decoder_chain_attn(P["mats"], P["norms"], P["qkn"], None, None, x, np.full(M, g + 1, np.int32),
                                state["pk"], state["pv"], slots=slots, **dims(P))
-        lg = mul_mat(P["heads"][g], H, rms_norm_rows(h, P["out_norm"], P["eps"]), mode, threads, want_bound=False)[0]
+        lg = mul_mat(P["heads"][g], Hp, rms_norm_rows(h, P["out_norm"], P["eps"]), mode, threads, want_bound=False)[0]
         plogits.append(lg)
         for m in range(M):
             codes[m, g + 1] = replay[m, g + 1] if replay is not None else select_code(lg[m])

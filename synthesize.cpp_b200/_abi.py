@@ -70,7 +70,8 @@ class StepArgs(ctypes.Structure):
 class FrameDesc(ctypes.Structure):
     _fields_ = [("talker", ctypes.c_void_p), ("predictor", ctypes.c_void_p), ("groups", ctypes.c_int32),
                 ("tables", ctypes.POINTER(ctypes.c_void_p)), ("table_rows", ctypes.c_int64),
-                ("repetition_penalty", ctypes.c_float)]
+                ("repetition_penalty", ctypes.c_float), ("input_projection", ctypes.c_void_p),
+                ("input_projection_bias", ctypes.c_void_p)]
 
 
 class FrameArgs(ctypes.Structure):

@@ -838,6 +838,10 @@ ChainInfo chain_info(const b200q8_chain * c) {
     return i;
 }
 
+int chain_mode(const b200q8_chain * c) {
+    return c->d.mode;
+}
+
 b200q8_status_t chain_resolve(b200q8_chain * c, const b200q8_step_args & a, StepIO & io) {
     if (a.M < 1 || a.M > c->d.max_m) {
         return set_error(B200Q8_ERR_INVALID_ARG, "chain_step: M (%lld) must be in [1, max_m]", (long long) a.M);

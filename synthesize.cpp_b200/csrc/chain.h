@@ -47,6 +47,9 @@ struct ChainInfo {
 
 ChainInfo chain_info(const b200q8_chain * c);
 
+// The chain's activation quantizer (B200Q8_QUANT_*).
+int chain_mode(const b200q8_chain * c);
+
 // Checks a against the chain and fills io (sets the error message on failure).
 b200q8_status_t chain_resolve(b200q8_chain * c, const b200q8_step_args & a, StepIO & io);
 

@@ -191,6 +191,14 @@ __global__ void fill_positions_kernel(int32_t * __restrict__ ppos, int32_t * __r
     }
 }
 
+// y[m][n] += b[n] (the projection's bias: ggml_add(mul_mat(W, x), b)).
+__global__ void add_bias_kernel(float * __restrict__ y, const float * __restrict__ b, int64_t M, int64_t N) {
+    const int64_t total = M * N;
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t) gridDim.x * blockDim.x) {
+        y[i] = __fadd_rn(y[i], b[i % N]);
+    }
+}
+
 int frame_grid(int64_t total, int sms) {
     return (int) std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t) sms * 4));
 }
@@ -206,6 +214,7 @@ struct b200q8_frame {
     ChainInfo            ti = {}, pi = {};
     int                  G         = 0;
     float                penalty   = 1.0f;
+    int                  mode      = 0;  // the predictor chain's quantizer
     int64_t              prows     = 0;
     int64_t              max_m     = 0;
     size_t               rb        = 0;  // Q8_0 row bytes at the hidden width
@@ -226,6 +235,12 @@ struct b200q8_frame {
     int32_t *            ppos      = nullptr;  // [2 max_m]: 0, 1, 0, 1, ...
     int32_t *            spos      = nullptr;  // [G-2][max_m]: g + 1 for group g
     uint8_t *            history   = nullptr;  // [talker n_slots][talker vocab]
+    // input projection (predictor narrower than the talker)
+    const uint8_t *      proj_w    = nullptr;  // Q8_0 [predictor hidden rows] of K = talker hidden
+    const float *        proj_b    = nullptr;
+    float *              xe        = nullptr;  // [max_m][talker hidden] embedded codes
+    float *              xq        = nullptr;  // [2 max_m][predictor hidden] projected input rows
+    void *               proj_ws   = nullptr;  // MUL_MAT workspace
     cudaStream_t         cap       = nullptr;
 
     struct Graph {
@@ -294,9 +309,23 @@ cudaError_t enqueue_frame(b200q8_frame * f, cudaStream_t st, const b200q8_frame_
                                                                    f->xp, M, H);
         e = cudaGetLastError();
     }
+    // x = W * Q(x) + b for n rows of talker width (the predictor's input projection)
+    auto project = [&](const float * x, int64_t n) -> cudaError_t {
+        const int64_t Ht = f->ti.hidden, Hp = f->pi.hidden;
+        cudaError_t   e2 = launch_gemm(f->proj_w, (size_t) (Ht / kQK) * kBlockBytes, Ht, Hp, x, (size_t) Ht, n, f->xq,
+                                       (size_t) Hp, f->mode, f->proj_ws, st, sms);
+        if (e2 == cudaSuccess) {
+            add_bias_kernel<<<frame_grid(n * Hp, sms), 256, 0, st>>>(f->xq, f->proj_b, n, Hp);
+            e2 = cudaGetLastError();
+        }
+        return e2;
+    };
+    if (e == cudaSuccess && f->proj_w != nullptr) {
+        e = project(f->xp, 2 * M);
+    }
     if (e == cudaSuccess) {
         StepIO io;
-        io.M = 2 * M; io.x_in = f->xp; io.pos = f->ppos; io.slots = f->pslots;
+        io.M = 2 * M; io.x_in = f->proj_w ? f->xq : f->xp; io.pos = f->ppos; io.slots = f->pslots;
         io.h_out = f->ph; io.hidden_out = f->phid; io.logits = f->plog; io.head = 0;
         e = chain_enqueue(f->predictor, st, io);
     }
@@ -308,7 +337,16 @@ cudaError_t enqueue_frame(b200q8_frame * f, cudaStream_t st, const b200q8_frame_
     // groups 1..G-2: embed the last code through its group's table, predict the next
     for (int g = 1; g + 1 < f->G && e == cudaSuccess; ++g) {
         StepIO io;
-        io.M = M; io.ids = f->cur; io.table = f->ptabs_host[g - 1]; io.table_rows = f->prows;
+        io.M = M;
+        if (f->proj_w != nullptr) {  // embed at talker width, then project
+            e = launch_dequant_rows(f->ptabs_host[g - 1], f->rb, f->prows, f->cur, M, H, f->xe,
+                                    (size_t) H * sizeof(float), st, sms);  // row strides in bytes
+            if (e == cudaSuccess) e = project(f->xe, M);
+            if (e != cudaSuccess) break;
+            io.x_in = f->xq;
+        } else {
+            io.ids = f->cur; io.table = f->ptabs_host[g - 1]; io.table_rows = f->prows;
+        }
         io.pos = f->spos + (int64_t) (g - 1) * f->max_m; io.slots = f->slots1;
         io.h_out = f->ph; io.hidden_out = f->phid; io.logits = f->plog; io.head = g;
         e = chain_enqueue(f->predictor, st, io);
@@ -345,9 +383,17 @@ b200q8_status_t b200q8_frame_create(const b200q8_frame_desc * desc, b200q8_frame
         return set_error(B200Q8_ERR_INVALID_ARG, "frame_create: both chains need attention and an output desc "
                                                  "(talker >= 1 head, predictor >= groups - 1 heads)");
     }
-    if (ti.device != pi.device || ti.hidden != pi.hidden) {
-        return set_error(B200Q8_ERR_UNSUPPORTED, "frame_create: the chains must share a device and a hidden width "
-                                                 "(a predictor input projection is not supported)");
+    if (ti.device != pi.device) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "frame_create: the chains must share a device");
+    }
+    const bool proj = desc->input_projection != nullptr || desc->input_projection_bias != nullptr;
+    if (proj ? (desc->input_projection == nullptr || desc->input_projection_bias == nullptr ||
+                reinterpret_cast<uintptr_t>(desc->input_projection) % 16 != 0 || ti.hidden % 256 != 0 ||
+                !gemm_supported(static_cast<const uint8_t *>(desc->input_projection),
+                                (size_t) (ti.hidden / kQK) * kBlockBytes, ti.hidden, pi.hidden, 2 * pi.max_m))
+             : ti.hidden != pi.hidden) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "frame_create: a predictor of another width than the talker needs "
+                                                 "both the input projection (16-byte aligned Q8_0) and its bias");
     }
     if (pi.n_ctx < G || pi.n_slots < ti.n_slots) {
         return set_error(B200Q8_ERR_INVALID_ARG, "frame_create: the predictor needs n_ctx >= groups and n_slots >= "
@@ -370,6 +416,9 @@ b200q8_status_t b200q8_frame_create(const b200q8_frame_desc * desc, b200q8_frame
     f->prows     = desc->table_rows;
     f->max_m     = max_m;
     f->rb        = (size_t) (ti.hidden / kQK) * kBlockBytes;
+    f->mode      = chain_mode(desc->predictor);
+    f->proj_w    = static_cast<const uint8_t *>(desc->input_projection);
+    f->proj_b    = desc->input_projection_bias;
     for (int g = 0; g + 1 < G; ++g) {
         f->ptabs_host.push_back(static_cast<const uint8_t *>(desc->tables[g]));
     }
@@ -389,8 +438,14 @@ b200q8_status_t b200q8_frame_create(const b200q8_frame_desc * desc, b200q8_frame
     f->thid    = static_cast<float *>(alloc(sizeof(float) * (size_t) (max_m * H)));
     f->tlog    = static_cast<float *>(alloc(sizeof(float) * (size_t) (max_m * ti.vocab)));
     f->xp      = static_cast<float *>(alloc(sizeof(float) * (size_t) (2 * max_m * H)));
-    f->ph      = static_cast<float *>(alloc(sizeof(float) * (size_t) (2 * max_m * H)));
-    f->phid    = static_cast<float *>(alloc(sizeof(float) * (size_t) (2 * max_m * H)));
+    const int64_t Hp = pi.hidden;
+    f->ph      = static_cast<float *>(alloc(sizeof(float) * (size_t) (2 * max_m * Hp)));
+    f->phid    = static_cast<float *>(alloc(sizeof(float) * (size_t) (2 * max_m * Hp)));
+    if (f->proj_w != nullptr) {
+        f->xe      = static_cast<float *>(alloc(sizeof(float) * (size_t) (max_m * H)));
+        f->xq      = static_cast<float *>(alloc(sizeof(float) * (size_t) (2 * max_m * Hp)));
+        f->proj_ws = alloc(gemm_workspace_bytes(H, 2 * max_m));
+    }
     f->plog    = static_cast<float *>(alloc(sizeof(float) * (size_t) (2 * max_m * pi.vocab)));
     f->cur     = static_cast<int32_t *>(alloc(sizeof(int32_t) * (size_t) max_m));
     f->slots1  = static_cast<int32_t *>(alloc(sizeof(int32_t) * (size_t) max_m));

@@ -599,9 +599,19 @@ b200q8_status_t b200q8_gguf_decoder(const b200q8_gguf * g, int32_t device, int64
         return set_error(B200Q8_ERR_INVALID_ARG, "%s: bad hyperparameters (intermediate sizes, eps, rope_theta, "
                                                  "code groups >= 2 and equal for both heads)", who);
     }
-    if (ps.hidden != ts.hidden) {
-        return set_error(B200Q8_ERR_UNSUPPORTED, "%s: the predictor's width differs from the talker's "
-                                                 "(small_to_mtp_projection is not supported)", who);
+    // a predictor of another width than the talker reads its input through
+    // small_to_mtp_projection (catalog.cpp:322-340): weight and bias
+    const bool              proj = ps.hidden != ts.hidden;
+    std::vector<const Tensor *> proj_found;
+    if (proj) {
+        const std::vector<Need> pn = {
+            { "talker.code_predictor.small_to_mtp_projection.weight", 8, ts.hidden, ps.hidden },
+            { "talker.code_predictor.small_to_mtp_projection.bias", 0, ps.hidden, 1 },
+        };
+        st = find_tensors(g, pn, who, proj_found);
+        if (st != B200Q8_OK) {
+            return st;
+        }
     }
     ts.prefix       = "talker.model.layers.";
     ts.attention    = true;
@@ -623,7 +633,7 @@ b200q8_status_t b200q8_gguf_decoder(const b200q8_gguf * g, int32_t device, int64
         ps.tables.push_back("talker.code_predictor.model.codec_embedding." + std::to_string(k) + ".weight");
         ps.head_names.push_back("talker.code_predictor.lm_head." + std::to_string(k) + ".weight");
     }
-    ps.table_hidden = ts.hidden;
+    ps.table_hidden = ts.hidden;  // the predictor's tables are at the talker's width (catalog.cpp:297-321)
     ps.table_rows   = p_vocab;
     ps.norm         = "talker.code_predictor.model.norm.weight";
     ps.vocab        = p_vocab;
@@ -631,8 +641,21 @@ b200q8_status_t b200q8_gguf_decoder(const b200q8_gguf * g, int32_t device, int64
     std::vector<const void *> ptables;
     st = build_stack(g, ts, device, max_m, mode, who, &tc, nullptr);
     if (st == B200Q8_OK) st = build_stack(g, ps, device, std::max<int64_t>(8, 2 * max_m), mode, who, &pc, &ptables);
+    std::vector<const void *> proj_ptr(2, nullptr);
+    if (st == B200Q8_OK && proj) {  // uploaded into a buffer the predictor chain owns
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaError_t e = cudaSetDevice(device);
+        uint8_t *   buf = nullptr;
+        st = e == cudaSuccess ? upload_tensors(g, proj_found, &buf, proj_ptr) : cuda_error(e, "gguf: cudaSetDevice");
+        if (st == B200Q8_OK) {
+            pc->owned.push_back(buf);
+        }
+        cudaSetDevice(prev);
+    }
     if (st == B200Q8_OK && frame != nullptr) {
-        const b200q8_frame_desc fd = { tc, pc, (int32_t) t_groups, ptables.data(), p_vocab, penalty };
+        const b200q8_frame_desc fd = { tc, pc, (int32_t) t_groups, ptables.data(), p_vocab, penalty, proj_ptr[0],
+                                       static_cast<const float *>(proj_ptr[1]) };
         st                         = b200q8_frame_create(&fd, frame);
     }
     if (st != B200Q8_OK) {

@@ -20,12 +20,15 @@ class Frame:
     G-1 codec tables (uint8 Q8_0 [rows, hidden/32*34] CUDA tensors)."""
 
     def __init__(self, talker: DecodeChain, predictor: DecodeChain, tables: list[torch.Tensor], *,
-                 repetition_penalty: float = 1.0):
-        self._keep = (talker, predictor, tables)
+                 repetition_penalty: float = 1.0, projection: tuple[torch.Tensor, torch.Tensor] | None = None):
+        """projection: (W uint8 Q8_0 [predictor hidden, talker hidden/32*34], bias float32 [predictor hidden]) for a
+        predictor narrower than the talker."""
+        self._keep = (talker, predictor, tables, projection)
         self.groups = len(tables) + 1
         arr = (ctypes.c_void_p * len(tables))(*[t.data_ptr() for t in tables])
+        pw, pb = (projection[0].data_ptr(), projection[1].data_ptr()) if projection is not None else (None, None)
         desc = FrameDesc(talker._h, predictor._h, self.groups, ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)),
-                         tables[0].shape[0], repetition_penalty)
+                         tables[0].shape[0], repetition_penalty, pw, pb)
         handle = ctypes.c_void_p()
         check(lib().b200q8_frame_create(ctypes.byref(desc), ctypes.byref(handle)))
         self._h = handle

@@ -223,3 +223,53 @@ def test_frame_selection_rule(chain_mod, frame_mod, O, dev):
     fr.run(codes, hidden=hid, talker_logits=t(lg, dev), skip_talker=True)
     torch.cuda.synchronize(dev)
     assert [int(c) for c in codes.cpu().numpy()[:, 0]] == [O.select_code(lg[i]) for i in range(m)]
+
+
+def test_frame_with_input_projection(chain_mod, frame_mod, O, dev):
+    """A predictor narrower than the talker (the 1.7B packages' small_to_mtp_projection): every predictor input row
+    is projected, x = W * Q(x) + b, before its layers; greedy frames against the oracle replaying the GPU's codes."""
+    m = 2
+    HP = 512
+    talker, tref = stack(O, dev, 2, 4000, TV, 1, TV, chain_mod, n_ctx=16, n_slots=m, max_m=8)
+    # a narrower predictor: hidden 512, 4 query heads, 2 kv heads of 128, intermediate 1024
+    shapes = [(4 * HD, HP), (2 * HD, HP), (2 * HD, HP), (HP, 4 * HD), (1024, HP), (1024, HP), (HP, 1024)]
+    mats, norms = [], []
+    for l in range(2):
+        for j, (n, k) in enumerate(shapes):
+            mats.append(O.quantize_rows(O.normal(7000 + 16 * l + j, n * k, 0.03).reshape(n, k)))
+        for j in range(2):
+            norms.append((1.0 + 0.1 * O.normal(7000 + 16 * l + 8 + j, HP)).astype(np.float32))
+    norms = np.stack(norms)
+    qkn = np.stack([(1.0 + 0.2 * O.normal(7100 + i, HD)).astype(np.float32) for i in range(4)])
+    out_norm = (1.0 + 0.1 * O.normal(7200, HP)).astype(np.float32)
+    heads = [O.quantize_rows(O.normal(7300 + g, PV * HP, 0.03).reshape(PV, HP)) for g in range(G - 1)]
+    ptables = [O.quantize_rows(O.normal(7400 + g, PV * H, 0.5).reshape(PV, H)) for g in range(G - 1)]  # talker width
+    proj_w = O.quantize_rows(O.normal(7500, HP * H, 0.03).reshape(HP, H))
+    proj_b = (0.1 * O.normal(7501, HP)).astype(np.float32)
+    keys = ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown")
+    layers = [dict({k: t(mats[7 * l + j], dev) for j, k in enumerate(keys)}, norm_in=t(norms[2 * l], dev),
+                   norm_post=t(norms[2 * l + 1], dev), q_norm=t(qkn[2 * l], dev), k_norm=t(qkn[2 * l + 1], dev))
+              for l in range(2)]
+    pred = chain_mod.DecodeChain(layers, t(heads[0], dev), hidden=HP, n_head=4, n_kv=2, head_dim=HD, inter=1024,
+                                 eps=EPS, max_m=8, attention=dict(rope_theta=THETA, n_ctx=G, n_slots=m),
+                                 output=dict(norm=t(out_norm, dev), heads=[t(h, dev) for h in heads]))
+    fr = frame_mod.Frame(talker, pred, [t(p, dev) for p in ptables], projection=(t(proj_w, dev), t(proj_b, dev)))
+    pref = dict(mats=mats, norms=norms, qkn=qkn, out_norm=out_norm, heads=heads, hidden=HP, n_head=4, n_kv=2,
+                head_dim=HD, inter=1024, eps=EPS, theta=THETA, vocab=PV, proj_w=proj_w, proj_b=proj_b)
+    state = dict(tk=np.zeros((2, m, 16, KV), np.float32), tv=np.zeros((2, m, 16, KV), np.float32),
+                 pk=np.zeros((2, m, G, 2 * HD), np.float32), pv=np.zeros((2, m, G, 2 * HD), np.float32), history={})
+    rng = np.random.default_rng(21)
+    prev = np.stack([rng.integers(0, TV, m)] + [rng.integers(0, PV, m) for _ in range(G - 1)], 1).astype(np.int32)
+    codes = torch.empty((m, G), dtype=torch.int32, device=dev)
+    slots = np.arange(m, dtype=np.int32)
+    for f in range(3):
+        text = rng.standard_normal((m, H)).astype(np.float32)
+        pos = np.full(m, f, np.int32)
+        fr.run(codes, text=t(text, dev), prev=t(prev, dev), pos=t(pos, dev))
+        torch.cuda.synchronize(dev)
+        got = codes.cpu().numpy()
+        _, _, _, wplog = O.frame(tref, pref, ptables, G, text, prev, pos, slots, state, replay=got)
+        for i in range(m):
+            for g in range(1, G):
+                assert_choice(int(got[i, g]), wplog[g - 1][i], 2e-2 * np.abs(wplog[g - 1][i]).max())
+        prev = got

@@ -89,16 +89,18 @@ DP = dict(hidden=256, heads=4, kv=2, head_dim=64, inter=512, t_layers=2, p_layer
           groups=4, eps=1e-6, theta=1.0e4, penalty=1.2)
 
 
-def tiny_decoder_package(O, tmp_path):
+def tiny_decoder_package(O, tmp_path, t_hidden=None):
     """A package with the talker (attention norms, final norm, codec head) and the code predictor (layers, norm,
-    per-group tables and heads), named and keyed as the reference's catalog and loader expect."""
+    per-group tables and heads), named and keyed as the reference's catalog and loader expect.  t_hidden: a talker
+    wider than the predictor, which then reads its input through small_to_mtp_projection."""
     H, Q, KV, I = DP["hidden"], DP["heads"] * DP["head_dim"], DP["kv"] * DP["head_dim"], DP["inter"]
+    HT = t_hidden or H
     kv = {}
-    for p, layers, vocab_key, vocab in (("synthesize.qwen3-tts.talker.", DP["t_layers"], "codec_vocab_size",
-                                         DP["t_vocab"]),
-                                        ("synthesize.qwen3-tts.code_predictor.", DP["p_layers"], "vocab_size",
-                                         DP["p_vocab"])):
-        kv.update({p + "layer_count": ("uint32", layers), p + "hidden_size": ("uint32", H),
+    for p, layers, vocab_key, vocab, hid in (("synthesize.qwen3-tts.talker.", DP["t_layers"], "codec_vocab_size",
+                                              DP["t_vocab"], HT),
+                                             ("synthesize.qwen3-tts.code_predictor.", DP["p_layers"], "vocab_size",
+                                              DP["p_vocab"], H)):
+        kv.update({p + "layer_count": ("uint32", layers), p + "hidden_size": ("uint32", hid),
                    p + "attention_head_count": ("uint32", DP["heads"]), p + "key_value_head_count": ("uint32", DP["kv"]),
                    p + "head_dim": ("uint32", DP["head_dim"]), p + vocab_key: ("uint32", vocab),
                    p + "code_group_count": ("uint32", DP["groups"])})
@@ -106,8 +108,9 @@ def tiny_decoder_package(O, tmp_path):
     kv.update({t + "intermediate_size": ("uint32", I), t + "rms_norm_eps": ("float32", DP["eps"]),
                t + "rope_theta": ("float32", DP["theta"]), t + "rope_type": ("string", "1d"),
                "synthesize.qwen3-tts.sampling.repetition_penalty": ("float32", DP["penalty"])})
-    shapes = {"self_attn.q_proj": (Q, H), "self_attn.k_proj": (KV, H), "self_attn.v_proj": (KV, H),
-              "self_attn.o_proj": (H, Q), "mlp.gate_proj": (I, H), "mlp.up_proj": (I, H), "mlp.down_proj": (H, I)}
+    shapes_of = lambda h: {"self_attn.q_proj": (Q, h), "self_attn.k_proj": (KV, h), "self_attn.v_proj": (KV, h),
+                           "self_attn.o_proj": (h, Q), "mlp.gate_proj": (I, h), "mlp.up_proj": (I, h),
+                           "mlp.down_proj": (h, I)}
     Q8 = gguf.GGMLQuantizationType.Q8_0
     tensors = []
     stacks = {}
@@ -121,58 +124,65 @@ def tiny_decoder_package(O, tmp_path):
         seed[0] += 1
         return (1.0 + O.normal(seed[0], n, scale)).astype(np.float32)
 
-    for name, prefix, n_layers in (("talker", "talker.model.layers.", DP["t_layers"]),
-                                   ("predictor", "talker.code_predictor.model.layers.", DP["p_layers"])):
+    for name, prefix, n_layers, hid in (("talker", "talker.model.layers.", DP["t_layers"], HT),
+                                        ("predictor", "talker.code_predictor.model.layers.", DP["p_layers"], H)):
         layers = []
         for l in range(n_layers):
             b = f"{prefix}{l}."
             L = {}
-            for key, (n, k) in shapes.items():
+            for key, (n, k) in shapes_of(hid).items():
                 L[key] = q8(n, k)
                 tensors.append((b + key + ".weight", L[key], None, Q8))
-            for key, n, sc in (("input_layernorm", H, 0.1), ("post_attn_norm", H, 0.1),
+            for key, n, sc in (("input_layernorm", hid, 0.1), ("post_attn_norm", hid, 0.1),
                                ("self_attn.q_norm", DP["head_dim"], 0.2), ("self_attn.k_norm", DP["head_dim"], 0.2)):
                 L[key] = vec(n, sc)
                 tensors.append((b + key + ".weight", L[key], None, None))
             layers.append(L)
         stacks[name] = layers
-    ttable = q8(DP["t_vocab"], H, 0.5)
-    thead = q8(DP["t_vocab"], H)
-    tnorm = vec(H, 0.1)
+    ttable = q8(DP["t_vocab"], HT, 0.5)
+    thead = q8(DP["t_vocab"], HT)
+    tnorm = vec(HT, 0.1)
     tensors += [("talker.model.codec_embedding.weight", ttable, None, Q8), ("talker.codec_head.weight", thead, None, Q8),
                 ("talker.model.norm.weight", tnorm, None, None)]
     ptables, pheads = [], []
     for g in range(DP["groups"] - 1):
-        ptables.append(q8(DP["p_vocab"], H, 0.5))
+        ptables.append(q8(DP["p_vocab"], HT, 0.5))  # the predictor's tables are at the talker's width
         pheads.append(q8(DP["p_vocab"], H))
         tensors += [(f"talker.code_predictor.model.codec_embedding.{g}.weight", ptables[-1], None, Q8),
                     (f"talker.code_predictor.lm_head.{g}.weight", pheads[-1], None, Q8)]
     pnorm = vec(H, 0.1)
     tensors.append(("talker.code_predictor.model.norm.weight", pnorm, None, None))
+    proj = None
+    if HT != H:
+        proj = (q8(H, HT), (0.1 * O.normal(seed[0] + 1, H)).astype(np.float32))
+        tensors += [("talker.code_predictor.small_to_mtp_projection.weight", proj[0], None, Q8),
+                    ("talker.code_predictor.small_to_mtp_projection.bias", proj[1], None, None)]
     path = tmp_path / "tiny_decoder.gguf"
     write_package(path, kv, tensors)
-    return path, stacks, (ttable, thead, tnorm), (ptables, pheads, pnorm)
+    return path, stacks, (ttable, thead, tnorm), (ptables, pheads, pnorm), proj
 
 
-def test_package_decoder_matches_direct_frame(pkg, O, chain_mod, frame_mod, dev, tmp_path):
+@pytest.mark.parametrize("t_hidden", [None, 512])
+def test_package_decoder_matches_direct_frame(pkg, O, chain_mod, frame_mod, dev, tmp_path, t_hidden):
     from synthesize_cpp_b200 import gguf as G
 
-    path, stacks, (ttable, thead, tnorm), (ptables, pheads, pnorm) = tiny_decoder_package(O, tmp_path)
+    path, stacks, (ttable, thead, tnorm), (ptables, pheads, pnorm), proj = tiny_decoder_package(O, tmp_path, t_hidden)
+    HT = t_hidden or DP["hidden"]
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
     keys = {"wq": "self_attn.q_proj", "wk": "self_attn.k_proj", "wv": "self_attn.v_proj", "wo": "self_attn.o_proj",
             "wgate": "mlp.gate_proj", "wup": "mlp.up_proj", "wdown": "mlp.down_proj", "norm_in": "input_layernorm",
             "norm_post": "post_attn_norm", "q_norm": "self_attn.q_norm", "k_norm": "self_attn.k_norm"}
     m, n_ctx = 2, 8
     mk = lambda layers: [{k: t(L[v]) for k, v in keys.items()} for L in layers]
-    common = dict(hidden=DP["hidden"], n_head=DP["heads"], n_kv=DP["kv"], head_dim=DP["head_dim"], inter=DP["inter"],
-                  eps=DP["eps"])
-    talker = chain_mod.DecodeChain(mk(stacks["talker"]), t(ttable), max_m=8, **common,
+    common = dict(n_head=DP["heads"], n_kv=DP["kv"], head_dim=DP["head_dim"], inter=DP["inter"], eps=DP["eps"])
+    talker = chain_mod.DecodeChain(mk(stacks["talker"]), t(ttable), max_m=8, hidden=HT, **common,
                                    attention=dict(rope_theta=DP["theta"], n_ctx=n_ctx, n_slots=m),
                                    output=dict(norm=t(tnorm), heads=[t(thead)]))
-    pred = chain_mod.DecodeChain(mk(stacks["predictor"]), t(ptables[0]), max_m=8, **common,
+    pred = chain_mod.DecodeChain(mk(stacks["predictor"]), t(pheads[0]), max_m=8, hidden=DP["hidden"], **common,
                                  attention=dict(rope_theta=DP["theta"], n_ctx=DP["groups"], n_slots=m),
                                  output=dict(norm=t(pnorm), heads=[t(h) for h in pheads]))
-    direct = frame_mod.Frame(talker, pred, [t(p) for p in ptables], repetition_penalty=DP["penalty"])
+    direct = frame_mod.Frame(talker, pred, [t(p) for p in ptables], repetition_penalty=DP["penalty"],
+                             projection=(t(proj[0]), t(proj[1])) if proj else None)
     with G.Package(path) as p:
         _, _, from_pkg = p.decoder(device=dev.index or 0, max_m=m, n_ctx=n_ctx, n_slots=m)
     rng = np.random.default_rng(9)
@@ -181,12 +191,12 @@ def test_package_decoder_matches_direct_frame(pkg, O, chain_mod, frame_mod, dev,
     outs = []
     for fr in (direct, from_pkg):
         codes = torch.empty((m, DP["groups"]), dtype=torch.int32, device=dev)
-        hid = torch.empty((m, DP["hidden"]), device=dev)
+        hid = torch.empty((m, HT), device=dev)
         lg = torch.empty((m, DP["t_vocab"]), device=dev)
         pv = t(prev)
         seq = []
         for f in range(5):
-            text = t(np.random.default_rng(100 + f).standard_normal((m, DP["hidden"])).astype(np.float32))
+            text = t(np.random.default_rng(100 + f).standard_normal((m, HT)).astype(np.float32))
             fr.run(codes, text=text, prev=pv, pos=t(np.full(m, f, np.int32)), hidden=hid, talker_logits=lg)
             seq.append((codes.clone(), hid.clone(), lg.clone()))
             pv = codes.clone()
