@@ -169,8 +169,7 @@ b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_ro
 /* The same MUL_MAT for callers that cannot allocate device memory at the
  * point of the call -- a ggml backend computing a graph whose buffers were all
  * placed before the graph ran, a real-time streaming callback that must not
- * block on cudaMalloc's device-wide synchronisation, code inside a CUDA stream
- * capture.  No counterpart in the reference (its CPU path allocates nothing
+ * block on cudaMalloc's device-wide synchronisation.  No counterpart in the reference (its CPU path allocates nothing
  * on the device).  It allocates nothing: the quantized activations go to a
  * fixed 1 MiB array in the library's own device memory, held by every GPU
  * that loads the library until the process exits.  Requires

@@ -7,9 +7,8 @@
 // allocator to turn to at the point of the call: a ggml backend computes a
 // graph whose buffers were all placed by ggml-alloc beforehand and cannot
 // grow them mid-graph; a real-time audio/streaming callback must not block on
-// cudaMalloc's device-wide synchronisation; code inside a CUDA stream capture
-// may not allocate.  This entry point takes the scratch from a fixed array in
-// the library's own device memory instead.
+// cudaMalloc's device-wide synchronisation.  This entry point takes the
+// scratch from a fixed array in the library's own device memory instead.
 //
 // The array, its limits and its sharing rules:
 //  * kNoAllocScratchBytes (1 MiB) per device, a file-scope __device__ array

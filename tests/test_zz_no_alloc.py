@@ -1,6 +1,6 @@
 """b200q8_mul_mat_noalloc, the MUL_MAT entry point for callers that cannot
 allocate device memory (a ggml backend mid-graph, a real-time streaming
-callback, code under stream capture).  It keeps its scratch in a fixed 1 MiB
+callback that must not block on cudaMalloc).  It keeps its scratch in a fixed 1 MiB
 device array inside the library instead of a caller workspace.
 
 Checked through the C ABI against the existing entry point b200q8_mul_mat on
