@@ -60,9 +60,11 @@ __device__ __forceinline__ int group_max_int(int v) {
 }
 
 // All 32 lanes of the warp must call this (shuffles use the full mask).
-// lane_in_group = lane % G; v[e] is element lane_in_group*E + e of the block.
-template <int G, int E>
+// lane_in_group = lane % G; v[e] is element lane_in_group*E + e of the block,
+// or with STRIDED element lane_in_group + G*e.
+template <int G, int E, bool STRIDED = false>
 __device__ __forceinline__ float block_amax(const float (&v)[E], int lane_in_group) {
+    auto pos = [&](int e) { return STRIDED ? lane_in_group + G * e : lane_in_group * E + e; };
     bool has_nan = false;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
@@ -80,14 +82,14 @@ __device__ __forceinline__ float block_amax(const float (&v)[E], int lane_in_gro
 #pragma unroll
     for (int e = 0; e < E; ++e) {
         if (isnan(v[e])) {
-            last_nan = lane_in_group * E + e;
+            last_nan = max(last_nan, pos(e));
         }
     }
     last_nan = group_max_int<G>(last_nan);
     float m  = 0.0f;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-        if (lane_in_group * E + e > last_nan) {
+        if (pos(e) > last_nan) {
             m = fmaxf(m, fabsf(v[e]));
         }
     }
@@ -171,6 +173,14 @@ __device__ __forceinline__ void fence_mbar_init() {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// `count` arrivals in one operation (one thread standing in for `count`
+// warps that are known, through a barrier, to have arrived).
+__device__ __forceinline__ void mbar_arrive_count(uint64_t * bar, uint32_t count) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_addr(bar)),
+                 "r"(count)
                  : "memory");
 }
 

@@ -349,17 +349,15 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
     }
 }
 
-// Quantizes K values per token into the staging buffer xc/xd (chunk-major
-// layout of tile_dot.cuh).  LPB lanes per block, 32/LPB values per lane; the
-// caller picks LPB so that every block of a token is staged in one round
-// (LL inputs are waited for round by round).  src_kind: 0 = normed shared
-// buffer (hsrc * scale * norm), 1 = LL words via index map (GQA expansion
-// when map_gqa, else identity).  Ends with the consumer barrier, which also
-// ORs every thread's failure flag: returns true when the step must stop.
+// Quantizes K values per token of the normed shared buffer (hsrc * scale *
+// norm) into the staging buffer xc/xd (chunk-major layout of tile_dot.cuh).
+// LPB lanes per block, 32/LPB consecutive values per lane; the caller picks
+// LPB so that every block of a token is staged in one round.  Ends with the
+// consumer barrier, which also ORs every thread's failure flag: returns true
+// when the step must stop.
 template <int M_T, int MODE, int LPB>
-__device__ bool stage_activations_t(const StepArgs & a, const Smem & s, int K, int M, int src_kind, const float * hsrc,
-                                    const float * norm, const float (&scale)[M_T], const unsigned long long * ll,
-                                    size_t ll_stride, bool map_gqa, unsigned epoch, float * trace_x,
+__device__ bool stage_activations_t(const StepArgs & a, const Smem & s, int K, int M, const float * hsrc,
+                                    const float * norm, const float (&scale)[M_T], float * trace_x,
                                     size_t trace_stride, uint8_t * xc, float * xd, bool & fail) {
     constexpr int E    = 32 / LPB;  // values per lane
     constexpr int BPW  = 32 / LPB;  // blocks per warp per round
@@ -371,36 +369,14 @@ __device__ bool stage_activations_t(const StepArgs & a, const Smem & s, int K, i
     const int     eb   = lane % LPB;  // values E*eb .. E*eb+E-1 of the block
     for (int m = 0; m < M; ++m)
     for (int base = warp * BPW; base < NB; base += kStepConsumerWarps * BPW) {
-        const int  b     = base + gb;
-        const bool valid = b < NB;
-        const int  i0    = (valid ? b : 0) * kQK + eb * E;
-        float      v[E];
-        if (src_kind == 0) {
-            const float sc = scale[m < M_T ? m : 0];
+        const int   b     = base + gb;
+        const bool  valid = b < NB;
+        const int   i0    = (valid ? b : 0) * kQK + eb * E;
+        const float sc    = scale[m < M_T ? m : 0];
+        float       v[E];
 #pragma unroll
-            for (int k = 0; k < E; ++k) {
-                v[k] = valid ? __fmul_rn(__fmul_rn(hsrc[(size_t) m * K + i0 + k], sc), norm[i0 + k]) : 0.0f;
-            }
-        } else {
-            const unsigned long long * src[E];
-            unsigned long long         w[E];
-#pragma unroll
-            for (int k = 0; k < E; ++k) {
-                int j = i0 + k;
-                if (map_gqa) {  // query head j >> lg_hd reads kv head (j >> lg_hd) >> lg_group
-                    j = (((j >> a.lg_head_dim) >> a.lg_group) << a.lg_head_dim) | (j & ((1 << a.lg_head_dim) - 1));
-                }
-                src[k] = ll + (size_t) m * ll_stride + j;
-                w[k]   = valid ? ld_ll(src[k]) : ((unsigned long long) epoch << 32);
-            }
-            if (!fail && !ll_settle<E>(a, s, src, w, valid ? E : 0, epoch)) {
-                raise_abort(a, s);
-                fail = true;
-            }
-#pragma unroll
-            for (int k = 0; k < E; ++k) {
-                v[k] = valid ? __uint_as_float((unsigned) (w[k] & 0xffffffffu)) : 0.0f;
-            }
+        for (int k = 0; k < E; ++k) {
+            v[k] = valid ? __fmul_rn(__fmul_rn(hsrc[(size_t) m * K + i0 + k], sc), norm[i0 + k]) : 0.0f;
         }
         const float       am = block_amax<LPB, E>(v, eb);
         const QuantParams qp = quant_params<MODE>(am);
@@ -437,56 +413,184 @@ __device__ bool stage_activations_t(const StepArgs & a, const Smem & s, int K, i
     return consumers_any(fail || local_stop(s));
 }
 
+// Quantizes K values per token read from LL words (ll + m * ll_stride) into
+// xc/xd.  Lane eb of a block's LPB lanes holds the block's values eb + LPB*k,
+// so at every load the lanes of a warp read whole 32-byte sectors (a lane
+// holding consecutive values would make each load touch a sector per lane).
+// With lg_rep > 0 (the single cached position's GQA expansion) the source
+// holds K >> lg_rep values, a kv head per 1 << lg_rep query heads: each source
+// block is waited for and quantized once and stored at every query-head
+// position that reads it.  Ends with the consumer barrier, which also ORs
+// every thread's failure flag: returns true when the step must stop.
+template <int M_T, int MODE, int LPB>
+__device__ bool stage_ll_t(const StepArgs & a, const Smem & s, int K, int M, const unsigned long long * ll,
+                           size_t ll_stride, int lg_rep, unsigned epoch, float * trace_x, size_t trace_stride,
+                           uint8_t * xc, float * xd, bool & fail) {
+    constexpr int E    = 32 / LPB;  // values per lane
+    constexpr int BPW  = 32 / LPB;  // blocks per warp per round
+    const int     warp = threadIdx.x >> 5;
+    const int     lane = threadIdx.x & 31;
+    const int     NB   = K >> 5;
+    const int     NSB  = K >> 8;
+    const int     NBs  = NB >> lg_rep;  // source blocks
+    const int     gb   = lane / LPB;
+    const int     eb   = lane % LPB;
+    for (int m = 0; m < M; ++m)
+    for (int base = warp * BPW; base < NBs; base += kStepConsumerWarps * BPW) {
+        const int                  b     = base + gb;
+        const bool                 valid = b < NBs;
+        const unsigned long long * row   = ll + (size_t) m * ll_stride + (size_t) (valid ? b : 0) * kQK + eb;
+        const unsigned long long * src[E];
+        unsigned long long         w[E];
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+            src[k] = row + LPB * k;
+            w[k]   = valid ? ld_ll(src[k]) : ((unsigned long long) epoch << 32);
+        }
+        if (!fail && !ll_settle<E>(a, s, src, w, valid ? E : 0, epoch)) {
+            raise_abort(a, s);
+            fail = true;
+        }
+        float v[E];
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+            v[k] = valid ? __uint_as_float((unsigned) (w[k] & 0xffffffffu)) : 0.0f;
+        }
+        const float       am = block_amax<LPB, E, true>(v, eb);
+        const QuantParams qp = quant_params<MODE>(am);
+        uint8_t           code[E];
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+            code[k] = (uint8_t) (quant_code<MODE>(v[k], qp.id) & 0xff);
+        }
+        if (valid) {
+            for (int r = 0; r < (1 << lg_rep); ++r) {
+                int db = b;  // destination block of replica r
+                if (lg_rep > 0) {
+                    const int j  = b << 5;  // first source index of the block
+                    const int hk = j >> a.lg_head_dim;
+                    db = ((((hk << lg_rep) + r) << a.lg_head_dim) | (j & ((1 << a.lg_head_dim) - 1))) >> 5;
+                }
+#pragma unroll
+                for (int k = 0; k < E; ++k) {
+                    xc[sb_code_offset(m, K, NSB, db >> 3, ((db & 7) << 5) + eb + LPB * k)] = code[k];
+                }
+                if (eb == 0) {
+                    xd[m * NB + db] = qp.d;
+                }
+                if (trace_x != nullptr) {
+#pragma unroll
+                    for (int k = 0; k < E; ++k) {
+                        trace_x[(size_t) m * trace_stride + (size_t) db * kQK + eb + LPB * k] = v[k];
+                    }
+                }
+            }
+        }
+    }
+    return consumers_any(fail || local_stop(s));
+}
+
 // One round per token whatever K is: 8 lanes per block up to 32*kStepConsumerWarps/8
-// blocks, then 4, then 2.
+// blocks, then 4, then 2.  src_kind 0 stages the normed shared buffer
+// (stage_activations_t), 1 LL words (stage_ll_t; map_gqa: the source holds
+// the kv heads of the GQA expansion).
 template <int M_T, int MODE>
 __device__ bool stage_activations(const StepArgs & a, const Smem & s, int K, int M, int src_kind, const float * hsrc,
                                   const float * norm, const float (&scale)[M_T], const unsigned long long * ll,
                                   size_t ll_stride, bool map_gqa, unsigned epoch, float * trace_x, size_t trace_stride,
                                   uint8_t * xc, float * xd, bool & fail) {
+    if (src_kind == 1) {
+        const int lg_rep = map_gqa ? a.lg_group : 0;
+        const int NBs    = (K >> 5) >> lg_rep;
+        if (NBs <= kStepConsumerWarps * 4) {
+            return stage_ll_t<M_T, MODE, 8>(a, s, K, M, ll, ll_stride, lg_rep, epoch, trace_x, trace_stride, xc, xd,
+                                            fail);
+        }
+        if (NBs <= kStepConsumerWarps * 8) {
+            return stage_ll_t<M_T, MODE, 4>(a, s, K, M, ll, ll_stride, lg_rep, epoch, trace_x, trace_stride, xc, xd,
+                                            fail);
+        }
+        return stage_ll_t<M_T, MODE, 2>(a, s, K, M, ll, ll_stride, lg_rep, epoch, trace_x, trace_stride, xc, xd, fail);
+    }
     const int NB = K >> 5;
     if (NB <= kStepConsumerWarps * 4) {
-        return stage_activations_t<M_T, MODE, 8>(a, s, K, M, src_kind, hsrc, norm, scale, ll, ll_stride, map_gqa,
-                                                 epoch, trace_x, trace_stride, xc, xd, fail);
+        return stage_activations_t<M_T, MODE, 8>(a, s, K, M, hsrc, norm, scale, trace_x, trace_stride, xc, xd, fail);
     }
     if (NB <= kStepConsumerWarps * 8) {
-        return stage_activations_t<M_T, MODE, 4>(a, s, K, M, src_kind, hsrc, norm, scale, ll, ll_stride, map_gqa,
-                                                 epoch, trace_x, trace_stride, xc, xd, fail);
+        return stage_activations_t<M_T, MODE, 4>(a, s, K, M, hsrc, norm, scale, trace_x, trace_stride, xc, xd, fail);
     }
-    return stage_activations_t<M_T, MODE, 2>(a, s, K, M, src_kind, hsrc, norm, scale, ll, ll_stride, map_gqa, epoch,
-                                             trace_x, trace_stride, xc, xd, fail);
+    return stage_activations_t<M_T, MODE, 2>(a, s, K, M, hsrc, norm, scale, trace_x, trace_stride, xc, xd, fail);
 }
 
-// Consumes all tiles of one op in a single pass over all consumer warps.
-// The op's rows come from segs[0..nseg) in streaming order; with pair_units
-// the op has two segments of equal length (gate, up) and unit u is the row
-// pair (seg0 row u, seg1 row u), computed by one lane group so that SwiGLU
-// can be applied before publishing.  Otherwise nseg == 1 and unit u is row u.
-// publish(u, acc0, acc1) is called by lane 0 of the unit's group.
+// The tiles of one op occupy consecutive ring slots in streaming order: tile
+// i sits in slot (sl0 + i) mod S and was filled in round ph0, flipped once per
+// wrap of the ring.
+__device__ __forceinline__ int tile_slot(int sl0, int S, int i) {
+    int q = sl0 + i;
+    while (q >= S) {
+        q -= S;
+    }
+    return q;
+}
+
+__device__ __forceinline__ uint32_t tile_phase(int sl0, uint32_t ph0, int S, int i) {
+    int      q = sl0 + i;
+    uint32_t p = ph0;
+    while (q >= S) {
+        q -= S;
+        p ^= 1u;
+    }
+    return p;
+}
+
+// The tiles of an op still held when consume_op returns: [a0, a1) and
+// [b0, b1) of the op's tile indices, counted from slot sl0.
+struct Release {
+    int sl0 = 0;
+    int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+};
+
+// Hands the op's held slots back to the producer.  Called by every consumer
+// after the consumer barrier that ends the op (so every warp is done with the
+// slots, whose data each saw land): one thread arrives for all consumer warps
+// at once, while the others go on to the next op's inputs.
+__device__ __forceinline__ void release_tiles(const Smem & s, int S, const Release & r) {
+    if (threadIdx.x == kStepConsumers - 32) {  // lane 0 of the last consumer warp
+        for (int i = r.a0; i < r.a1; ++i) {
+            mbar_arrive_count(&s.empty[tile_slot(r.sl0, S, i)], kStepConsumerWarps);
+        }
+        for (int i = r.b0; i < r.b1; ++i) {
+            mbar_arrive_count(&s.empty[tile_slot(r.sl0, S, i)], kStepConsumerWarps);
+        }
+    }
+}
+
+// Consumes all tiles of one op over all consumer warps.  The op's rows come
+// from segs[0..nseg) in streaming order; with pair_units the op has two
+// segments of equal length (gate, up) and unit u is the row pair (seg0 row u,
+// seg1 row u), computed by one lane group so that SwiGLU can be applied
+// before publishing.  Otherwise nseg == 1 and unit u is row u.
+// publish(u, acc0, acc1) is called by lane 0 of the unit's group.  The slots
+// of the op's last round are left held and described in rel: the caller
+// releases them with release_tiles after the op's consumer barrier.
 template <int M_T, typename Pub>
 __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, int S, int & sl, uint32_t & ph,
                                            const Seg * segs, int nseg, bool pair_units, int K, int M, int warp,
                                            int lane, const uint8_t * xc, const float * xd, bool & fail, int op,
-                                           Pub && publish) {
-    constexpr int kMaxOpTiles = 16;
-    int           t_sl[kMaxOpTiles];
-    uint32_t      t_ph[kMaxOpTiles];
-    int           seg_first[2] = { 0, 0 };
-    int           nt           = 0;
+                                           Release & rel, Pub && publish) {
+    constexpr int  kMaxOpTiles  = 16;
+    const int      sl0          = sl;
+    const uint32_t ph0          = ph;
+    int            seg_first[2] = { 0, 0 };
+    int            nt           = 0;
     for (int g = 0; g < nseg; ++g) {
         seg_first[g] = nt;
-        for (int r = 0; r < segs[g].n; r += segs[g].sr) {
-            if (nt < kMaxOpTiles) {
-                t_sl[nt] = sl;
-                t_ph[nt] = ph;
-            }
-            ++nt;
-            if (++sl == S) {
-                sl = 0;
-                ph ^= 1u;
-            }
-        }
+        nt += seg_tiles(segs[g]);
     }
+    sl      = tile_slot(sl0, S, nt);  // the ring position after this op's tiles
+    ph      = tile_phase(sl0, ph0, S, nt);
+    rel     = Release();
+    rel.sl0 = sl0;
 #ifdef B200Q8_TIMELINE
     const long long tc0 = clock64();
 #endif
@@ -505,7 +609,8 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
     const long long tc1 = clock64();
     long long       tc_pub = 0;
 #endif
-    for (int k0 = 0; k0 < n_r && !bad; k0 += per_rd) {
+    int k0 = 0;
+    for (; k0 < n_r && !bad; k0 += per_rd) {
         const int k1  = min(n_r, k0 + per_rd);
         const int nin = (pair_units ? 2 : 1) * (k1 - k0);  // tiles of this round
         auto      tile = [&](int i) { return i < k1 - k0 ? k0 + i : seg_first[1] + k0 + (i - (k1 - k0)); };
@@ -513,7 +618,7 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
         bool rbad = false;
         if (lane < nin) {
             const int ti = tile(lane);
-            if (!mbar_wait_bounded(&s.full[t_sl[ti]], t_ph[ti])) {
+            if (!mbar_wait_bounded(&s.full[tile_slot(sl0, S, ti)], tile_phase(sl0, ph0, S, ti))) {
                 raise_abort(a, s);
                 rbad = true;
             }
@@ -537,12 +642,12 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
         const int      u_lo   = pair_units ? k0 * segs[0].sr : 0;
         const int      u_hi   = pair_units ? min(segs[0].n, k1 * segs[0].sr) : segs[0].n;
         auto row_addr = [&](int g, int r) -> uint32_t {
-            int ti = 0;
+            int ti = seg_first[g];
             while (r >= segs[g].sr) {
                 r -= segs[g].sr;
                 ++ti;
             }
-            return ring_s + (uint32_t) (t_sl[seg_first[g] + ti] * kStepSlotBytes) + (uint32_t) (r * segs[g].rb);
+            return ring_s + (uint32_t) (tile_slot(sl0, S, ti) * kStepSlotBytes) + (uint32_t) (r * segs[g].rb);
         };
         for (int ub = u_lo + warp * gpw; ub < u_hi; ub += ngroup) {  // warp-uniform
             const int  u      = ub + (lane >> lgs);
@@ -574,19 +679,16 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
             tc_pub += clock64() - tp0;
 #endif
         }
-        if (k1 < n_r) {
-            // a later round follows: this round's slots go back to the producer
-            // once every warp is done with them (their data was seen to land)
-            __syncwarp();
-            if (lane == 0) {
-                for (int i = 0; i < nin; ++i) {
-                    mbar_arrive(&s.empty[t_sl[tile(i)]]);
-                }
-            }
-        }
         if (k1 >= n_r) {
-            // the last round: its tiles are released below with the op's
-            break;
+            break;  // the last round: its tiles stay held for release_tiles
+        }
+        // a later round follows: this round's slots go back to the producer
+        // once every warp is done with them (their data was seen to land)
+        __syncwarp();
+        if (lane == 0) {
+            for (int i = 0; i < nin; ++i) {
+                mbar_arrive(&s.empty[tile_slot(sl0, S, tile(i))]);
+            }
         }
     }
     __syncwarp();
@@ -599,17 +701,15 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
             (unsigned long long) (tc2 - tc1 - tc_pub) | ((unsigned long long) tc_pub << 32);
     }
 #endif
-    // Release the op's last-round slots only after their data was seen to land: a slot
-    // whose copy may still be in flight must not be handed back to the
-    // producer (it then times out instead, and drains before it exits).
-    if (lane == 0 && !bad) {
-        const int k0l = n_r > per_rd ? (n_r - 1) / per_rd * per_rd : 0;  // the last round's first tile pair
-        for (int i = 0; i < nt; ++i) {
-            const int seg_i = pair_units && i >= seg_first[1] ? 1 : 0;
-            const int k     = i - seg_first[seg_i];
-            if (k >= k0l) {
-                mbar_arrive(&s.empty[t_sl[i]]);
-            }
+    // A slot whose copy may still be in flight must not be handed back to the
+    // producer (it then times out instead, and drains before it exits): after
+    // a failure nothing is released.
+    if (!bad) {
+        rel.a0 = k0;  // the last round's first tile of segment 0
+        rel.a1 = n_r;
+        if (pair_units) {
+            rel.b0 = seg_first[1] + k0;
+            rel.b1 = nt;
         }
     }
 }
@@ -1093,6 +1193,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     const Part   po  = plan.ph;
     const Part   pg  = plan.pi;
     bool         stopped = false;
+    Release      rel;      // the slots the last op still holds
 
     for (int l = 0; l < a.n_layers; ++l) {
         const StepLayerDev &       L    = a.layers[l];
@@ -1133,7 +1234,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 0, 2);
         {
             float * tq = trace(l, 1);
-            consume_op<M_T>(a, s, S, sl, ph, &segs[0], 1, false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 0,
+            consume_op<M_T>(a, s, S, sl, ph, &segs[0], 1, false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 0, rel,
                             [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
                                 const int row = pq.r0 + u;
 #pragma unroll
@@ -1157,6 +1258,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             stopped = true;
             break;
         }
+        release_tiles(s, S, rel);
         // ---- attention: one CTA per (query head, token) publishes the head's output
         if (ATTN) {
             const int n_head = a.Q >> a.lg_head_dim;
@@ -1189,7 +1291,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 1, 2);
         {
             float * to = trace(l, 3);
-            consume_op<M_T>(a, s, S, sl, ph, &segs[1], 1, false, a.Q, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 1,
+            consume_op<M_T>(a, s, S, sl, ph, &segs[1], 1, false, a.Q, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 1, rel,
                             [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
 #pragma unroll
                                 for (int m = 0; m < M_T; ++m) {
@@ -1210,6 +1312,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             stopped = true;
             break;
         }
+        release_tiles(s, S, rel);
         // ---- g|u = W_gate|W_up * Q(rms_norm(h1) * norm_post), h1 = h + o; s = silu(g)*u published
         TL(4 * l + 2, 0);
         residual_and_rms<M_T>(a, s, ll_o, s.hbuf, s.h1buf, M, epoch, c == 0 ? trace(l, 4) : nullptr, L.norm_post,
@@ -1225,7 +1328,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         {
             float * tgu = trace(l, 6);
             float * ts  = trace(l, 7);
-            consume_op<M_T>(a, s, S, sl, ph, &segs[2], 2, true, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 2,
+            consume_op<M_T>(a, s, S, sl, ph, &segs[2], 2, true, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 2, rel,
                             [&](int u, const float (&g)[M_T], const float (&up)[M_T]) {
 #pragma unroll
                                 for (int m = 0; m < M_T; ++m) {
@@ -1251,6 +1354,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             stopped = true;
             break;
         }
+        release_tiles(s, S, rel);
         // ---- d = W_down * Q(s); d published (the last layer writes h_out = h1 + d)
         TL(4 * l + 3, 0);
         if (stage_activations<M_T, MODE>(a, s, a.I, M, 1, nullptr, nullptr, no_scale, ll_s, (size_t) a.I, false,
@@ -1263,7 +1367,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         {
             float *    td   = trace(l, 8);
             const bool last = l == a.n_layers - 1;
-            consume_op<M_T>(a, s, S, sl, ph, &segs[4], 1, false, a.I, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 3,
+            consume_op<M_T>(a, s, S, sl, ph, &segs[4], 1, false, a.I, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 3, rel,
                             [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
                                 const int row = po.r0 + u;
 #pragma unroll
@@ -1289,6 +1393,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             stopped = true;
             break;
         }
+        release_tiles(s, S, rel);
     }
     if (stopped || fail || a.head == nullptr) {
         return;
@@ -1308,7 +1413,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         }
         const Seg  hs = head_seg(a, plan, c, G);
         const Part pv = part(a.vocab, G, c);
-        consume_op<M_T>(a, s, S, sl, ph, &hs, 1, false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 0,
+        consume_op<M_T>(a, s, S, sl, ph, &hs, 1, false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 0, rel,
                         [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
 #pragma unroll
                             for (int m = 0; m < M_T; ++m) {
