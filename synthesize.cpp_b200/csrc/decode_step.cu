@@ -138,6 +138,7 @@ struct Smem {
     float *    att;        // attention scratch (attention steps): q, 2 k, 2 v rows, per-warp partials
     AttTok *   tok;        // attention steps: positions and slots of the launch's tokens
     uint8_t *  ring;
+    double     inv_h;      // 1 / H when H is a power of two, else 0
 };
 
 // Floats of attention scratch: q [hd], k and v of up to 2 in-launch tokens
@@ -260,9 +261,17 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
                                  const float * norm, bool & fail, float (&scale_out)[M_T]) {
     const int H = a.H;
     const int t = threadIdx.x;
-    // The norm weight goes to shared memory now, its L2 latency hidden under
-    // the wait for the previous op's outputs.
-    for (int i = t; i < H; i += kStepConsumers) {
+    // The norm weight is loaded into registers now and stored to shared
+    // memory after the wait for the previous op's outputs, which hides its L2
+    // latency (a store right behind the load would stall on it).
+    constexpr int kNormRegs = 8;  // widths up to 8 * kStepConsumers
+    float         nreg[kNormRegs];
+#pragma unroll
+    for (int k = 0; k < kNormRegs; ++k) {
+        const int i = t + k * kStepConsumers;
+        nreg[k]     = i < H ? norm[i] : 0.0f;
+    }
+    for (int i = t + kNormRegs * kStepConsumers; i < H; i += kStepConsumers) {
         s.normbuf[i] = norm[i];
     }
     double    ss[M_T];
@@ -323,6 +332,13 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
             }
         }
     }
+#pragma unroll
+    for (int k = 0; k < kNormRegs; ++k) {
+        const int i = t + k * kStepConsumers;
+        if (i < H) {
+            s.normbuf[i] = nreg[k];
+        }
+    }
     const int warp = t >> 5;
     const int lane = t & 31;
 #pragma unroll
@@ -344,7 +360,8 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
         for (int w = 0; w < kStepConsumerWarps; ++w) {
             tot += s.rms_part[w * 2 + m];
         }
-        const float mean = (float) (tot / (double) H);
+        // dividing by a power of two is multiplying by its exact reciprocal
+        const float mean = (float) (s.inv_h != 0.0 ? tot * s.inv_h : tot / (double) H);
         scale_out[m]     = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
     }
 }
@@ -1049,7 +1066,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         off += att_scratch_floats(a.head_dim) * 4;
     }
     off    = (off + 127) & ~(size_t) 127;
-    s.ring = smem + off;
+    s.ring  = smem + off;
+    s.inv_h = (H & (H - 1)) == 0 ? 1.0 / (double) H : 0.0;
     const int S = a.n_slots;
 
     if (threadIdx.x == 0) {
@@ -1204,10 +1222,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         unsigned long long * const ll_d   = ll_s + llm * a.I;
         Seg                        segs[5];
         layer_segs(a, plan, l, segs);
-        if (att_cta) {  // this layer's q_norm / k_norm, read after the qkv op
-            float * qk = s.att + att_norm_offset(a.head_dim);
-            for (int i = t_id; i < 2 * a.head_dim; i += kStepConsumers) {
-                qk[i] = i < a.head_dim ? L.q_norm[i] : L.k_norm[i - a.head_dim];
+        // attention CTAs: this layer's q_norm | k_norm (2 * head_dim <= 512
+        // values), loaded now and stored to shared memory after the qkv op, so
+        // that no thread stalls on the loads
+        float qkn[2] = { 0.0f, 0.0f };
+        if (ATTN && att_cta) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int i = t_id + k * kStepConsumers;
+                if (i < 2 * a.head_dim) {
+                    qkn[k] = i < a.head_dim ? L.q_norm[i] : L.k_norm[i - a.head_dim];
+                }
             }
         }
 
@@ -1251,6 +1276,16 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                             });
         }
         TL(4 * l + 0, 3);
+        if (ATTN && att_cta) {  // read by the attention phase, after the barrier below
+            float * qk = s.att + att_norm_offset(a.head_dim);
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int i = t_id + k * kStepConsumers;
+                if (i < 2 * a.head_dim) {
+                    qk[i] = qkn[k];
+                }
+            }
+        }
         // park warps that are done until the whole op is: a warp polling the
         // next op's inputs would steal issue slots from warps still computing
         if (consumers_any(fail || local_stop(s))) {
