@@ -582,32 +582,82 @@ __device__ __forceinline__ void release_tiles(const Smem & s, int S, const Relea
     }
 }
 
-// Consumes all tiles of one op over all consumer warps.  The op's rows come
-// from segs[0..nseg) in streaming order; with pair_units the op has two
-// segments of equal length (gate, up) and unit u is the row pair (seg0 row u,
-// seg1 row u), computed by one lane group so that SwiGLU can be applied
-// before publishing.  Otherwise nseg == 1 and unit u is row u.
-// publish(u, acc0, acc1) is called by lane 0 of the unit's group.  The slots
-// of the op's last round are left held and described in rel: the caller
-// releases them with release_tiles after the op's consumer barrier.
-template <int M_T, typename Pub>
-__device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, int S, int & sl, uint32_t & ph,
-                                           const Seg * segs, int nseg, bool pair_units, int K, int M, int warp,
-                                           int lane, const uint8_t * xc, const float * xd, bool & fail, int op,
-                                           Release & rel, Pub && publish) {
-    constexpr int  kMaxOpTiles  = 16;
-    const int      sl0          = sl;
-    const uint32_t ph0          = ph;
-    int            seg_first[2] = { 0, 0 };
-    int            nt           = 0;
+// One op's tile geometry and ring position, worked out (and its first
+// round's tiles waited for) by plan_op before the op's inputs are: none of it
+// depends on them, and a CTA always has time to spare while the previous op's
+// outputs travel.
+struct OpRun {
+    int      sl0;     // slot of the op's first tile
+    uint32_t ph0;     // its fill round mod 2
+    int      nt;      // tiles of the op
+    int      seg1;    // first tile of segment 1
+    int      n_r;     // tiles per segment (pair ops) or all tiles
+    int      per_rd;  // tile pairs per round (pair ops larger than the ring)
+    int      lgs;     // log2 of the lanes per row group (~1 half-superblock per lane)
+};
+
+// Plans the op on segs[0..nseg) (pair_units: two equal segments consumed as
+// row pairs) at ring position sl / ph, advances sl / ph past its tiles and
+// waits for the tiles of its first round: lane i of each warp waits for tile
+// i, so the round is checked in one go.  Sets fail (warp-uniform) when a wait
+// timed out or the op is beyond the tile table.
+__device__ __forceinline__ OpRun plan_op(const StepArgs & a, const Smem & s, int S, int & sl, uint32_t & ph,
+                                         const Seg * segs, int nseg, bool pair_units, int K, int lane, bool & fail) {
+    constexpr int kMaxOpTiles = 16;
+    OpRun         o;
+    o.sl0  = sl;
+    o.ph0  = ph;
+    o.nt   = 0;
+    o.seg1 = 0;
     for (int g = 0; g < nseg; ++g) {
-        seg_first[g] = nt;
-        nt += seg_tiles(segs[g]);
+        if (g == 1) {
+            o.seg1 = o.nt;
+        }
+        o.nt += seg_tiles(segs[g]);
     }
-    sl      = tile_slot(sl0, S, nt);  // the ring position after this op's tiles
-    ph      = tile_phase(sl0, ph0, S, nt);
+    sl       = tile_slot(o.sl0, S, o.nt);  // the ring position after this op's tiles
+    ph       = tile_phase(o.sl0, o.ph0, S, o.nt);
+    o.n_r    = pair_units ? o.seg1 : o.nt;
+    o.per_rd = pair_units && 2 * o.n_r > S ? min(o.n_r, S - o.n_r) : o.n_r;
+    o.lgs    = min(5, 32 - __clz(2 * (K >> 8) - 1));
+    // an op with no rows in this CTA (narrow shapes) has nothing to wait for;
+    // an op beyond the tile table is refused by decode_step_supported, and is
+    // recorded as an internal error should it get here
+    const bool too_big = o.nt > kMaxOpTiles || (o.nt > 0 && o.per_rd < 1);
+    if (too_big && lane == 0) {
+        record_device_error((unsigned) B200Q8_ERR_INTERNAL);
+    }
+    const int k1   = min(o.n_r, o.per_rd);
+    const int nin  = (pair_units ? 2 : 1) * k1;
+    bool      rbad = false;
+    if (!fail && !too_big && lane < nin) {
+        const int ti = lane < k1 ? lane : o.seg1 + (lane - k1);
+        if (!mbar_wait_bounded(&s.full[tile_slot(o.sl0, S, ti)], tile_phase(o.sl0, o.ph0, S, ti))) {
+            raise_abort(a, s);
+            rbad = true;
+        }
+    }
+    rbad = __any_sync(0xffffffffu, rbad);
+    fail = fail || rbad || too_big;
+    return o;
+}
+
+// Consumes all tiles of the op planned in o over all consumer warps.  The
+// op's rows come from segs[0..nseg) in streaming order; with pair_units the
+// op has two segments of equal length (gate, up) and unit u is the row pair
+// (seg0 row u, seg1 row u), computed by one lane group so that SwiGLU can be
+// applied before publishing.  Otherwise nseg == 1 and unit u is row u.
+// publish(u, acc0, acc1) is called by lane 0 of the unit's group.  The first
+// round's tiles were waited for by plan_op.  The slots of the op's last
+// round are left held and described in rel: the caller releases them with
+// release_tiles after the op's consumer barrier.
+template <int M_T, typename Pub>
+__device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, int S, const OpRun & o,
+                                           const Seg * segs, bool pair_units, int K, int M, int warp, int lane,
+                                           const uint8_t * xc, const float * xd, bool & fail, int op, Release & rel,
+                                           Pub && publish) {
     rel     = Release();
-    rel.sl0 = sl0;
+    rel.sl0 = o.sl0;
 #ifdef B200Q8_TIMELINE
     const long long tc0 = clock64();
 #endif
@@ -618,56 +668,53 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
     // the slot of a fill from an earlier op, and each later round's last fill
     // reuses a slot an earlier round released, so the producer never waits on
     // a slot the consumers still hold.
-    const int n_r    = pair_units ? seg_first[1] : nt;  // tiles per segment
-    const int per_rd = pair_units && 2 * n_r > S ? min(n_r, S - n_r) : n_r;
-    bool      bad    = fail || nt > kMaxOpTiles || nt > 32 || per_rd < 1;  // warp-uniform
-    fail             = fail || bad;
+    bool bad = fail;  // warp-uniform
 #ifdef B200Q8_TIMELINE
     const long long tc1 = clock64();
     long long       tc_pub = 0;
 #endif
-    int k0 = 0;
-    for (; k0 < n_r && !bad; k0 += per_rd) {
-        const int k1  = min(n_r, k0 + per_rd);
+    const int      NSB    = K >> 8;  // superblocks per row
+    const int      NB     = K >> 5;
+    const int      GS     = 1 << o.lgs;
+    const int      gpw    = 32 >> o.lgs;  // groups per warp
+    const int      ngroup = kStepConsumerWarps * gpw;
+    const int      gl     = lane & (GS - 1);
+    const uint32_t xc_s   = smem_addr(xc);
+    const uint32_t xd_s   = smem_addr(xd);
+    const uint32_t ring_s = smem_addr(s.ring);
+    int            k0     = 0;
+    for (; k0 < o.n_r && !bad; k0 += o.per_rd) {
+        const int k1  = min(o.n_r, k0 + o.per_rd);
         const int nin = (pair_units ? 2 : 1) * (k1 - k0);  // tiles of this round
-        auto      tile = [&](int i) { return i < k1 - k0 ? k0 + i : seg_first[1] + k0 + (i - (k1 - k0)); };
-        // lane i probes the round's tile i, so its tiles are checked in one go
-        bool rbad = false;
-        if (lane < nin) {
-            const int ti = tile(lane);
-            if (!mbar_wait_bounded(&s.full[tile_slot(sl0, S, ti)], tile_phase(sl0, ph0, S, ti))) {
-                raise_abort(a, s);
-                rbad = true;
+        auto      tile = [&](int i) { return i < k1 - k0 ? k0 + i : o.seg1 + k0 + (i - (k1 - k0)); };
+        if (k0 > 0) {  // a later round of a pair op larger than the ring
+            bool rbad = false;
+            if (lane < nin) {
+                const int ti = tile(lane);
+                if (!mbar_wait_bounded(&s.full[tile_slot(o.sl0, S, ti)], tile_phase(o.sl0, o.ph0, S, ti))) {
+                    raise_abort(a, s);
+                    rbad = true;
+                }
+            }
+            rbad = __any_sync(0xffffffffu, rbad);
+            if (rbad) {
+                bad  = true;
+                fail = true;
+                break;
             }
         }
-        rbad = __any_sync(0xffffffffu, rbad);
-        if (rbad) {
-            bad  = true;
-            fail = true;
-            break;
-        }
-        const int      NSB    = K >> 8;  // superblocks per row
-        const int      NB     = K >> 5;
-        const int      lgs    = min(5, 32 - __clz(2 * NSB - 1));  // ~1 half-superblock per lane
-        const int      GS     = 1 << lgs;
-        const int      gpw    = 32 >> lgs;  // groups per warp
-        const int      ngroup = kStepConsumerWarps * gpw;
-        const int      gl     = lane & (GS - 1);
-        const uint32_t xc_s   = smem_addr(xc);
-        const uint32_t xd_s   = smem_addr(xd);
-        const uint32_t ring_s = smem_addr(s.ring);
-        const int      u_lo   = pair_units ? k0 * segs[0].sr : 0;
-        const int      u_hi   = pair_units ? min(segs[0].n, k1 * segs[0].sr) : segs[0].n;
+        const int u_lo = pair_units ? k0 * segs[0].sr : 0;
+        const int u_hi = pair_units ? min(segs[0].n, k1 * segs[0].sr) : segs[0].n;
         auto row_addr = [&](int g, int r) -> uint32_t {
-            int ti = seg_first[g];
+            int ti = g ? o.seg1 : 0;
             while (r >= segs[g].sr) {
                 r -= segs[g].sr;
                 ++ti;
             }
-            return ring_s + (uint32_t) (tile_slot(sl0, S, ti) * kStepSlotBytes) + (uint32_t) (r * segs[g].rb);
+            return ring_s + (uint32_t) (tile_slot(o.sl0, S, ti) * kStepSlotBytes) + (uint32_t) (r * segs[g].rb);
         };
         for (int ub = u_lo + warp * gpw; ub < u_hi; ub += ngroup) {  // warp-uniform
-            const int  u      = ub + (lane >> lgs);
+            const int  u      = ub + (lane >> o.lgs);
             const bool active = u < u_hi;
             float      acc0[M_T], acc1[M_T];
 #pragma unroll
@@ -696,7 +743,7 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
             tc_pub += clock64() - tp0;
 #endif
         }
-        if (k1 >= n_r) {
+        if (k1 >= o.n_r) {
             break;  // the last round: its tiles stay held for release_tiles
         }
         // a later round follows: this round's slots go back to the producer
@@ -704,7 +751,7 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
         __syncwarp();
         if (lane == 0) {
             for (int i = 0; i < nin; ++i) {
-                mbar_arrive(&s.empty[tile_slot(sl0, S, tile(i))]);
+                mbar_arrive(&s.empty[tile_slot(o.sl0, S, tile(i))]);
             }
         }
     }
@@ -723,10 +770,10 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
     // a failure nothing is released.
     if (!bad) {
         rel.a0 = k0;  // the last round's first tile of segment 0
-        rel.a1 = n_r;
+        rel.a1 = o.n_r;
         if (pair_units) {
-            rel.b0 = seg_first[1] + k0;
-            rel.b1 = nt;
+            rel.b0 = o.seg1 + k0;
+            rel.b1 = o.nt;
         }
     }
 }
@@ -1247,6 +1294,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 0, 0);
         const unsigned long long * prev_d =
             l > 0 ? a.ll + (size_t) (l - 1) * a.ll_layer + llm * (qkv_dim + a.Q + a.H + a.I) : nullptr;
+        const OpRun o_qkv = plan_op(a, s, S, sl, ph, &segs[0], 1, false, H, lane, fail);
         residual_and_rms<M_T>(a, s, prev_d, s.h1buf, s.hbuf, M, epoch, (l > 0 && c == 0) ? trace(l - 1, 9) : nullptr,
                               L.norm_in, fail, scale);
         TL(4 * l + 0, 1);
@@ -1259,7 +1307,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 0, 2);
         {
             float * tq = trace(l, 1);
-            consume_op<M_T>(a, s, S, sl, ph, &segs[0], 1, false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 0, rel,
+            consume_op<M_T>(a, s, S, o_qkv, &segs[0], false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 0, rel,
                             [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
                                 const int row = pq.r0 + u;
 #pragma unroll
@@ -1316,6 +1364,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // ---- o = W_o * Q(attend); attention over the cache, or over one cached position; o published
         TL(4 * l + 1, 0);
         const unsigned long long * o_src = ATTN ? ll_att : ll_qkv + a.Q + a.KV;
+        const OpRun o_o = plan_op(a, s, S, sl, ph, &segs[1], 1, false, a.Q, lane, fail);
         if (stage_activations<M_T, MODE>(a, s, a.Q, M, 1, nullptr, nullptr, no_scale, o_src,
                                          ATTN ? (size_t) a.Q : (size_t) qkv_dim, !ATTN, epoch,
                                          c == 0 ? trace(l, 2) : nullptr, (size_t) a.Q, s.xc[1], s.xd[1], fail)) {
@@ -1326,7 +1375,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         TL(4 * l + 1, 2);
         {
             float * to = trace(l, 3);
-            consume_op<M_T>(a, s, S, sl, ph, &segs[1], 1, false, a.Q, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 1, rel,
+            consume_op<M_T>(a, s, S, o_o, &segs[1], false, a.Q, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 1, rel,
                             [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
 #pragma unroll
                                 for (int m = 0; m < M_T; ++m) {
@@ -1350,6 +1399,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         release_tiles(s, S, rel);
         // ---- g|u = W_gate|W_up * Q(rms_norm(h1) * norm_post), h1 = h + o; s = silu(g)*u published
         TL(4 * l + 2, 0);
+        const OpRun o_gu = plan_op(a, s, S, sl, ph, &segs[2], 2, true, H, lane, fail);
         residual_and_rms<M_T>(a, s, ll_o, s.hbuf, s.h1buf, M, epoch, c == 0 ? trace(l, 4) : nullptr, L.norm_post,
                               fail, scale);
         TL(4 * l + 2, 1);
@@ -1363,7 +1413,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         {
             float * tgu = trace(l, 6);
             float * ts  = trace(l, 7);
-            consume_op<M_T>(a, s, S, sl, ph, &segs[2], 2, true, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 2, rel,
+            consume_op<M_T>(a, s, S, o_gu, &segs[2], true, H, M, warp, lane, s.xc[0], s.xd[0], fail, 4 * l + 2, rel,
                             [&](int u, const float (&g)[M_T], const float (&up)[M_T]) {
 #pragma unroll
                                 for (int m = 0; m < M_T; ++m) {
@@ -1392,6 +1442,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         release_tiles(s, S, rel);
         // ---- d = W_down * Q(s); d published (the last layer writes h_out = h1 + d)
         TL(4 * l + 3, 0);
+        const OpRun o_d = plan_op(a, s, S, sl, ph, &segs[4], 1, false, a.I, lane, fail);
         if (stage_activations<M_T, MODE>(a, s, a.I, M, 1, nullptr, nullptr, no_scale, ll_s, (size_t) a.I, false,
                                          epoch, nullptr, 0, s.xc[1], s.xd[1], fail)) {
             stop_producer(s);
@@ -1402,7 +1453,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         {
             float *    td   = trace(l, 8);
             const bool last = l == a.n_layers - 1;
-            consume_op<M_T>(a, s, S, sl, ph, &segs[4], 1, false, a.I, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 3, rel,
+            consume_op<M_T>(a, s, S, o_d, &segs[4], false, a.I, M, warp, lane, s.xc[1], s.xd[1], fail, 4 * l + 3, rel,
                             [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
                                 const int row = po.r0 + u;
 #pragma unroll
@@ -1438,7 +1489,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     {
         const unsigned long long * last_d =
             a.ll + (size_t) (a.n_layers - 1) * a.ll_layer + llm * (qkv_dim + a.Q + a.H + a.I);
-        float scale[M_T];
+        float      scale[M_T];
+        const Seg  hs     = head_seg(a, plan, c, G);
+        const Part pv     = part(a.vocab, G, c);
+        const OpRun o_h   = plan_op(a, s, S, sl, ph, &hs, 1, false, H, lane, fail);
         residual_and_rms<M_T>(a, s, last_d, s.h1buf, s.hbuf, M, epoch, c == 0 ? a.h_out : nullptr, a.out_norm, fail,
                               scale);
         if (stage_activations<M_T, MODE>(a, s, H, M, 0, s.hbuf, s.normbuf, scale, nullptr, 0, false, epoch,
@@ -1446,9 +1500,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             stop_producer(s);
             return;
         }
-        const Seg  hs = head_seg(a, plan, c, G);
-        const Part pv = part(a.vocab, G, c);
-        consume_op<M_T>(a, s, S, sl, ph, &hs, 1, false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 0, rel,
+        consume_op<M_T>(a, s, S, o_h, &hs, false, H, M, warp, lane, s.xc[0], s.xd[0], fail, 0, rel,
                         [&](int u, const float (&y)[M_T], const float (&)[M_T]) {
 #pragma unroll
                             for (int m = 0; m < M_T; ++m) {
