@@ -225,8 +225,9 @@ __device__ __forceinline__ void stop_producer(const Smem & s) {
 // Reads n LL words (this thread's share, already loaded in w[]) until all
 // carry `epoch`.  Returns false on timeout/abort.
 template <int N>
-__device__ __forceinline__ bool ll_settle(const StepArgs & a, const Smem & s, const unsigned long long * const (&src)[N],
-                                          unsigned long long (&w)[N], int n, unsigned epoch) {
+__device__ __forceinline__ bool ll_settle_one(const StepArgs & a, const Smem & s,
+                                              const unsigned long long * const (&src)[N], unsigned long long (&w)[N],
+                                              int n, unsigned epoch) {
     long long start = -1;
     for (unsigned iter = 0;; ++iter) {
         bool done = true;
@@ -249,6 +250,90 @@ __device__ __forceinline__ bool ll_settle(const StepArgs & a, const Smem & s, co
             return false;
         }
     }
+}
+
+template <int N>
+__device__ __forceinline__ bool ll_settle(const StepArgs & a, const Smem & s, const unsigned long long * const (&src)[N],
+                                          unsigned long long (&w)[N], int n, unsigned epoch) {
+    if (N > 4) {  // the staggered second reads would not fit the registers
+        return ll_settle_one<N>(a, s, src, w, n, epoch);
+    }
+    unsigned pend = 0;  // words not yet seen with this launch's epoch
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        if (i < n && (unsigned) (w[i] >> 32) != epoch) {
+            pend |= 1u << i;
+        }
+    }
+    if (pend == 0) {
+        return true;
+    }
+    // Two reads of each pending word stay in flight, the second started
+    // kPollStagger cycles after the first, so a word that lands is seen about
+    // half a round trip sooner than with one read at a time.  Landed words go
+    // to val (a register a read is still headed for is never written over).
+    constexpr long long kPollStagger = 300;
+    unsigned long long  val[N];
+    unsigned long long  r1[N], r2[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        val[i] = w[i];
+        r1[i]  = w[i];
+    }
+    const long long start = clock64();
+    while (clock64() - start < kPollStagger) {
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        r2[i] = (pend >> i) & 1u ? ld_ll(src[i]) : 0ull;
+    }
+    for (unsigned iter = 0;; ++iter) {
+        // the pending words' first reads (r1 holds the caller's reads at first)
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            if (((pend >> i) & 1u) && (unsigned) (r1[i] >> 32) == epoch) {
+                val[i] = r1[i];
+                pend &= ~(1u << i);
+            }
+        }
+        if (pend == 0) {
+            break;
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            if ((pend >> i) & 1u) {
+                r1[i] = ld_ll(src[i]);
+            }
+        }
+        // their second reads
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            if (((pend >> i) & 1u) && (unsigned) (r2[i] >> 32) == epoch) {
+                val[i] = r2[i];
+                pend &= ~(1u << i);
+            }
+        }
+        if (pend == 0) {
+            break;
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            if ((pend >> i) & 1u) {
+                r2[i] = ld_ll(src[i]);
+            }
+        }
+        if (clock64() - start > kWaitLimitCycles) {
+            return false;
+        } else if ((iter & 255u) == 255u && aborted(a, s)) {
+            // the global abort word costs an L2 round trip: look rarely
+            return false;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        w[i] = val[i];
+    }
+    return true;
 }
 
 // Phase A of a norm stage: h_dst[m][i] = h_src[m][i] + published delta[m][i]
