@@ -1208,12 +1208,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             mbar_init(&s.empty[i], kStepConsumerWarps);
         }
         *s.abort_local = 0;
-        // launch k (1-based) of this plan: every CTA computes the same k
-        *s.epoch = atomicAdd(&a.sync[0], 1u) / (unsigned) G + 1u;
         fence_mbar_init();
     }
     __syncthreads();
-    const unsigned epoch = *s.epoch;
     const int      warp  = threadIdx.x >> 5;
     const int      lane  = threadIdx.x & 31;
     const Plan     plan  = make_plan(a, c, G);
@@ -1284,6 +1281,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
 
     // ----------------------------------------------------------- consumers
     const int t_id = threadIdx.x;
+    if (t_id == 0) {
+        // launch k (1-based) of this plan: every CTA computes the same k.  Taken
+        // here, not before the CTA barrier above, so that the producer's first
+        // copies do not wait for the atomic's round trip; the consumers read it
+        // after their barrier below, and the producer only on a timeout.
+        *s.epoch = atomicAdd(&a.sync[0], 1u) / (unsigned) G + 1u;
+    }
     // step input: h = x_in + get_rows(table, ids), every CTA for itself
     // (either term may be absent: ids == nullptr or x_in == nullptr)
     for (int m = 0; m < M; ++m) {
@@ -1330,6 +1334,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         }
     }
     named_barrier_sync(1, kStepConsumers);
+    const unsigned epoch = *s.epoch;
 
     const int qkv_dim = a.Q + 2 * a.KV;
     int       sl      = 0;      // slot of the next tile, mirrors the producer
