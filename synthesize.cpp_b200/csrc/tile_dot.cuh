@@ -197,77 +197,23 @@ __device__ __forceinline__ void group_reduce(float (&acc)[M_T], int GS) {
 // aligned whenever the row is (K % 256 == 0).  A lane reads one with 17
 // 128-bit shared loads.  Activation layout for this path ("chunk-major"):
 // token m's codes occupy K bytes at m*K; 16-byte chunk c (0..15) of
-// superblock j sits at m*K + (c*NSB + j)*16, so the lanes of a row group,
-// which read the same chunk of consecutive superblocks, touch consecutive
-// 16-byte words.  Scales: fp32 at [m*NB + b] as before.
+// superblock j sits at m*K + ((c*NSB + j)*16 XOR 64*(c >= 8)), so the lanes
+// of a row group, which read the same chunk of consecutive superblocks, touch
+// consecutive 16-byte words.  The XOR moves the second half-superblock's
+// chunks by 16 banks: the lanes on the first and on the second half of the
+// same superblocks would otherwise read the same banks (a two-way conflict on
+// every activation load at K = 1024).  Bit 6 flips inside a 128-byte segment
+// of the second half's region, so the layout stays a permutation.  Scales:
+// fp32 at [m*NB + b] as before.
 
 // Byte offset of code `pos` (0..255) of superblock j of token m.
 __device__ __forceinline__ int sb_code_offset(int m, int K, int NSB, int j, int pos) {
-    return m * K + (((pos >> 4) * NSB + j) << 4) + (pos & 15);
-}
-
-// This lane's partial dot product of one weight row with the M staged tokens
-// over superblocks gl, gl+GS, ... < NSB.
-template <int M_T>
-__device__ __forceinline__ void dot_row_sb(uint32_t row, int NSB, int NB, int K, int gl, int GS, uint32_t xc_s,
-                                           uint32_t xd_s, int M, float (&acc)[M_T]) {
-    for (int j = gl; j < NSB; j += GS) {
-        uint32_t w[68];
-#pragma unroll
-        for (int k = 0; k < 17; ++k) {
-            const uint4 v = lds_v4(row + (uint32_t) (272 * j + 16 * k));
-            w[4 * k]      = v.x;
-            w[4 * k + 1]  = v.y;
-            w[4 * k + 2]  = v.z;
-            w[4 * k + 3]  = v.w;
-        }
-#pragma unroll
-        for (int m = 0; m < M_T; ++m) {
-            if (m < M) {
-                const uint4 dlo = lds_v4(xd_s + (uint32_t) ((m * NB + 8 * j) * 4));
-                const uint4 dhi = lds_v4(xd_s + (uint32_t) ((m * NB + 8 * j + 4) * 4));
-                const float dx[8] = { __uint_as_float(dlo.x), __uint_as_float(dlo.y), __uint_as_float(dlo.z),
-                                      __uint_as_float(dlo.w), __uint_as_float(dhi.x), __uint_as_float(dhi.y),
-                                      __uint_as_float(dhi.z), __uint_as_float(dhi.w) };
-#pragma unroll
-                for (int b = 0; b < 8; ++b) {
-                    // block b of the superblock: scale and codes out of the 68 words
-                    const int      wb = 17 * (b >> 1);
-                    const float    dw = __half2float(__ushort_as_half(
-                        (unsigned short) ((b & 1) ? (w[wb + 8] >> 16) : (w[wb] & 0xffffu))));
-                    const uint32_t x0 = xc_s + (uint32_t) (m * K + (((2 * b) * NSB + j) << 4));
-                    const uint4    xa = lds_v4(x0);
-                    const uint4    xb = lds_v4(x0 + (uint32_t) (NSB << 4));
-                    int            s0 = 0, s1 = 0;
-                    if (b & 1) {
-                        s0 = __dp4a((int) w[wb + 9], (int) xa.x, s0);
-                        s1 = __dp4a((int) w[wb + 10], (int) xa.y, s1);
-                        s0 = __dp4a((int) w[wb + 11], (int) xa.z, s0);
-                        s1 = __dp4a((int) w[wb + 12], (int) xa.w, s1);
-                        s0 = __dp4a((int) w[wb + 13], (int) xb.x, s0);
-                        s1 = __dp4a((int) w[wb + 14], (int) xb.y, s1);
-                        s0 = __dp4a((int) w[wb + 15], (int) xb.z, s0);
-                        s1 = __dp4a((int) w[wb + 16], (int) xb.w, s1);
-                    } else {
-                        s0 = __dp4a((int) __byte_perm(w[wb + 0], w[wb + 1], 0x5432), (int) xa.x, s0);
-                        s1 = __dp4a((int) __byte_perm(w[wb + 1], w[wb + 2], 0x5432), (int) xa.y, s1);
-                        s0 = __dp4a((int) __byte_perm(w[wb + 2], w[wb + 3], 0x5432), (int) xa.z, s0);
-                        s1 = __dp4a((int) __byte_perm(w[wb + 3], w[wb + 4], 0x5432), (int) xa.w, s1);
-                        s0 = __dp4a((int) __byte_perm(w[wb + 4], w[wb + 5], 0x5432), (int) xb.x, s0);
-                        s1 = __dp4a((int) __byte_perm(w[wb + 5], w[wb + 6], 0x5432), (int) xb.y, s1);
-                        s0 = __dp4a((int) __byte_perm(w[wb + 6], w[wb + 7], 0x5432), (int) xb.z, s0);
-                        s1 = __dp4a((int) __byte_perm(w[wb + 7], w[wb + 8], 0x5432), (int) xb.w, s1);
-                    }
-                    acc[m] = __fmaf_rn((float) (s0 + s1), __fmul_rn(dw, dx[b]), acc[m]);
-                }
-            }
-        }
-    }
+    return m * K + (((((pos >> 4) * NSB + j) << 4) ^ ((pos >> 7) << 6)) | (pos & 15));
 }
 
 // Half-superblock units: a lane takes 4 blocks (136 bytes, 8-byte aligned:
-// 17 64-bit shared loads) -- twice the lanes of dot_row_sb on the same row,
-// half the work per lane.  Unit u of a row is half (u & 1) of superblock
+// 17 64-bit shared loads) -- twice the lanes of a whole-superblock split on
+// the same row, half the work per lane.  Unit u of a row is half (u & 1) of superblock
 // (u >> 1).
 template <int M_T>
 __device__ __forceinline__ void dot_row_half(uint32_t row, int NSB, int NB, int K, int gl, int GS, uint32_t xc_s,
@@ -297,9 +243,10 @@ __device__ __forceinline__ void dot_row_half(uint32_t row, int NSB, int NB, int 
                     const float    dw = __half2float(__ushort_as_half(
                         (unsigned short) ((b & 1) ? (w[wb + 8] >> 16) : (w[wb] & 0xffffu))));
                     const int      bs = 4 * h + b;  // block within the superblock
-                    const uint32_t x0 = xc_s + (uint32_t) (m * K + (((2 * bs) * NSB + j) << 4));
-                    const uint4    xa = lds_v4(x0);
-                    const uint4    xb = lds_v4(x0 + (uint32_t) (NSB << 4));
+                    // chunks 2bs and 2bs+1 of superblock j (sb_code_offset's layout)
+                    const uint32_t xm = xc_s + (uint32_t) (m * K);
+                    const uint4    xa = lds_v4(xm + (uint32_t) (((((2 * bs) * NSB + j) << 4)) ^ (h << 6)));
+                    const uint4    xb = lds_v4(xm + (uint32_t) (((((2 * bs + 1) * NSB + j) << 4)) ^ (h << 6)));
                     int            s0 = 0, s1 = 0;
                     if (b & 1) {
                         s0 = __dp4a((int) w[wb + 9], (int) xa.x, s0);
