@@ -476,9 +476,21 @@ __device__ bool stage_activations_t(const StepArgs & a, const Smem & s, int K, i
         const int   i0    = (valid ? b : 0) * kQK + eb * E;
         const float sc    = scale[m < M_T ? m : 0];
         float       v[E];
+        // 128-bit loads (both buffers and i0 are 16-byte aligned): a lane's
+        // values are 16 bytes apart from its neighbour's, and scalar loads at
+        // that stride would conflict four ways
+#pragma unroll
+        for (int q = 0; q < E / 4; ++q) {
+            const float4 h4 = *reinterpret_cast<const float4 *>(hsrc + (size_t) m * K + i0 + 4 * q);
+            const float4 n4 = *reinterpret_cast<const float4 *>(norm + i0 + 4 * q);
+            v[4 * q]        = __fmul_rn(__fmul_rn(h4.x, sc), n4.x);
+            v[4 * q + 1]    = __fmul_rn(__fmul_rn(h4.y, sc), n4.y);
+            v[4 * q + 2]    = __fmul_rn(__fmul_rn(h4.z, sc), n4.z);
+            v[4 * q + 3]    = __fmul_rn(__fmul_rn(h4.w, sc), n4.w);
+        }
 #pragma unroll
         for (int k = 0; k < E; ++k) {
-            v[k] = valid ? __fmul_rn(__fmul_rn(hsrc[(size_t) m * K + i0 + k], sc), norm[i0 + k]) : 0.0f;
+            v[k] = valid ? v[k] : 0.0f;
         }
         const float       am = block_amax<LPB, E>(v, eb);
         const QuantParams qp = quant_params<MODE>(am);
