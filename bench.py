@@ -135,18 +135,17 @@ def physical_gpu_index(local_rank):
     return local_rank
 
 
-def cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s, max_tokens, m=1):
-    """Oracle decode chain (ggml-cpu's Q8_0 arithmetic restated in C, OpenMP over rows) on the host cores."""
-    from synthesize_cpp_b200.workloads import stream_inputs
-
-    x, ids = stream_inputs(m, shape.hidden, shape.table_rows)
+def cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s, max_steps, x, ids):
+    """Oracle decode chain (ggml-cpu's Q8_0 arithmetic restated in C, OpenMP over rows) on the host cores:
+    steps until budget_s runs out (at most max_steps); returns (tokens/s, steps, seconds)."""
+    m = x.shape[0]
     kw = dict(hidden=shape.hidden, n_head=shape.n_head, n_kv=shape.n_kv, head_dim=shape.head_dim,
               inter=shape.inter, eps=shape.eps, threads=threads)
     O.decoder_chain(mats, norms, table, ids, x, **kw)  # warm-up
     t0 = time.perf_counter()
     O.decoder_chain(mats, norms, table, ids, x, **kw)
     one = time.perf_counter() - t0
-    n = max(1, min(max_tokens, int(budget_s / max(one, 1e-6))))
+    n = max(1, min(max_steps, int(budget_s / max(one, 1e-6))))
     t0 = time.perf_counter()
     for _ in range(n):
         O.decoder_chain(mats, norms, table, ids, x, **kw)
@@ -162,6 +161,124 @@ def host_threads() -> int:
         return len(os.sched_getaffinity(0))
     except (AttributeError, OSError):
         return os.cpu_count() or 1
+
+
+def cpu_info() -> dict:
+    """The host CPU model and core counts (nproc = the cores this process may use)."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "nproc": host_threads(), "logical_cpus": os.cpu_count()}
+
+
+def default_threads(n: int) -> int:
+    """The reference's default synthesis thread count for n available cores, min(n/2, n-1) and at least 1
+    (src/cpu-parallelism.cpp:93-99)."""
+    return 1 if n <= 2 else min(n // 2, n - 1)
+
+
+def load_shapes():
+    """The workload geometry (synthesize.cpp_b200/shapes.py), loaded by file path: pure arithmetic, so the CPU
+    reference arm states the same workload without importing the product package or any native library."""
+    import importlib.util
+
+    name = "b200q8_workload_shapes"
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, "synthesize.cpp_b200", "shapes.py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+    return sys.modules[name]
+
+
+def talker_shape(args):
+    S = load_shapes()
+    return S.TALKER_17B if args.workload == "talker-1.7b" else S.TALKER_06B
+
+
+def talker_sizes(args, world: int, rank: int):
+    """(first stream, [batch sizes]) this rank runs per step."""
+    if args.workload == "dp-sweep":
+        # BASELINE config 5: 512 independent streams split evenly over the ranks, run as M=64 batches
+        return load_shapes().partition_streams(512, world, rank, 64)
+    return rank * args.batch, [args.batch]
+
+
+def talker_config(args, shape, sizes, world: int) -> dict:
+    """The workload's config dict; both arms print exactly this."""
+    dp = args.workload == "dp-sweep"
+    if dp:
+        workload = (f"{shape.name} decode, BASELINE config 5: 512 streams over {world} GPU(s), "
+                    f"batches {sizes} per GPU per step")
+    else:
+        cfg = "4" if args.workload == "talker-1.7b" else ("2" if args.batch == 1 else "3")
+        workload = f"{shape.name} decode step (BASELINE config {cfg}), M={args.batch} per GPU"
+    return {"workload": workload, "layers": shape.n_layers, "batch_per_gpu": sum(sizes),
+            "global_batch": 512 if dp else world * args.batch,
+            "parallelism": f"replicas x{world} (no collectives)",
+            "l2": "inputs larger than L2: weights streamed every step exceed 126 MB",
+            "weight_bytes_per_step": shape.weight_bytes() * len(sizes),
+            "algorithmic_bytes_per_step": sum(shape.step_bytes(m) for m in sizes),
+            "int8_ops_per_step": sum(shape.step_flops(m) for m in sizes)}
+
+
+def config3_outliers(args) -> bool:
+    """BASELINE config 3 (the 0.6B talker at M > 1) scales 1 % of the activation entries by 20."""
+    return args.workload == "talker" and args.batch > 1
+
+
+def oracle_stream_inputs(O, m: int, hidden: int, table_rows: int, first_stream: int = 0, outliers: bool = False):
+    """The streams' N(0,1) activations and token ids, drawn by the oracle's restatement of the reference's
+    stream (the same values the product's host library draws), with config 3's outliers when asked."""
+    import numpy as np
+
+    S = load_shapes()
+    x = np.stack(O.normal_many([S.STREAM_SEED + first_stream + s for s in range(m)], [1.0] * m,
+                               [hidden] * m)).astype(np.float32)
+    if outliers:
+        x.reshape(-1)[S.outlier_positions(m, hidden, first_stream)] *= np.float32(S.OUTLIER_SCALE)
+    return x, np.asarray(S.stream_ids(m, table_rows, first_stream), dtype=np.int32)
+
+
+def oracle_model(O, shape, seed: int = 1000, threads: int = 0):
+    """The talker model on the host, drawn and packed by the oracle: seeds as the device workload uses them
+    (base + 16*layer + index), 0.02*N(0,1) weights packed by quantize_row_q8_0_ref, 1 + 0.1*N(0,1) norms."""
+    import numpy as np
+
+    mats, norms = [], []
+    shp = shape.matrices()
+    for l in range(shape.n_layers):
+        seeds = [seed + 16 * l + j for j in range(7)] + [seed + 16 * l + 8, seed + 16 * l + 9]
+        vals = O.normal_many(seeds, [0.02] * 7 + [0.1, 0.1], [n * k for n, k in shp] + [shape.hidden] * 2, threads)
+        for j, (n, k) in enumerate(shp):
+            mats.append(O.quantize_rows_mt(vals[j].reshape(n, k), threads=threads))
+        norms += [1.0 + vals[7], 1.0 + vals[8]]
+    tab = O.normal_many([seed - 1], [0.02], [shape.table_rows * shape.hidden])[0]
+    table = O.quantize_rows_mt(tab.reshape(shape.table_rows, shape.hidden), threads=threads)
+    return mats, np.stack(norms).astype(np.float32), table
+
+
+def cpu_chain_baseline(O, mats, norms, table, shape, m, budget_s, max_steps, first_stream=0, outliers=False):
+    """The oracle chain at the reference's default thread count and at every host core, each on a bounded
+    sample; returns the cpu_baseline dict (value = all cores)."""
+    x, ids = oracle_stream_inputs(O, m, shape.hidden, shape.table_rows, first_stream, outliers)
+    info = cpu_info()
+    runs = {}
+    for key, threads in (("default", default_threads(info["nproc"])), ("all", info["nproc"])):
+        tps, n, dt = cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s, max_steps, x, ids)
+        runs[key] = {"threads": threads, "value": tps, "steps": n, "seconds": round(dt, 2)}
+    return {"value": runs["all"]["value"], "unit": "tok/s", "cores": runs["all"]["threads"], "kind": "port",
+            "sample": (f"{runs['all']['steps']} steps of the full {shape.n_layers}-layer step at M={m} "
+                       f"({runs['all']['seconds']} s; oracle C port of ggml-cpu Q8_0, OpenMP {info['nproc']} threads); "
+                       f"reference default min(n/2, n-1) = {runs['default']['threads']} threads: "
+                       f"{runs['default']['value']:.1f} tok/s over {runs['default']['steps']} steps"),
+            **info, "threads": runs}
 
 
 def frame_positions(i: int, prompt: int, window: int) -> int:
@@ -385,41 +502,26 @@ def run_frame(args, rank, local_rank):
 
 
 def run_reference(args, rank):
-    """The reference's CPU path for the same step: rank 0 only, all host threads."""
+    """The reference's CPU path for the same step, rank 0 only: the oracle's restatement of ggml-cpu's Q8_0
+    arithmetic (ggml itself is absent from the reference tree) on every host core.  Nothing from the product
+    package or its native libraries is imported: the weights are drawn and packed by the oracle, and the
+    workload geometry comes from the pure-arithmetic shapes module."""
     if rank != 0:
         return
     if args.workload == "frame":
         run_reference_frame(args, rank)
         return
-    import numpy as np
-    import torch  # noqa: F401  (keeps the same import cost profile as our arm)
-
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
-    import __graft_entry__ as g
-
-    g.load_package()
-    from synthesize_cpp_b200 import host
-    from synthesize_cpp_b200.q8 import row_bytes  # noqa: F401
-    from synthesize_cpp_b200.workloads import TALKER_06B, TALKER_17B
-
-    shape = TALKER_17B if args.workload == "talker-1.7b" else TALKER_06B
-    # Pack on the CPU with the oracle's ref quantizer (what synthesize-quantize does).
-    mats, norms = [], []
-    for l in range(shape.n_layers):
-        for j, (n, k) in enumerate(shape.matrices()):
-            mats.append(O.quantize_rows(host.normal(1000 + 16 * l + j, n * k, 0.02).reshape(n, k)))
-        norms += [1.0 + host.normal(1000 + 16 * l + 8, shape.hidden, 0.1),
-                  1.0 + host.normal(1000 + 16 * l + 9, shape.hidden, 0.1)]
-    norms = np.stack(norms).astype(np.float32)
-    table = O.quantize_rows(host.normal(999, shape.table_rows * shape.hidden, 0.02).reshape(shape.table_rows,
-                                                                                             shape.hidden))
-    threads = host_threads()
-    from synthesize_cpp_b200.workloads import stream_inputs
-
-    m = 64 if args.workload == "dp-sweep" else args.batch
-    x, ids = stream_inputs(m, shape.hidden, shape.table_rows)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    shape = talker_shape(args)
+    first, sizes = talker_sizes(args, world, 0)
+    m = sizes[0]
+    info = cpu_info()
+    threads = info["nproc"]
+    mats, norms, table = oracle_model(O, shape, threads=threads)
+    x, ids = oracle_stream_inputs(O, m, shape.hidden, shape.table_rows, first, config3_outliers(args))
     kw = dict(hidden=shape.hidden, n_head=shape.n_head, n_kv=shape.n_kv, head_dim=shape.head_dim,
               inter=shape.inter, eps=shape.eps, threads=threads)
     for _ in range(max(1, min(args.warmup, 3))):
@@ -434,16 +536,23 @@ def run_reference(args, rank):
     for _ in range(n):
         O.decoder_chain(mats, norms, table, ids, x, **kw)
     dt = time.perf_counter() - t0
+    # the per-step rate of this sample: one batch of m streams (a dp-sweep rank runs len(sizes) such batches)
     value = n * m / dt
+    d_threads = default_threads(threads)
+    tps_d, n_d, dt_d = cpu_chain_tokens_per_s(O, mats, norms, table, shape, d_threads, 20.0, args.steps, x, ids)
     sample = (f"{n} of {args.steps} steps of the full {shape.n_layers}-layer step at M={m} "
-              f"(oracle C port of ggml-cpu Q8_0 MUL_MAT, OpenMP {threads} threads)")
+              f"(oracle C port of ggml-cpu Q8_0 MUL_MAT, OpenMP {threads} threads); reference default "
+              f"min(n/2, n-1) = {d_threads} threads: {tps_d:.1f} tok/s over {n_d} steps")
     line = {
         "impl": "reference", "metric": "talker-shaped Q8_0 decode throughput", "value": value, "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / n,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32, f32 scale",
-        "data": "synthetic (seeded N(0,1) stream of src/random-stream.cpp)",
-        "config": {"workload": f"{shape.name} decode step, M={m}", "layers": shape.n_layers, "batch": m},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "higher_is_better": True, "scaling": "strong" if args.workload == "dp-sweep" else "weak",
+        "vs_baseline": None, "dtype": "int8xint8->int32, f32 scale (Q8_0 x F32)",
+        "data": "synthetic (seeded N(0,1) stream of src/random-stream.cpp; weights 0.02*N, packed by the oracle)",
+        "config": talker_config(args, shape, sizes, world),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample, **info,
+                         "threads": {"default": {"threads": d_threads, "value": tps_d, "steps": n_d},
+                                     "all": {"threads": threads, "value": value, "steps": n}}},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -684,7 +793,7 @@ def main():
     g.load_package()
     from synthesize_cpp_b200 import chain as chain_mod
     from synthesize_cpp_b200 import q8
-    from synthesize_cpp_b200.workloads import TALKER_06B, TALKER_17B, build_model, host_copy, stream_inputs
+    from synthesize_cpp_b200.workloads import build_model, host_copy, stream_inputs
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -701,14 +810,9 @@ def main():
     def max_over_ranks(v):
         return dpu.max_over_ranks(v, dev)
 
-    shape = TALKER_17B if args.workload == "talker-1.7b" else TALKER_06B
+    shape = talker_shape(args)
     dp = args.workload == "dp-sweep"
-    if dp:
-        # 512 independent streams split evenly over the ranks, run as M=64 batches
-        first, sizes = dpu.partition_streams(512, world, rank, 64)
-    else:
-        first = rank * args.batch
-        sizes = [args.batch]
+    first, sizes = talker_sizes(args, world, rank)
     m_max = max(sizes)
     dm = build_model(shape, dev)
     os.environ["B200Q8_CHAIN_PER_OP"] = "1" if args.chain == "per-op" else "0"
@@ -717,7 +821,8 @@ def main():
     batches = []
     off = first
     for m in sizes:
-        x_np, ids_np = stream_inputs(m, shape.hidden, shape.table_rows, first_stream=off)
+        x_np, ids_np = stream_inputs(m, shape.hidden, shape.table_rows, first_stream=off,
+                                     outliers=config3_outliers(args))
         off += m
         x_host = torch.from_numpy(x_np).pin_memory()
         ids_host = torch.from_numpy(ids_np).pin_memory()
@@ -757,7 +862,16 @@ def main():
     t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     clocks = sampler.stop()
 
-    # ---- end to end through the C ABI with host buffers
+    # ---- end to end through the C ABI with host buffers, host clock: every step copies its inputs in from
+    # pinned host memory, runs, copies the result out and waits for it before the next step is issued (a
+    # synthesis loop reads each step's output before it can form the next input, model.cpp:1402-1414)
+    barrier_sync()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step_e2e()
+        stream.synchronize()
+    t_e2e = max_over_ranks(time.perf_counter() - t0)
+    # the same copies enqueued back to back without the per-step wait (device clock)
     barrier_sync()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
@@ -765,16 +879,38 @@ def main():
         step_e2e()
     f1.record(stream)
     barrier_sync()
-    t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
+    t_e2e_async = max_over_ranks(f0.elapsed_time(f1) / 1e3)
     if q8.device_status(local_rank) != 0:
         raise RuntimeError("device status set during the timed region")
+
+    # ---- parity: one step of this rank's first batch against the oracle's chain on the same inputs and weights
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+
+    import oracle as O
+
+    x_host, ids_host, h_host, x_dev, ids_dev, h_dev = batches[0]
+    h_dev.zero_()
+    ch.run(ids_dev, x_dev, h_dev)
+    got = h_dev.cpu().numpy()
+    mats, norms, table = host_copy(dm)
+    ref = O.decoder_chain(mats, norms, table, ids_host.numpy(), x_host.numpy(), hidden=shape.hidden,
+                          n_head=shape.n_head, n_kv=shape.n_kv, head_dim=shape.head_dim, inter=shape.inter,
+                          eps=shape.eps, threads=max(1, host_threads() // world))
+    rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+    cos = float(np.sum(got.astype(np.float64) * ref) / (np.linalg.norm(got) * np.linalg.norm(ref)))
+    # an ulp of fp32 summation order before a quantization can move one activation code by one step; the
+    # parity tests bound the whole step the same way
+    if not (rel < 2e-3 and cos > 0.99999):
+        raise RuntimeError(f"step output differs from the oracle: rel L2 {rel:.3e}, cosine {cos:.8f}")
 
     tokens = (512 if dp else world * args.batch) * args.steps
     value = tokens / t_dev
     step_s = t_dev / args.steps
     peaks, peak_kind = measured_peaks()
-    step_bytes = sum(shape.step_bytes(m) for m in sizes)
-    step_flops = sum(shape.step_flops(m) for m in sizes)
+    config = talker_config(args, shape, sizes, world)
+    step_bytes = config["algorithmic_bytes_per_step"]
+    step_flops = config["int8_ops_per_step"]
     achieved = step_bytes / step_s / 1e9
     persistent = args.chain == "auto" and m_max <= 2
     per_batch = lambda m: 1 if persistent else (2 + 8 * shape.n_layers if m > 8 else 1 + 4 * shape.n_layers)
@@ -787,43 +923,29 @@ def main():
         kernel_name = "gemv_q8_0_kernel (every launch of the step; 1 + 4*layers launches)"
     h2d = sum(m * shape.hidden * 4 + m * 4 for m in sizes)
     d2h = sum(m * shape.hidden * 4 for m in sizes)
-    if dp:
-        workload = (f"{shape.name} decode, BASELINE config 5: 512 streams over {world} GPU(s), "
-                    f"batches {sizes} per GPU per step")
-    else:
-        workload = f"{shape.name} decode step (BASELINE config {'2' if args.batch == 1 else '3'}), M={args.batch} per GPU"
     line = {
         "metric": "talker-shaped Q8_0 decode throughput", "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * step_s, "higher_is_better": True,
         "scaling": "strong" if dp else "weak", "vs_baseline": None, "dtype": "int8xint8->int32, f32 scale (Q8_0 x F32)",
         "data": "synthetic (seeded N(0,1) stream of src/random-stream.cpp; weights 0.02*N, packed on device)",
-        "config": {"workload": workload, "layers": shape.n_layers, "batch_per_gpu": sum(sizes),
-                   "global_batch": 512 if dp else world * args.batch,
-                   "parallelism": f"replicas x{world} (no collectives)",
-                   "l2": "inputs larger than L2: weights streamed every step exceed 126 MB",
-                   "weight_bytes_per_step": shape.weight_bytes() * len(sizes), "algorithmic_bytes_per_step": step_bytes,
-                   "int8_ops_per_step": step_flops},
+        "config": config,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic(f"{shape.name}-m{m_max}"),
                      "kernel": kernel_name,
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                      "int8_tops": step_flops / step_s / 1e12},
-        "e2e": {"value": tokens / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "e2e": {"value": tokens / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "clock": "host perf_counter over K steps, each copy-in + step + copy-out waited for before the next"},
+        "e2e_async": {"value": tokens / t_e2e_async, "unit": "tok/s",
+                      "clock": "CUDA events around K copy-in + step + copy-out sequences enqueued back to back"},
+        "parity": {"checked": f"rank {rank}, batch of {sizes[0]} streams, one step against oracle.decoder_chain",
+                   "rel_l2": rel, "cosine": cos, "bound": "rel L2 < 2e-3 and cosine > 0.99999"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import oracle as O
-
-        mats, norms, table = host_copy(dm)
-        threads = host_threads()
-        mcpu = min(m_max, 64)
-        tps, n, dt = cpu_chain_tokens_per_s(O, mats, norms, table, shape, threads, budget_s=12.0, max_tokens=400,
-                                            m=mcpu)
-        line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
-                                "sample": f"{n} steps of the full {shape.n_layers}-layer step at M={mcpu} "
-                                          f"({dt:.1f} s; oracle C port of ggml-cpu Q8_0, OpenMP)"}
+        line["cpu_baseline"] = cpu_chain_baseline(O, mats, norms, table, shape, min(m_max, 64), budget_s=8.0,
+                                                  max_steps=400, first_stream=first, outliers=config3_outliers(args))
     ch.close()
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -170,14 +170,19 @@ b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_ro
  * point of the call -- a ggml backend computing a graph whose buffers were all
  * placed before the graph ran, a real-time streaming callback that must not
  * block on cudaMalloc's device-wide synchronisation.  No counterpart in the reference (its CPU path allocates nothing
- * on the device).  It allocates nothing: the quantized activations go to a
- * fixed 1 MiB array in the library's own device memory, held by every GPU
- * that loads the library until the process exits.  Requires
- * M * (K/32) * 34 <= 1048576 bytes (else B200Q8_ERR_INVALID_ARG).  Every call
- * on a device shares that array, so calls whose kernels overlap on the GPU
- * race; order them on one stream.  The first call on each device looks up the
- * array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture.  Results as b200q8_mul_mat. */
+ * on the device).  It allocates nothing: its scratch (quantized or staged
+ * activations) is a fixed 1 MiB array in the library's own device memory,
+ * held by every GPU that loads the library until the process exits.  Requires
+ * M * (K/32) * 34 <= 1048576 bytes (else B200Q8_ERR_INVALID_ARG).  It runs the
+ * path b200q8_mul_mat runs with a workspace of the array's size (the
+ * tensor-core GEMM when its records fit, else the streaming GEMV, which needs
+ * no scratch, else the general kernel).  Every call on a device shares that
+ * array, so calls whose kernels overlap on the GPU race; order them on one
+ * stream.  The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  Calls on a stream that is not capturing look it
+ * up again, so a device reset is picked up by the next such call.  Results as
+ * b200q8_mul_mat. */
 b200q8_status_t b200q8_mul_mat_noalloc(const void * w, int64_t K, int64_t N, size_t w_row_bytes, const float * x,
                                        int64_t M, size_t x_col_stride, float * y, size_t y_col_stride, int32_t mode,
                                        b200q8_stream_t stream);

@@ -43,11 +43,28 @@ _lib = None
 _ref = None
 
 
-def build(reference_root: str | None = None) -> None:
-    """Compile the oracle (and, when the reference tree exists, oracle/_ref)."""
+def reference_root() -> str | None:
+    """Where the reference tree is, if anywhere: $SYNTH_REFERENCE, else the "reference_path" that the
+    repository's BASELINE.json records.  None when neither names an existing tree."""
+    cands = [os.environ.get("SYNTH_REFERENCE")]
+    try:
+        import json
+
+        with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+            cands.append(json.load(f).get("reference_path"))
+    except (OSError, ValueError):
+        pass
+    for c in cands:
+        if c and os.path.isdir(os.path.join(c, "src")):
+            return c
+    return None
+
+
+def build(reference: str | None = None) -> None:
+    """Compile the oracle (and, when a reference tree is found, oracle/_ref)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    ref = reference_root or "/root/reference"
-    if os.path.isdir(os.path.join(ref, "src")):
+    ref = reference or reference_root()
+    if ref is not None:
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
 
 
@@ -77,6 +94,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_normal_fill.argtypes = [ctypes.c_uint64, c_void_p, c_size_t]
         L.oracle_uniform_fill.argtypes = [ctypes.c_uint64, c_void_p, c_size_t]
         L.oracle_normal_fill_scaled.argtypes = [ctypes.c_uint64, ctypes.c_float, c_void_p, c_size_t]
+        L.oracle_normal_fill_scaled_many.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int]
+        L.oracle_quantize_rows_mt.argtypes = [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int]
         L.oracle_default_synthesis_threads.argtypes = [c_int]
         L.oracle_default_synthesis_threads.restype = c_int
         L.oracle_max_threads.restype = c_int
@@ -127,6 +146,16 @@ def quantize_rows(x: np.ndarray, mode: int = QUANT_REF) -> np.ndarray:
     xr = x.reshape(rows, k)
     for r in range(rows):
         L.oracle_quantize_row_q8_0(_ptr(xr[r]), _ptr(out[r]), k, mode)
+    return out
+
+
+def quantize_rows_mt(x: np.ndarray, mode: int = QUANT_REF, threads: int = 0) -> np.ndarray:
+    """quantize_rows on OpenMP threads (bytes identical; for building large fixtures)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    k = x.shape[-1]
+    rows = x.size // k
+    out = np.empty((rows, row_bytes(k)), dtype=np.uint8)
+    lib().oracle_quantize_rows_mt(_ptr(x), _ptr(out), rows, k, mode, threads)
     return out
 
 
@@ -188,6 +217,18 @@ def normal(seed: int, count: int, scale: float | None = None) -> np.ndarray:
     else:
         lib().oracle_normal_fill_scaled(seed, scale, _ptr(out), count)
     return out
+
+
+def normal_many(seeds, scales, counts, threads: int = 0) -> list:
+    """[normal(seeds[j], counts[j], scales[j]) for j] filled on OpenMP threads (same values)."""
+    n = len(seeds)
+    outs = [np.empty(c, dtype=np.float32) for c in counts]
+    s = (ctypes.c_uint64 * n)(*seeds)
+    f = (ctypes.c_float * n)(*scales)
+    p = (ctypes.c_void_p * n)(*[_ptr(o) for o in outs])
+    c = (ctypes.c_size_t * n)(*counts)
+    lib().oracle_normal_fill_scaled_many(n, s, f, p, c, threads)
+    return outs
 
 
 def uniform(seed: int, count: int) -> np.ndarray:

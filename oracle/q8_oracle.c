@@ -302,6 +302,29 @@ void oracle_normal_fill_scaled(uint64_t seed, float scale, float * out, size_t c
     }
 }
 
+/* Fills n independent tensors, tensor j from its own stream seeds[j] times
+ * scales[j]; tensors are spread over OpenMP threads (each stream is still
+ * drawn in order, so the values equal oracle_normal_fill_scaled's). */
+void oracle_normal_fill_scaled_many(int n, const uint64_t * seeds, const float * scales, float * const * outs,
+                                    const size_t * counts, int threads) {
+    const int nt = threads > 0 ? threads : omp_get_max_threads();
+#pragma omp parallel for num_threads(nt) schedule(dynamic, 1)
+    for (int j = 0; j < n; ++j) {
+        oracle_normal_fill_scaled(seeds[j], scales[j], outs[j], counts[j]);
+    }
+}
+
+/* oracle_quantize_row_q8_0 over rows rows of k values (dense), rows spread
+ * over OpenMP threads; each row's bytes are independent of the split. */
+void oracle_quantize_rows_mt(const float * x, void * dst, int64_t rows, int64_t k, int mode, int threads) {
+    const size_t row_size = (size_t) (k / ORACLE_QK8_0) * ORACLE_BLOCK_BYTES;
+    const int    nt       = threads > 0 ? threads : omp_get_max_threads();
+#pragma omp parallel for num_threads(nt) schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        oracle_quantize_row_q8_0(x + r * k, (uint8_t *) dst + (size_t) r * row_size, k, mode);
+    }
+}
+
 /* ------------------------------------------------------------ threads ---- */
 
 int oracle_default_synthesis_threads(int available) {

@@ -80,6 +80,12 @@ void oracle_uniform_fill(uint64_t seed, float * out, size_t count);
 /* out[i] = scale * normal_i: the synthetic weight generator. */
 void oracle_normal_fill_scaled(uint64_t seed, float scale, float * out, size_t count);
 
+/* Test-fixture helpers: many seeded tensors, and many packed rows, on OpenMP
+ * threads; the values are those of the single-threaded routines above. */
+void oracle_normal_fill_scaled_many(int n, const uint64_t * seeds, const float * scales, float * const * outs,
+                                    const size_t * counts, int threads);
+void oracle_quantize_rows_mt(const float * x, void * dst, int64_t rows, int64_t k, int mode, int threads);
+
 /* min(n/2, n-1) threads for n available (1 when n <= 2):
  * src/cpu-parallelism.cpp:93-99. */
 int oracle_default_synthesis_threads(int available);

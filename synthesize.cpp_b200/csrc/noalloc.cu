@@ -13,18 +13,26 @@
 // The array, its limits and its sharing rules:
 //  * kNoAllocScratchBytes (1 MiB) per device, a file-scope __device__ array
 //    that every GPU which loads this library holds until the process exits;
-//  * a call needs M * (K/32) * 34 bytes of it and is rejected with
-//    B200Q8_ERR_INVALID_ARG when that is more than the maximum;
+//  * a call is accepted when M * (K/32) * 34 bytes (its activations in Q8_0)
+//    fit in the array, and rejected with B200Q8_ERR_INVALID_ARG otherwise;
+//  * it runs the path b200q8_mul_mat would run with a workspace of the
+//    array's size: the tensor-core GEMM when the shape suits it and its
+//    staged activation records fit in the array; else the streaming GEMV,
+//    which needs no scratch at all; else the general kernel on activations
+//    quantized into the array;
 //  * all calls on a device share the one array and it keeps whatever the last
-//    call left in it.  Nothing in it has to start at zero: every byte the
-//    GEMV reads is written first by the same call's quantize kernel.  Two
-//    calls whose kernels overlap on the GPU (different streams, no ordering
-//    between them) race on the array and may corrupt each other's results;
-//    order them on one stream or with events;
+//    call left in it.  Nothing in it has to start at zero: every byte a
+//    kernel reads from it is written first by the same call.  Two calls whose
+//    kernels overlap on the GPU (different streams, no ordering between them)
+//    race on the array and may corrupt each other's results; order them on
+//    one stream or with events;
 //  * the array's name is only a host-side stand-in in host code, so its
-//    device address is looked up with cudaGetSymbolAddress -- once per
-//    device, with that device current, on the first call made on it.  Make
-//    that first call on each device before any stream capture begins.
+//    device address is looked up with cudaGetSymbolAddress, with the device
+//    current.  The first call made on a device does that lookup; make it
+//    before any stream capture begins.  Later calls on a stream that is not
+//    capturing look the address up again, so a device reset (which reloads
+//    the module and may move the array) is picked up by the next such call;
+//    calls during a capture use the address found last.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -45,8 +53,9 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 void *     g_noalloc_ptr[kNoAllocMaxDevices] = {};
 std::mutex g_noalloc_mu;
 
-// Device address of g_noalloc_scratch on the current device.
-b200q8_status_t noalloc_scratch(void ** out) {
+// Device address of g_noalloc_scratch on the current device.  refresh: look
+// it up again even when one is cached (the stream is not capturing).
+b200q8_status_t noalloc_scratch(void ** out, bool refresh) {
     int         dev = -1;
     cudaError_t e   = cudaGetDevice(&dev);
     if (e != cudaSuccess) {
@@ -57,7 +66,7 @@ b200q8_status_t noalloc_scratch(void ** out) {
                          kNoAllocMaxDevices);
     }
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
+    if (g_noalloc_ptr[dev] == nullptr || refresh) {
         void * p = nullptr;
         e        = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || p == nullptr) {
@@ -68,6 +77,18 @@ b200q8_status_t noalloc_scratch(void ** out) {
     }
     *out = g_noalloc_ptr[dev];
     return B200Q8_OK;
+}
+
+// True when `s` is known not to be capturing.  A query that fails (the legacy
+// stream while another stream captures in global mode answers with an error)
+// counts as capturing, so the cached address is used.
+bool stream_not_capturing(cudaStream_t s) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
+        (void) cudaGetLastError();
+        return false;
+    }
+    return cs == cudaStreamCaptureStatusNone;
 }
 
 }  // namespace
@@ -101,18 +122,51 @@ extern "C" b200q8_status_t b200q8_mul_mat_noalloc(const void * w, int64_t K, int
         (M > 1 && (x_col_stride < (size_t) K * 4 || y_col_stride < (size_t) N * 4))) {
         return set_error(B200Q8_ERR_INVALID_ARG, "mul_mat_noalloc: bad pointer, alignment, row size or stride");
     }
+    cudaStream_t    s       = reinterpret_cast<cudaStream_t>(stream);
     void *          scratch = nullptr;
-    b200q8_status_t st      = noalloc_scratch(&scratch);
+    b200q8_status_t st      = noalloc_scratch(&scratch, stream_not_capturing(s));
     if (st != B200Q8_OK) {
         return st;
     }
-    cudaStream_t s  = reinterpret_cast<cudaStream_t>(stream);
-    const size_t xs = M > 1 ? x_col_stride : (size_t) K * 4;
-    const size_t ys = M > 1 ? y_col_stride : (size_t) N * 4;
-    cudaError_t  e  = launch_quantize(x, M, K, xs, scratch, row, mode, s, current_sm_count());
+    const int    sms = current_sm_count();
+    const size_t xs  = M > 1 ? x_col_stride / 4 : (size_t) K;
+    const size_t ys  = M > 1 ? y_col_stride / 4 : (size_t) N;
+    const auto * wb  = static_cast<const uint8_t *>(w);
+    // 1. the int8 tensor-core GEMM, its staged records in the array
+    if (N <= INT32_MAX && K <= INT32_MAX && gemm_supported(wb, w_row_bytes, K, N, M) &&
+        gemm_workspace_bytes(K, M) <= kNoAllocScratchBytes) {
+        cudaError_t e = launch_gemm(wb, w_row_bytes, K, N, x, xs, M, y, ys, mode, scratch, s, sms);
+        return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "mul_mat_noalloc: tensor-core GEMM launch");
+    }
+    // 2. the streaming GEMV, 8 tokens per launch, no scratch
+    GemvParams p = {};
+    p.w          = wb;
+    p.row_bytes  = w_row_bytes;
+    p.K          = (int) K;
+    p.N          = (int) N;
+    p.M          = (int) std::min<int64_t>(M, 8);
+    p.pro        = kProPlain;
+    p.x          = x;
+    p.x_stride   = xs;
+    p.y          = y;
+    p.y_stride   = ys;
+    p.mode       = mode;
+    if (N <= INT32_MAX && K <= INT32_MAX && gemv_supported(p)) {
+        for (int64_t m0 = 0; m0 < M; m0 += 8) {
+            p.M           = (int) std::min<int64_t>(M - m0, 8);
+            p.x           = x + m0 * xs;
+            p.y           = y + m0 * ys;
+            cudaError_t e = launch_gemv(p, s, sms, false);
+            if (e != cudaSuccess) {
+                return cuda_error(e, "mul_mat_noalloc: gemv launch");
+            }
+        }
+        return B200Q8_OK;
+    }
+    // 3. general shapes: activations quantized into the array, then the plain kernel
+    cudaError_t e = launch_quantize(x, M, K, xs * 4, scratch, row, mode, s, sms);
     if (e == cudaSuccess) {
-        e = launch_gemv_generic(static_cast<const uint8_t *>(w), w_row_bytes, K, N,
-                                static_cast<const uint8_t *>(scratch), M, y, ys, s);
+        e = launch_gemv_generic(wb, w_row_bytes, K, N, static_cast<const uint8_t *>(scratch), M, y, ys * 4, s);
     }
     return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "mul_mat_noalloc launch");
 }

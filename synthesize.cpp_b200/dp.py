@@ -13,16 +13,7 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
-
-def partition_streams(total: int, world: int, rank: int, batch: int) -> tuple[int, list[int]]:
-    """Rank `rank`'s contiguous share of `total` streams as batches of at most `batch`:
-    returns (first stream index, [batch sizes])."""
-    if world < 1 or not 0 <= rank < world or batch < 1 or total < 0:
-        raise ValueError("bad partition arguments")
-    base, rem = divmod(total, world)
-    mine = base + (1 if rank < rem else 0)
-    first = rank * base + min(rank, rem)
-    return first, [min(batch, mine - o) for o in range(0, mine, batch)]
+from .shapes import partition_streams  # noqa: F401  (re-exported: the stream split lives with the workload geometry)
 
 
 def init(backend: str, timeout_s: float = 300.0, device: torch.device | None = None) -> tuple[int, int]:

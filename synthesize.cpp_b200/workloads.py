@@ -15,52 +15,8 @@ import torch
 
 from . import host
 from .q8 import quantize_rows, row_bytes
-
-
-@dataclass
-class Shape:
-    name: str
-    n_layers: int
-    hidden: int
-    n_head: int
-    n_kv: int
-    head_dim: int
-    inter: int
-    table_rows: int = 3072
-    eps: float = 1e-6
-
-    @property
-    def q_dim(self) -> int:
-        return self.n_head * self.head_dim
-
-    @property
-    def kv_dim(self) -> int:
-        return self.n_kv * self.head_dim
-
-    def matrices(self):
-        """(rows N, K) of q,k,v,o,gate,up,down."""
-        H, Q, KV, I = self.hidden, self.q_dim, self.kv_dim, self.inter
-        return [(Q, H), (KV, H), (KV, H), (H, Q), (I, H), (I, H), (H, I)]
-
-    def weight_bytes(self) -> int:
-        return self.n_layers * sum(n * row_bytes(k) for n, k in self.matrices())
-
-    def weights(self) -> int:
-        return self.n_layers * sum(n * k for n, k in self.matrices())
-
-    def step_bytes(self, m: int) -> int:
-        """Algorithmic HBM bytes of one step for m tokens: every Q8_0 weight once, every MUL_MAT's F32 input and
-        output once, plus the GET_ROWS row read (34/32 B per value) and written (4 B per value)."""
-        act = sum((k + n) * 4 for n, k in self.matrices()) * self.n_layers * m
-        emb = (row_bytes(self.hidden) + 4 * self.hidden) * m
-        return self.weight_bytes() + act + emb
-
-    def step_flops(self, m: int) -> int:
-        return 2 * self.weights() * m
-
-
-TALKER_06B = Shape("qwen3-tts-0.6b-talker", 28, 1024, 16, 8, 128, 3072)
-TALKER_17B = Shape("qwen3-tts-1.7b-talker", 28, 2048, 16, 8, 128, 6144)
+from .shapes import (OUTLIER_SCALE, PREDICTOR_06B, STREAM_SEED, TALKER_06B, TALKER_17B, Shape,  # noqa: F401
+                     outlier_positions, stream_ids)
 
 
 @dataclass
@@ -106,10 +62,14 @@ def build_model(shape: Shape, device: torch.device, seed: int = 1000, threads: i
     return dm
 
 
-def stream_inputs(m: int, hidden: int, table_rows: int, first_stream: int = 0, seed: int = 5000):
-    """Per-stream N(0,1) activations (stream s from seed + s) and token ids."""
+def stream_inputs(m: int, hidden: int, table_rows: int, first_stream: int = 0, seed: int = STREAM_SEED,
+                  outliers: bool = False):
+    """Per-stream N(0,1) activations (stream s from seed + s) and token ids; with outliers, the 1 % of entries
+    shapes.outlier_positions names are scaled by 20."""
     x = np.stack([host.normal(seed + first_stream + s, hidden) for s in range(m)]).astype(np.float32)
-    ids = ((np.arange(m) + first_stream) * 7919 % table_rows).astype(np.int32)
+    if outliers:
+        x.reshape(-1)[outlier_positions(m, hidden, first_stream)] *= np.float32(OUTLIER_SCALE)
+    ids = np.asarray(stream_ids(m, table_rows, first_stream), dtype=np.int32)
     return x, ids
 
 
@@ -125,9 +85,6 @@ def host_copy(dm: DeviceModel):
 
 
 # ---------------------------------------------------------------- decode frame
-
-PREDICTOR_06B = Shape("qwen3-tts-0.6b-code-predictor", 5, 1024, 16, 8, 128, 3072, table_rows=2048)
-
 
 @dataclass
 class FrameShape:

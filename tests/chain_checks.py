@@ -1,0 +1,100 @@
+"""Shared checks of the talker-shaped decode step against the oracle (imported by the chain tests).
+
+check_layer: one decoder layer of the step, op by op, on the GPU's own inputs to each op (read back from the
+chain's per-layer buffers): norms, GQA expansion and residual adds bit-exact, every MUL_MAT within 1e-5 of its
+abs-sum bound, SwiGLU within a few ulp (expf on the device and in libm may differ by an ulp).  The op order is
+decoder_layer's (src/arch/qwen3-tts/operations.cpp:44-148) with the single cached position of the benchmark step.
+
+check_end_to_end: the whole step against the oracle's own chain, where those ulps can flip an occasional
+activation code, so the comparison is a relative L2 and cosine bound.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass
+class Dims:
+    hidden: int
+    n_head: int
+    n_kv: int
+    head_dim: int
+    inter: int
+    eps: float = 1e-6
+
+    @property
+    def q(self) -> int:
+        return self.n_head * self.head_dim
+
+    @property
+    def kv(self) -> int:
+        return self.n_kv * self.head_dim
+
+    def shapes(self):
+        H, Q, KV, I = self.hidden, self.q, self.kv, self.inter
+        return [(Q, H), (KV, H), (KV, H), (H, Q), (I, H), (I, H), (H, I)]
+
+    def kw(self) -> dict:
+        return dict(hidden=self.hidden, n_head=self.n_head, n_kv=self.n_kv, head_dim=self.head_dim,
+                    inter=self.inter, eps=self.eps)
+
+
+def rms_norm(x, w, eps):
+    ss = np.sum((x.astype(np.float32) * x.astype(np.float32)).astype(np.float64), axis=-1, keepdims=True)
+    mean = (ss / x.shape[-1]).astype(np.float32)
+    scale = (np.float32(1) / np.sqrt(mean + np.float32(eps))).astype(np.float32)
+    return ((x * scale).astype(np.float32) * w).astype(np.float32)
+
+
+def check_mm(O, wq, k, x, y, threads=0):
+    y_ref, bound = O.mul_mat(wq, k, x, threads=threads)
+    err = np.abs(y.astype(np.float64) - y_ref)
+    assert np.all(err <= 1e-5 * bound + 1e-30), (err / (1e-5 * bound + 1e-30)).max()
+
+
+def check_layer(O, ch, mats, norms, l, m, h, d: Dims, h_next=None):
+    """Checks layer l's ops given its input h [m, hidden]; returns the layer's output (the chain's buffer, or
+    h_next when given, e.g. the step's h_out for the last layer)."""
+    H, Q, KV, I = d.hidden, d.q, d.kv, d.inter
+    buf = lambda name: ch.buffer(l, name, m).cpu().numpy()
+    n1 = buf("n1")
+    assert np.array_equal(n1, rms_norm(h, norms[2 * l], d.eps)), f"layer {l}: input norm"
+    qkv = buf("qkv")
+    check_mm(O, np.concatenate(mats[7 * l: 7 * l + 3]), H, n1, qkv)
+    v = qkv[:, Q + KV:]
+    group = d.n_head // d.n_kv
+    exp_attn = np.concatenate([v[:, (hq // group) * d.head_dim:(hq // group + 1) * d.head_dim]
+                               for hq in range(d.n_head)], axis=1)
+    assert np.array_equal(buf("attn"), exp_attn), f"layer {l}: GQA expansion"
+    o = buf("o")
+    check_mm(O, mats[7 * l + 3], Q, exp_attn, o)
+    h1 = buf("h1")
+    assert np.array_equal(h1, (h + o).astype(np.float32)), f"layer {l}: attention residual"
+    n2 = buf("n2")
+    assert np.array_equal(n2, rms_norm(h1, norms[2 * l + 1], d.eps)), f"layer {l}: post-attention norm"
+    gu = buf("gu")
+    check_mm(O, np.concatenate(mats[7 * l + 4: 7 * l + 6]), H, n2, gu)
+    g, u = gu[:, :I].astype(np.float64), gu[:, I:].astype(np.float64)
+    s = buf("s")
+    s_exact = g / (1.0 + np.exp(-g)) * u
+    assert np.all(np.abs(s - s_exact) <= 4e-7 * np.abs(s_exact) + 1e-30), f"layer {l}: SwiGLU"
+    down = buf("down")
+    check_mm(O, mats[7 * l + 6], I, s, down)
+    out = h_next if h_next is not None else buf("h")
+    assert np.array_equal(out, (h1 + down).astype(np.float32)), f"layer {l}: FFN residual"
+    return out
+
+
+def check_end_to_end(O, mats, norms, table, ids, x_in, got, d: Dims, threads=0):
+    ref = O.decoder_chain(mats, norms, table, ids, x_in, threads=threads, **d.kw())
+    # An ulp of difference before a quantization can move one activation code
+    # by one step (about 1/127 of its block's amax); over a few hundred
+    # thousand quantized values per layer a handful of such flips is expected
+    # and shows up at the 1e-4 level in the residual stream.
+    rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert rel < 2e-3, rel
+    cos = float(np.sum(got.astype(np.float64) * ref) / (np.linalg.norm(got) * np.linalg.norm(ref)))
+    assert cos > 0.99999, cos
+    return rel, cos

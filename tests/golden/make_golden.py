@@ -71,7 +71,8 @@ def edge_rows() -> dict[str, np.ndarray]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SYNTH_REFERENCE", ""),
+                    help="reference tree (default: $SYNTH_REFERENCE; the RNG pin is skipped without one)")
     args = ap.parse_args()
 
     # ---- packing fixtures (gguf-py is the oracle's pin)
@@ -95,7 +96,7 @@ def main() -> None:
         json.dump(pack, f, indent=1)
 
     # ---- seeded config-1 digests
-    if os.path.isdir(os.path.join(args.reference, "src")):
+    if args.reference and os.path.isdir(os.path.join(args.reference, "src")):
         O.build(args.reference)
     ref = O.ref_lib()
 
