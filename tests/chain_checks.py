@@ -87,14 +87,58 @@ def check_layer(O, ch, mats, norms, l, m, h, d: Dims, h_next=None):
     return out
 
 
+def oracle_layer(O, mats, norms, l, h, d: Dims, threads=0):
+    """The oracle's decoder layer l on the input h [m, hidden] (the step input is h itself: a zero Q8_0 table row
+    adds exactly 0)."""
+    m = h.shape[0]
+    zero = np.zeros((1, d.hidden // 32 * 34), np.uint8)
+    return O.decoder_chain(mats[7 * l: 7 * l + 7], norms[2 * l: 2 * l + 2], zero, np.zeros(m, np.int32),
+                           np.ascontiguousarray(h, np.float32), threads=threads, **d.kw())
+
+
+def check_teacher_forced(O, ch, mats, norms, h0, got, d: Dims, threads=0, bound=2e-3, token_bound=1e-2):
+    """Every layer of the step against the oracle's layer on the GPU's own input to it (the chain's per-layer
+    buffers).  A layer may differ only by the activation-code flips that an ulp of fp32 summation order causes
+    now and then inside it, and a flip moves the codes after it: over the whole batch the layer is held to the
+    bound the short chains are held to (rel L2 < 2e-3), and each token to 1e-2 (one token in which a flip
+    cascaded through the layer's later quantizations measured 3.5e-3 at the 1.7B shapes).  Returns the worst
+    per-token relative L2."""
+    n_layers = len(mats) // 7
+    m = h0.shape[0]
+    h = h0
+    worst = 0.0
+    for l in range(n_layers):
+        out = got if l == n_layers - 1 else ch.buffer(l, "h", m).cpu().numpy()
+        ref = oracle_layer(O, mats, norms, l, h, d, threads)
+        rel_all = np.linalg.norm(out - ref) / np.linalg.norm(ref)
+        rel = np.linalg.norm(out - ref, axis=1) / np.linalg.norm(ref, axis=1)
+        assert rel_all < bound and np.all(rel < token_bound), (l, rel_all, rel.max())
+        worst = max(worst, float(rel.max()))
+        h = out
+    return worst
+
+
+# Bounds of the step against the oracle's own chain over many layers.  The
+# quantized chain amplifies any difference that moves an activation code: in
+# the oracle alone, scaling 10 of the 1024 inputs of the 28-layer config-2
+# step by (1 + 1e-4) moves its output by 0.42 % (rel L2) after 2 layers and
+# 1.75 % after 28.  An ulp of fp32 summation order before a quantization flips
+# a code now and then (each layer is held to 2e-3 on its own inputs), and
+# over 28 layers those flips compound to about 1 % (measured 1.1 % on the
+# GPU).  Short chains keep the tight bound.
+def e2e_bounds(n_layers: int):
+    return (2e-3, 0.99999) if n_layers <= 4 else (5e-2, 0.998)
+
+
 def check_end_to_end(O, mats, norms, table, ids, x_in, got, d: Dims, threads=0):
     ref = O.decoder_chain(mats, norms, table, ids, x_in, threads=threads, **d.kw())
     # An ulp of difference before a quantization can move one activation code
     # by one step (about 1/127 of its block's amax); over a few hundred
     # thousand quantized values per layer a handful of such flips is expected
-    # and shows up at the 1e-4 level in the residual stream.
+    # and shows up at the 1e-4 level in the residual stream of a short chain.
+    rel_bound, cos_bound = e2e_bounds(len(mats) // 7)
     rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
-    assert rel < 2e-3, rel
+    assert rel < rel_bound, rel
     cos = float(np.sum(got.astype(np.float64) * ref) / (np.linalg.norm(got) * np.linalg.norm(ref)))
-    assert cos > 0.99999, cos
+    assert cos > cos_bound, cos
     return rel, cos
