@@ -353,6 +353,18 @@ typedef struct b200q8_frame_desc {
      * NULL / NULL when the widths agree. */
     const void *         input_projection;       /* Q8_0 with ne = [talker hidden, predictor hidden] */
     const float *        input_projection_bias;  /* F32 [predictor hidden]                          */
+    /* The talker's text side, for frames run from text token ids
+     * (build_text_projection, src/arch/qwen3-tts/talker.cpp:37-50):
+     *   text = W2 * Q(silu(W1 * Q(text_embedding[id]) + b1)) + b2
+     * (a Q8_0 GET_ROWS, then two Q8_0 MUL_MATs with F32 biases).  All NULL:
+     * frames take precomputed text rows only. */
+    const void *         text_embedding;         /* Q8_0 with ne = [text hidden, text_rows]             */
+    int64_t              text_rows;              /* the text vocabulary                                 */
+    int64_t              text_hidden;
+    const void *         text_fc1;               /* Q8_0 ne = [text hidden, text hidden] (linear_fc1)   */
+    const float *        text_fc1_bias;          /* F32 [text hidden]                                   */
+    const void *         text_fc2;               /* Q8_0 ne = [text hidden, talker hidden] (linear_fc2) */
+    const float *        text_fc2_bias;          /* F32 [talker hidden]                                 */
 } b200q8_frame_desc;
 
 typedef struct b200q8_frame b200q8_frame;
@@ -377,9 +389,24 @@ typedef struct b200q8_frame_args {
     int32_t *       codes;          /* [M][G] out                                               */
     float *         hidden;         /* [M][hidden] talker hidden: out (in when skip_talker); may be NULL unless skip_talker */
     float *         talker_logits;  /* [M][talker vocab]: same                                  */
+    /* [M] text token ids (device): the frame computes its text rows through
+     * the desc's text projection, and `text` is ignored.  NULL: `text`
+     * holds the rows.  An id outside [0, text_rows) gives a zero embedding
+     * row and records B200Q8_ERR_INVALID_ARG in b200q8_device_status. */
+    const int32_t * text_ids;
 } b200q8_frame_args;
 
 b200q8_status_t b200q8_frame_run(b200q8_frame * frame, const b200q8_frame_args * args, b200q8_stream_t stream);
+
+/* The talker's text rows for M text token ids through the frame's text
+ * projection (build_text_projection, src/arch/qwen3-tts/talker.cpp:37-50):
+ * out [M][talker hidden] = W2 * Q(silu(W1 * Q(text_embedding[id]) + b1)) + b2,
+ * the rows a frame run with text_ids adds to its input.  h1 (may be NULL)
+ * receives silu(W1 * Q(text_embedding[id]) + b1), [M][text hidden].  Device
+ * pointers, enqueued on `stream`; M <= the frame's max M.  The frame must have
+ * been built with a text projection. */
+b200q8_status_t b200q8_frame_text_rows(b200q8_frame * frame, const int32_t * text_ids, int64_t M, float * h1,
+                                       float * out, b200q8_stream_t stream);
 
 /* Forgets the chosen-code history of one slot (slot < 0: every slot), as a
  * new utterance starts with an empty history.  Enqueued on `stream`. */

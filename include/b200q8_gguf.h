@@ -64,7 +64,12 @@ b200q8_status_t b200q8_gguf_talker_chain(const b200q8_gguf * g, int32_t device, 
  *               its norm and lm_head.{g}; cache of code_group_count
  *               positions; max_m = max(8, 2 * max_m)) with its codec tables;
  *   *frame      (optional: frame may be NULL) b200q8_frame_create over both,
- *               with sampling.repetition_penalty (1 when the key is absent).
+ *               with sampling.repetition_penalty (1 when the key is absent)
+ *               and, when the package holds talker.model.text_embedding,
+ *               the talker's text projection (its Q8_0 embedding and
+ *               text_projection.linear_fc1 / linear_fc2 with F32 biases,
+ *               talker.text_hidden_size / text_vocab_size), so that frames
+ *               run from text token ids.
  * Hyperparameters follow weights.cpp:128-212 (the predictor's
  * intermediate_size falls back to the talker's; eps and rope_theta are the
  * talker's, model.cpp:315-322).  A predictor of another width than the

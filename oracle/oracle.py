@@ -109,6 +109,7 @@ def lib() -> ctypes.CDLL:
                                                 c_int64, c_int64, ctypes.c_float, ctypes.c_float, c_void_p, c_int64,
                                                 c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                                 c_void_p, c_void_p, c_void_p, c_int, c_int]
+        L.oracle_bias_silu_rows.argtypes = [c_void_p, c_void_p, c_int64, c_int64]
         L.oracle_rms_norm_rows.argtypes = [c_void_p, c_void_p, c_void_p, c_int64, c_int64, ctypes.c_float]
         _lib = L
     return _lib
@@ -335,15 +336,29 @@ def select_code(logits: np.ndarray, history: set | None = None, penalty: float =
     return best
 
 
+def text_projection(tp: dict, ids: np.ndarray, mode: int = QUANT_REF, threads: int = 0, want_h1: bool = False):
+    """The talker's text rows for text token ids (build_text_projection, src/arch/qwen3-tts/talker.cpp:37-50):
+    GET_ROWS from the Q8_0 text_embedding, fc1 (Q8_0 MUL_MAT) + bias, silu, fc2 + bias.  tp: dict(embedding, fc1,
+    fc1_bias, fc2, fc2_bias, hidden = the text width).  Returns the rows [M, talker hidden] (and, with want_h1,
+    silu(fc1 + b1) [M, text hidden] as well)."""
+    Th = tp["hidden"]
+    x = get_rows(tp["embedding"], Th, np.asarray(ids, np.int32))[0]
+    h1 = np.ascontiguousarray(mul_mat(tp["fc1"], Th, x, mode, threads, want_bound=False)[0])
+    lib().oracle_bias_silu_rows(_ptr(h1), _ptr(np.ascontiguousarray(tp["fc1_bias"], np.float32)), h1.shape[0], Th)
+    out = (mul_mat(tp["fc2"], Th, h1, mode, threads, want_bound=False)[0] + tp["fc2_bias"]).astype(np.float32)
+    return (out, h1) if want_h1 else out
+
+
 def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.ndarray | None, prev: np.ndarray | None,
           pos: np.ndarray, slots: np.ndarray, state: dict, *, replay: np.ndarray | None = None, penalty: float = 1.0,
           hidden_in: np.ndarray | None = None, logits_in: np.ndarray | None = None, mode: int = QUANT_REF,
-          threads: int = 0):
+          threads: int = 0, text_ids: np.ndarray | None = None):
     """One decode frame for M streams (src/arch/qwen3-tts/model.cpp:1310-1489 with request.sample == false or
     replay codes): talker step on sum(code embeddings) + text, greedy/replayed code 0, predictor prefill over
     [hidden, ttable[code 0]] at positions 0, 1 and G-2 single-position predictor steps.  talker / predictor: dicts
     with mats, norms, qkn, table (talker only), out_norm, heads (list of Q8_0 arrays), hidden, n_head, n_kv,
-    head_dim, inter, eps, theta, vocab; the predictor's may hold proj_w / proj_b (its input projection).  state: {"tk", "tv", "pk", "pv" caches, "history": {slot: set}} updated in
+    head_dim, inter, eps, theta, vocab; the predictor's may hold proj_w / proj_b (its input projection), the
+    talker's "text" (a text_projection dict; then text_ids [M] may replace text).  state: {"tk", "tv", "pk", "pv" caches, "history": {slot: set}} updated in
     place.  hidden_in / logits_in: the talker's outputs when its step already ran (the prompt pass).
     Returns (codes [M, G] int32, talker hidden [M, H], talker logits [M, V], predictor logits: a list of G-1
     arrays [M, V_p], the one each acoustic code was chosen from)."""
@@ -352,6 +367,8 @@ def frame(talker: dict, predictor: dict, ptables: list, groups: int, text: np.nd
     M = pos.shape[0]
     dims = lambda c: dict(hidden=c["hidden"], n_head=c["n_head"], n_kv=c["n_kv"], head_dim=c["head_dim"],
                           inter=c["inter"], eps=c["eps"], theta=c["theta"], mode=mode, threads=threads)
+    if hidden_in is None and text_ids is not None:  # text rows through the talker's text projection
+        text = text_projection(T["text"], text_ids, mode, threads)
     if hidden_in is None:
         x = np.empty((M, H), np.float32)
         for m in range(M):

@@ -362,6 +362,16 @@ static float silu_f32(float x) {
     return x / (1.0f + expf(-x));
 }
 
+/* x[r][i] = silu(x[r][i] + b[i]) in fp32: ggml_silu(ggml_add(mul_mat(W1, t), b1))
+ * of the talker's text projection (src/arch/qwen3-tts/talker.cpp:45-47). */
+void oracle_bias_silu_rows(float * x, const float * b, int64_t rows, int64_t n) {
+    for (int64_t r = 0; r < rows; ++r) {
+        for (int64_t i = 0; i < n; ++i) {
+            x[r * n + i] = silu_f32(x[r * n + i] + b[i]);
+        }
+    }
+}
+
 /* Qwen3's per-head RMS norm followed by NEOX RoPE, in place, for one token:
  * x holds n_heads heads of head_dim values (src/arch/qwen3-tts/operations.cpp:
  * 95-101: rms_norm(q, q_norm) then ggml_rope_ext(..., GGML_ROPE_TYPE_NEOX,

@@ -113,6 +113,7 @@ void oracle_decoder_chain_attn(int n_layers, const void * const * weights, const
                                const int32_t * ids, const float * x_in, const int32_t * pos, const int32_t * slots,
                                int64_t M, int64_t n_slots, int64_t n_ctx, float * kcache, float * vcache, float * h_out,
                                int mode, int threads);
+void oracle_bias_silu_rows(float * x, const float * b, int64_t rows, int64_t n);
 void oracle_rms_norm_rows(const float * x, const float * w, float * y, int64_t rows, int64_t n, float eps);
 int oracle_max_threads(void);
 

@@ -71,20 +71,22 @@ class FrameDesc(ctypes.Structure):
     _fields_ = [("talker", ctypes.c_void_p), ("predictor", ctypes.c_void_p), ("groups", ctypes.c_int32),
                 ("tables", ctypes.POINTER(ctypes.c_void_p)), ("table_rows", ctypes.c_int64),
                 ("repetition_penalty", ctypes.c_float), ("input_projection", ctypes.c_void_p),
-                ("input_projection_bias", ctypes.c_void_p)]
+                ("input_projection_bias", ctypes.c_void_p), ("text_embedding", ctypes.c_void_p),
+                ("text_rows", ctypes.c_int64), ("text_hidden", ctypes.c_int64), ("text_fc1", ctypes.c_void_p),
+                ("text_fc1_bias", ctypes.c_void_p), ("text_fc2", ctypes.c_void_p), ("text_fc2_bias", ctypes.c_void_p)]
 
 
 class FrameArgs(ctypes.Structure):
     _fields_ = [("M", ctypes.c_int64), ("skip_talker", ctypes.c_int32), ("text", ctypes.c_void_p),
                 ("prev", ctypes.c_void_p), ("pos", ctypes.c_void_p), ("slots", ctypes.c_void_p),
                 ("replay", ctypes.c_void_p), ("codes", ctypes.c_void_p), ("hidden", ctypes.c_void_p),
-                ("talker_logits", ctypes.c_void_p)]
+                ("talker_logits", ctypes.c_void_p), ("text_ids", ctypes.c_void_p)]
 
 
 def header_symbols(header: str = HEADER) -> list[str]:
     """Every function a public header declares."""
     text = open(header).read()
-    return sorted(set(re.findall(r"^\S[^\n;]*?\b(b200q8_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\S[^\n;]*?\b(b200q8h?_\w+)\s*\(", text, flags=re.M)))
 
 
 def lib() -> ctypes.CDLL:
@@ -140,6 +142,8 @@ def lib() -> ctypes.CDLL:
     L.b200q8_frame_create.restype = i32
     L.b200q8_frame_run.argtypes = [vp, ctypes.POINTER(FrameArgs), vp]
     L.b200q8_frame_run.restype = i32
+    L.b200q8_frame_text_rows.argtypes = [vp, vp, i64, vp, vp, vp]
+    L.b200q8_frame_text_rows.restype = i32
     L.b200q8_frame_reset_history.argtypes = [vp, i32, vp]
     L.b200q8_frame_reset_history.restype = i32
     L.b200q8_frame_destroy.argtypes = [vp]

@@ -1,8 +1,11 @@
 """Build recipe for the in-tree native libraries of the Q8_0 hot path.
 
     libb200q8.so       the CUDA kernels + C ABI (include/b200q8.h), sm_100a only
-    libb200q8_host.so  host C++: seeded input streams, thread policy and the
-                       ggml-seam shim over that ABI (host/*.cpp)
+    libb200q8_host.so  host C++: seeded input streams, thread policy, the
+                       ggml-seam shim and the package decoder driver
+                       (include/b200q8_host.h) over that ABI (host/*.cpp)
+    synth_b200_frames  the command-line frame driver (host/cli/), over
+                       libb200q8_host.so
 
 Both are written next to this file so they travel with the source tree.
 """
@@ -18,6 +21,7 @@ CSRC = os.path.join(PKG, "csrc")
 HOST = os.path.join(PKG, "host")
 LIB = os.path.join(PKG, "libb200q8.so")
 HOST_LIB = os.path.join(PKG, "libb200q8_host.so")
+CLI = os.path.join(PKG, "synth_b200_frames")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -31,6 +35,11 @@ def _nvcc() -> str:
         if cand and os.path.exists(cand):
             return cand
     raise RuntimeError("nvcc not found: the B200 library cannot be built")
+
+
+def _cuda_home() -> str:
+    nvcc = _nvcc()
+    return os.path.dirname(os.path.dirname(os.path.realpath(nvcc)))
 
 
 def _sources(d: str, exts: tuple[str, ...]) -> list[str]:
@@ -55,13 +64,23 @@ def build(force: bool = False, verbose: bool = False) -> list[str]:
         subprocess.run(cmd, check=True)
     out = [LIB]
     host_srcs = _sources(HOST, (".cpp",))
+    cuda = _cuda_home()
+    cuda_flags = [f"-I{os.path.join(cuda, 'include')}"]
+    cuda_libs = [f"-L{os.path.join(cuda, 'lib64')}", "-lcudart", f"-Wl,-rpath,{os.path.join(cuda, 'lib64')}"]
     if host_srcs:
         host_deps = host_srcs + _sources(HOST, (".h",)) + _sources(include, (".h",)) + [LIB]
         if force or _stale(HOST_LIB, host_deps):
-            cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-pthread", f"-I{include}", "-o", HOST_LIB,
-                   *host_srcs, f"-L{PKG}", "-lb200q8", "-Wl,-rpath,$ORIGIN"]
+            cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-pthread", f"-I{include}", *cuda_flags, "-o",
+                   HOST_LIB, *host_srcs, f"-L{PKG}", "-lb200q8", *cuda_libs, "-Wl,-rpath,$ORIGIN"]
             subprocess.run(cmd, check=True)
         out.append(HOST_LIB)
+    cli_srcs = _sources(os.path.join(HOST, "cli"), (".cpp",))
+    if cli_srcs:
+        if force or _stale(CLI, cli_srcs + _sources(include, (".h",)) + [HOST_LIB]):
+            cmd = ["g++", "-O2", "-std=c++17", f"-I{include}", "-o", CLI, *cli_srcs, f"-L{PKG}", "-lb200q8_host",
+                   "-lb200q8", "-Wl,-rpath,$ORIGIN"]
+            subprocess.run(cmd, check=True)
+        out.append(CLI)
     return out
 
 

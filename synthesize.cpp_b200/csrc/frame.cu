@@ -199,6 +199,15 @@ __global__ void add_bias_kernel(float * __restrict__ y, const float * __restrict
     }
 }
 
+// y[m][n] = silu(y[m][n] + b[n]): the text projection's first Linear and its
+// activation (ggml_silu(ggml_add(mul_mat(W1, x), b1)), talker.cpp:45-47).
+__global__ void add_bias_silu_kernel(float * __restrict__ y, const float * __restrict__ b, int64_t M, int64_t N) {
+    const int64_t total = M * N;
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t) gridDim.x * blockDim.x) {
+        y[i] = silu_f32(__fadd_rn(y[i], b[i % N]));
+    }
+}
+
 int frame_grid(int64_t total, int sms) {
     return (int) std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t) sms * 4));
 }
@@ -215,6 +224,7 @@ struct b200q8_frame {
     int                  G         = 0;
     float                penalty   = 1.0f;
     int                  mode      = 0;  // the predictor chain's quantizer
+    int                  tmode     = 0;  // the talker chain's quantizer
     int64_t              prows     = 0;
     int64_t              max_m     = 0;
     size_t               rb        = 0;  // Q8_0 row bytes at the hidden width
@@ -241,6 +251,18 @@ struct b200q8_frame {
     float *              xe        = nullptr;  // [max_m][talker hidden] embedded codes
     float *              xq        = nullptr;  // [2 max_m][predictor hidden] projected input rows
     void *               proj_ws   = nullptr;  // MUL_MAT workspace
+    // text projection (frames run from text token ids)
+    const uint8_t *      txt_emb   = nullptr;  // Q8_0 [txt_rows][txt_hidden]
+    int64_t              txt_rows  = 0;
+    int64_t              txt_hidden = 0;
+    const uint8_t *      txt_w1    = nullptr;  // Q8_0 [txt_hidden rows] of K = txt_hidden
+    const float *        txt_b1    = nullptr;
+    const uint8_t *      txt_w2    = nullptr;  // Q8_0 [talker hidden rows] of K = txt_hidden
+    const float *        txt_b2    = nullptr;
+    float *              tx0       = nullptr;  // [max_m][txt_hidden] embedded text tokens
+    float *              tx1       = nullptr;  // [max_m][txt_hidden] after fc1 + silu
+    float *              tx2       = nullptr;  // [max_m][talker hidden] text rows
+    void *               txt_ws    = nullptr;  // MUL_MAT workspace
     cudaStream_t         cap       = nullptr;
 
     struct Graph {
@@ -255,7 +277,7 @@ namespace {
 bool same_args(const b200q8_frame_args & x, const b200q8_frame_args & y) {
     return x.M == y.M && x.skip_talker == y.skip_talker && x.text == y.text && x.prev == y.prev && x.pos == y.pos &&
            x.slots == y.slots && x.replay == y.replay && x.codes == y.codes && x.hidden == y.hidden &&
-           x.talker_logits == y.talker_logits;
+           x.talker_logits == y.talker_logits && x.text_ids == y.text_ids;
 }
 
 void frame_free(b200q8_frame * f) {
@@ -278,6 +300,33 @@ void frame_free(b200q8_frame * f) {
     delete f;
 }
 
+// The talker's text rows for M token ids (build_text_projection,
+// talker.cpp:37-50): out = W2 * Q(silu(W1 * Q(text_embedding[id]) + b1)) + b2.
+// h1 (nullable) receives silu(W1 * Q(.) + b1), [M][text hidden].
+cudaError_t enqueue_text(b200q8_frame * f, cudaStream_t st, const int32_t * ids, int64_t M, float * h1, float * out) {
+    const int64_t Th  = f->txt_hidden, H = f->ti.hidden;
+    const int     sms = f->ti.sms;
+    const size_t  rt  = (size_t) (Th / kQK) * kBlockBytes;
+    float *       y1  = h1 != nullptr ? h1 : f->tx1;
+    cudaError_t   e   = launch_dequant_rows(f->txt_emb, rt, f->txt_rows, ids, M, Th, f->tx0,
+                                            (size_t) Th * sizeof(float), st, sms);
+    if (e == cudaSuccess) {
+        e = launch_gemm(f->txt_w1, rt, Th, Th, f->tx0, (size_t) Th, M, y1, (size_t) Th, f->tmode, f->txt_ws, st, sms);
+    }
+    if (e == cudaSuccess) {
+        add_bias_silu_kernel<<<frame_grid(M * Th, sms), 256, 0, st>>>(y1, f->txt_b1, M, Th);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        e = launch_gemm(f->txt_w2, rt, Th, H, y1, (size_t) Th, M, out, (size_t) H, f->tmode, f->txt_ws, st, sms);
+    }
+    if (e == cudaSuccess) {
+        add_bias_kernel<<<frame_grid(M * H, sms), 256, 0, st>>>(out, f->txt_b2, M, H);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
 cudaError_t enqueue_frame(b200q8_frame * f, cudaStream_t st, const b200q8_frame_args & a) {
     const int64_t M = a.M, H = f->ti.hidden;
     const int     sms = f->ti.sms;
@@ -285,9 +334,14 @@ cudaError_t enqueue_frame(b200q8_frame * f, cudaStream_t st, const b200q8_frame_
     float *       tlg = a.talker_logits != nullptr ? a.talker_logits : f->tlog;
     frame_setup_kernel<<<1, 256, 0, st>>>(a.slots, f->slots1, f->pslots, M);
     cudaError_t e = cudaGetLastError();
+    const float * text = a.text;
+    if (e == cudaSuccess && !a.skip_talker && a.text_ids != nullptr) {
+        e    = enqueue_text(f, st, a.text_ids, M, nullptr, f->tx2);
+        text = f->tx2;
+    }
     if (e == cudaSuccess && !a.skip_talker) {
         frame_embed_kernel<<<frame_grid(M * H, sms), 256, 0, st>>>(f->ptabs, f->prows, f->ti.table, f->ti.table_rows,
-                                                                 f->rb, a.prev, f->G, a.text, f->xt, M, H);
+                                                                 f->rb, a.prev, f->G, text, f->xt, M, H);
         e = cudaGetLastError();
         if (e == cudaSuccess) {
             StepIO io;
@@ -395,6 +449,22 @@ b200q8_status_t b200q8_frame_create(const b200q8_frame_desc * desc, b200q8_frame
         return set_error(B200Q8_ERR_INVALID_ARG, "frame_create: a predictor of another width than the talker needs "
                                                  "both the input projection (16-byte aligned Q8_0) and its bias");
     }
+    const bool txt = desc->text_embedding != nullptr || desc->text_fc1 != nullptr || desc->text_fc2 != nullptr ||
+                     desc->text_fc1_bias != nullptr || desc->text_fc2_bias != nullptr;
+    if (txt) {
+        const int64_t Th = desc->text_hidden;
+        const size_t  rt = Th > 0 ? (size_t) (Th / kQK) * kBlockBytes : 0;
+        const int64_t mm = std::min<int64_t>(ti.max_m, pi.max_m / 2);
+        if (desc->text_embedding == nullptr || desc->text_fc1 == nullptr || desc->text_fc2 == nullptr ||
+            desc->text_fc1_bias == nullptr || desc->text_fc2_bias == nullptr || desc->text_rows < 1 || Th < 256 ||
+            Th % 256 != 0 || reinterpret_cast<uintptr_t>(desc->text_embedding) % 2 != 0 || mm < 1 ||
+            !gemm_supported(static_cast<const uint8_t *>(desc->text_fc1), rt, Th, Th, mm) ||
+            !gemm_supported(static_cast<const uint8_t *>(desc->text_fc2), rt, Th, ti.hidden, mm)) {
+            return set_error(B200Q8_ERR_INVALID_ARG, "frame_create: a text projection needs the embedding, both "
+                                                     "Linears (16-byte aligned Q8_0) and both biases, with a text "
+                                                     "width that is a multiple of 256");
+        }
+    }
     if (pi.n_ctx < G || pi.n_slots < ti.n_slots) {
         return set_error(B200Q8_ERR_INVALID_ARG, "frame_create: the predictor needs n_ctx >= groups and n_slots >= "
                                                  "the talker's");
@@ -417,6 +487,16 @@ b200q8_status_t b200q8_frame_create(const b200q8_frame_desc * desc, b200q8_frame
     f->max_m     = max_m;
     f->rb        = (size_t) (ti.hidden / kQK) * kBlockBytes;
     f->mode      = chain_mode(desc->predictor);
+    f->tmode     = chain_mode(desc->talker);
+    if (txt) {
+        f->txt_emb    = static_cast<const uint8_t *>(desc->text_embedding);
+        f->txt_rows   = desc->text_rows;
+        f->txt_hidden = desc->text_hidden;
+        f->txt_w1     = static_cast<const uint8_t *>(desc->text_fc1);
+        f->txt_b1     = desc->text_fc1_bias;
+        f->txt_w2     = static_cast<const uint8_t *>(desc->text_fc2);
+        f->txt_b2     = desc->text_fc2_bias;
+    }
     f->proj_w    = static_cast<const uint8_t *>(desc->input_projection);
     f->proj_b    = desc->input_projection_bias;
     for (int g = 0; g + 1 < G; ++g) {
@@ -445,6 +525,13 @@ b200q8_status_t b200q8_frame_create(const b200q8_frame_desc * desc, b200q8_frame
         f->xe      = static_cast<float *>(alloc(sizeof(float) * (size_t) (max_m * H)));
         f->xq      = static_cast<float *>(alloc(sizeof(float) * (size_t) (2 * max_m * Hp)));
         f->proj_ws = alloc(gemm_workspace_bytes(H, 2 * max_m));
+    }
+    if (f->txt_emb != nullptr) {
+        const int64_t Th = f->txt_hidden;
+        f->tx0    = static_cast<float *>(alloc(sizeof(float) * (size_t) (max_m * Th)));
+        f->tx1    = static_cast<float *>(alloc(sizeof(float) * (size_t) (max_m * Th)));
+        f->tx2    = static_cast<float *>(alloc(sizeof(float) * (size_t) (max_m * H)));
+        f->txt_ws = alloc(gemm_workspace_bytes(Th, max_m));
     }
     f->plog    = static_cast<float *>(alloc(sizeof(float) * (size_t) (2 * max_m * pi.vocab)));
     f->cur     = static_cast<int32_t *>(alloc(sizeof(int32_t) * (size_t) max_m));
@@ -480,9 +567,12 @@ b200q8_status_t b200q8_frame_run(b200q8_frame * f, const b200q8_frame_args * a, 
                          (long long) a->M, (long long) f->max_m);
     }
     if (a->skip_talker ? (a->hidden == nullptr || a->talker_logits == nullptr)
-                       : (a->text == nullptr || a->prev == nullptr || a->pos == nullptr)) {
+                       : ((a->text == nullptr && a->text_ids == nullptr) || a->prev == nullptr || a->pos == nullptr)) {
         return set_error(B200Q8_ERR_INVALID_ARG, a->skip_talker ? "frame_run: skip_talker needs hidden and talker_logits"
-                                                                : "frame_run: needs text, prev and pos");
+                                                                : "frame_run: needs text (or text_ids), prev and pos");
+    }
+    if (a->text_ids != nullptr && !a->skip_talker && f->txt_emb == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "frame_run: text_ids given to a frame built without a text projection");
     }
     if (a->slots == nullptr && a->M > f->ti.n_slots) {
         return set_error(B200Q8_ERR_INVALID_ARG, "frame_run: M (%lld) streams need explicit slots beyond n_slots",
@@ -545,6 +635,28 @@ b200q8_status_t b200q8_frame_run(b200q8_frame * f, const b200q8_frame_args * a, 
     e = cudaGraphLaunch(exec, reinterpret_cast<cudaStream_t>(stream));
     cudaSetDevice(prev);
     return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "frame_run: graph launch");
+}
+
+b200q8_status_t b200q8_frame_text_rows(b200q8_frame * f, const int32_t * text_ids, int64_t M, float * h1,
+                                       float * out, b200q8_stream_t stream) {
+    if (f == nullptr || text_ids == nullptr || out == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "frame_text_rows: null argument");
+    }
+    if (f->txt_emb == nullptr) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "frame_text_rows: the frame was built without a text projection");
+    }
+    if (M < 1 || M > f->max_m) {
+        return set_error(B200Q8_ERR_INVALID_ARG, "frame_text_rows: M (%lld) must be in [1, %lld]", (long long) M,
+                         (long long) f->max_m);
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(f->ti.device);
+    if (e == cudaSuccess) {
+        e = enqueue_text(f, reinterpret_cast<cudaStream_t>(stream), text_ids, M, h1, out);
+    }
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "frame_text_rows");
 }
 
 b200q8_status_t b200q8_frame_reset_history(b200q8_frame * f, int32_t slot, b200q8_stream_t stream) {

@@ -613,6 +613,30 @@ b200q8_status_t b200q8_gguf_decoder(const b200q8_gguf * g, int32_t device, int64
             return st;
         }
     }
+    // the talker's text side (build_text_projection, talker.cpp:37-50; tensors
+    // as catalog.cpp:271-275 resolves them), when the package carries it
+    const bool                  txt = b200q8_gguf_find_tensor(g, "talker.model.text_embedding.weight") >= 0;
+    uint32_t                    t_text_hidden = 0, t_text_vocab = 0;
+    std::vector<const Tensor *> txt_found;
+    if (txt) {
+        if (b200q8_gguf_get_u32(g, (tp + "text_hidden_size").c_str(), &t_text_hidden) != B200Q8_OK ||
+            b200q8_gguf_get_u32(g, (tp + "text_vocab_size").c_str(), &t_text_vocab) != B200Q8_OK ||
+            t_text_hidden == 0 || t_text_vocab == 0) {
+            return set_error(B200Q8_ERR_INVALID_ARG, "%s: text_embedding without text_hidden_size / text_vocab_size",
+                             who);
+        }
+        const std::vector<Need> tn = {
+            { "talker.model.text_embedding.weight", 8, t_text_hidden, t_text_vocab },
+            { "talker.text_projection.linear_fc1.weight", 8, t_text_hidden, t_text_hidden },
+            { "talker.text_projection.linear_fc1.bias", 0, t_text_hidden, 1 },
+            { "talker.text_projection.linear_fc2.weight", 8, t_text_hidden, ts.hidden },
+            { "talker.text_projection.linear_fc2.bias", 0, ts.hidden, 1 },
+        };
+        st = find_tensors(g, tn, who, txt_found);
+        if (st != B200Q8_OK) {
+            return st;
+        }
+    }
     ts.prefix       = "talker.model.layers.";
     ts.attention    = true;
     ts.n_ctx        = n_ctx;
@@ -653,10 +677,38 @@ b200q8_status_t b200q8_gguf_decoder(const b200q8_gguf * g, int32_t device, int64
         }
         cudaSetDevice(prev);
     }
+    std::vector<const void *> txt_ptr(5, nullptr);
+    if (st == B200Q8_OK && txt) {  // uploaded into a buffer the talker chain owns
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaError_t e = cudaSetDevice(device);
+        uint8_t *   buf = nullptr;
+        st = e == cudaSuccess ? upload_tensors(g, txt_found, &buf, txt_ptr) : cuda_error(e, "gguf: cudaSetDevice");
+        if (st == B200Q8_OK) {
+            tc->owned.push_back(buf);
+        }
+        cudaSetDevice(prev);
+    }
     if (st == B200Q8_OK && frame != nullptr) {
-        const b200q8_frame_desc fd = { tc, pc, (int32_t) t_groups, ptables.data(), p_vocab, penalty, proj_ptr[0],
-                                       static_cast<const float *>(proj_ptr[1]) };
-        st                         = b200q8_frame_create(&fd, frame);
+        b200q8_frame_desc fd     = {};
+        fd.talker                = tc;
+        fd.predictor             = pc;
+        fd.groups                = (int32_t) t_groups;
+        fd.tables                = ptables.data();
+        fd.table_rows            = p_vocab;
+        fd.repetition_penalty    = penalty;
+        fd.input_projection      = proj_ptr[0];
+        fd.input_projection_bias = static_cast<const float *>(proj_ptr[1]);
+        if (txt) {
+            fd.text_embedding = txt_ptr[0];
+            fd.text_rows      = t_text_vocab;
+            fd.text_hidden    = t_text_hidden;
+            fd.text_fc1       = txt_ptr[1];
+            fd.text_fc1_bias  = static_cast<const float *>(txt_ptr[2]);
+            fd.text_fc2       = txt_ptr[3];
+            fd.text_fc2_bias  = static_cast<const float *>(txt_ptr[4]);
+        }
+        st = b200q8_frame_create(&fd, frame);
     }
     if (st != B200Q8_OK) {
         b200q8_chain_destroy(tc);

@@ -171,3 +171,37 @@ def test_modules_import_without_gpu(pkg, name):
     import importlib
 
     importlib.import_module("synthesize_cpp_b200." + name)
+
+
+def test_host_driver_header_is_exported_and_checks_arguments(pkg, tmp_path):
+    """include/b200q8_host.h: every function exported by libb200q8_host.so; argument and file errors answer with
+    status codes and a message before any device is touched; the command-line driver prints its usage."""
+    import os
+
+    from synthesize_cpp_b200 import _abi, build, host
+
+    hdr = os.path.join(os.path.dirname(_abi.HEADER), "b200q8_host.h")
+    declared = _abi.header_symbols(hdr)
+    assert declared == ["b200q8h_decoder_free", "b200q8h_decoder_info_get", "b200q8h_decoder_load",
+                        "b200q8h_decoder_run", "b200q8h_last_error"]
+    out = subprocess.run(["nm", "-D", "--defined-only", host.HOST_LIB], capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert set(declared) <= exported
+    L = host.lib()
+    L.b200q8h_decoder_load.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_void_p]
+    L.b200q8h_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+    buf = ctypes.create_string_buffer(512)
+    h = ctypes.c_void_p()
+    assert L.b200q8h_decoder_load(b"x.gguf", None, ctypes.byref(h)) == _abi.ERR_INVALID_ARG
+    assert L.b200q8h_last_error(buf, 512) == _abi.ERR_INVALID_ARG and b"null" in buf.value
+
+    class Params(ctypes.Structure):
+        _fields_ = [("device", ctypes.c_int32), ("max_streams", ctypes.c_int64), ("n_ctx", ctypes.c_int64),
+                    ("mode", ctypes.c_int32)]
+
+    missing = str(tmp_path / "missing.gguf").encode()
+    assert L.b200q8h_decoder_load(missing, ctypes.byref(Params(0, 1, 16, 0)), ctypes.byref(h)) != _abi.OK
+    L.b200q8h_last_error(buf, 512)
+    assert b"decoder_load" in buf.value and not h.value
+    r = subprocess.run([build.CLI], capture_output=True, text=True)
+    assert r.returncode == 2 and "usage" in r.stderr

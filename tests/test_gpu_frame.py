@@ -273,3 +273,108 @@ def test_frame_with_input_projection(chain_mod, frame_mod, O, dev):
             for g in range(1, G):
                 assert_choice(int(got[i, g]), wplog[g - 1][i], 2e-2 * np.abs(wplog[g - 1][i]).max())
         prev = got
+
+
+TH, TROWS = 512, 300  # text hidden width and text vocabulary of these tests
+
+
+def text_projection(O, dev, seed=8000):
+    """The talker's text side: a Q8_0 text_embedding [TROWS, TH], fc1 [TH, TH] and fc2 [H, TH] with F32 biases;
+    (device dict for Frame, oracle dict for O.text_projection)."""
+    ref = dict(embedding=O.quantize_rows(O.normal(seed, TROWS * TH, 0.5).reshape(TROWS, TH)),
+               fc1=O.quantize_rows(O.normal(seed + 1, TH * TH, 0.05).reshape(TH, TH)),
+               fc1_bias=(0.1 * O.normal(seed + 2, TH)).astype(np.float32),
+               fc2=O.quantize_rows(O.normal(seed + 3, H * TH, 0.05).reshape(H, TH)),
+               fc2_bias=(0.1 * O.normal(seed + 4, H)).astype(np.float32), hidden=TH)
+    return {k: t(v, dev) for k, v in ref.items() if k != "hidden"}, ref
+
+
+def make_text_frame(O, dev, chain_mod, frame_mod, m):
+    """make_frame's talker and predictor, and a frame over them with the text projection."""
+    talker, tref = stack(O, dev, 2, 4000, TV, 1, TV, chain_mod, n_ctx=16, n_slots=m, max_m=max(8, m))
+    pred, pref = stack(O, dev, 2, 5000, PV, G - 1, 8, chain_mod, n_ctx=G, n_slots=m, max_m=max(8, 2 * m))
+    ptables = [O.quantize_rows(O.normal(6000 + g, PV * H, 0.5).reshape(PV, H)) for g in range(G - 1)]
+    tp_dev, tp_ref = text_projection(O, dev)
+    fr = frame_mod.Frame(talker, pred, [t(p, dev) for p in ptables], text_projection=tp_dev)
+    tref["text"] = tp_ref
+    state = dict(tk=np.zeros((2, m, 16, KV), np.float32), tv=np.zeros((2, m, 16, KV), np.float32),
+                 pk=np.zeros((2, m, G, KV), np.float32), pv=np.zeros((2, m, G, KV), np.float32), history={})
+    return fr, tref, pref, ptables, state
+
+
+@pytest.mark.parametrize("m", [1, 5])
+def test_text_rows_against_oracle(chain_mod, frame_mod, O, dev, q8, m):
+    """b200q8_frame_text_rows (build_text_projection, talker.cpp:37-50) op by op: the Q8_0 GET_ROWS exact (it is
+    checked through fc1), fc1 within its MUL_MAT bound with the bias and silu (expf on the device and in libm may
+    differ by an ulp), fc2 on the GPU's own activation within its bound plus the bias's rounding."""
+    fr, tref, *_ = make_text_frame(O, dev, chain_mod, frame_mod, m)
+    tp = tref["text"]
+    ids = np.random.default_rng(m).integers(0, TROWS, m).astype(np.int32)
+    out = torch.empty((m, H), device=dev)
+    h1 = torch.empty((m, TH), device=dev)
+    fr.text_rows(t(ids, dev), out, h1)
+    torch.cuda.synchronize(dev)
+    h1g, outg = h1.cpu().numpy(), out.cpu().numpy()
+    x = O.get_rows(tp["embedding"], TH, ids)[0]
+    y1, b1 = O.mul_mat(tp["fc1"], TH, x)
+    h1_ref = np.ascontiguousarray(y1, np.float32)
+    O.lib().oracle_bias_silu_rows(h1_ref.ctypes.data, tp["fc1_bias"].ctypes.data, m, TH)
+    # silu's slope is within [-0.1, 1.1]: the MUL_MAT bound carries through, plus an ulp of the bias add and
+    # an ulp or two of expf
+    z = np.abs(y1.astype(np.float64) + tp["fc1_bias"])
+    assert np.all(np.abs(h1g - h1_ref) <= 1.2e-5 * b1 + 5e-7 * np.abs(h1_ref) + 2.4e-7 * z + 1e-30)
+    y2, b2 = O.mul_mat(tp["fc2"], TH, h1g)
+    want = y2 + tp["fc2_bias"]
+    assert np.all(np.abs(outg - want) <= 1e-5 * b2 + 1.2e-7 * np.abs(want) + 1e-30)
+    # the whole projection against the oracle's own: only fc2's activation codes can differ, rarely
+    rel = np.linalg.norm(outg - O.text_projection(tp, ids)) / np.linalg.norm(outg)
+    assert rel < 2e-3, rel
+    # an id outside the vocabulary: a zero embedding row, reported in the device status
+    bad = ids.copy()
+    bad[0] = TROWS
+    fr.text_rows(t(bad, dev), out)
+    torch.cuda.synchronize(dev)
+    assert q8.device_status(0) == 1
+    assert q8.device_status(0) == 0
+    fr.close()
+
+
+def test_frame_from_text_ids(chain_mod, frame_mod, O, dev):
+    """Frames run from text token ids: bit-identical to frames given the text rows b200q8_frame_text_rows computes,
+    and greedy frames against the oracle's frame over the same ids (the oracle replaying the GPU's codes)."""
+    m = 2
+    runs = []
+    for use_ids in (True, False):
+        fr, tref, pref, ptables, state = make_text_frame(O, dev, chain_mod, frame_mod, m)
+        rng = np.random.default_rng(31)
+        prev = np.stack([rng.integers(0, TV, m)] + [rng.integers(0, PV, m) for _ in range(G - 1)], 1).astype(np.int32)
+        codes = torch.empty((m, G), dtype=torch.int32, device=dev)
+        hid = torch.empty((m, H), device=dev)
+        tlog = torch.empty((m, TV), device=dev)
+        rows = torch.empty((m, H), device=dev)
+        seq = []
+        for f in range(4):
+            ids = rng.integers(0, TROWS, m).astype(np.int32)
+            pos = np.full(m, f, np.int32)
+            if use_ids:
+                fr.run(codes, text_ids=t(ids, dev), prev=t(prev, dev), pos=t(pos, dev), hidden=hid, talker_logits=tlog)
+            else:
+                fr.text_rows(t(ids, dev), rows)
+                fr.run(codes, text=rows, prev=t(prev, dev), pos=t(pos, dev), hidden=hid, talker_logits=tlog)
+            torch.cuda.synchronize(dev)
+            got = codes.cpu().numpy()
+            seq.append((got.copy(), hid.cpu().numpy(), tlog.cpu().numpy()))
+            if use_ids:
+                _, whid, wlog, wplog = O.frame(tref, pref, ptables, G, None, prev, pos, np.arange(m, dtype=np.int32),
+                                               state, replay=got, text_ids=ids)
+                rel = np.linalg.norm(seq[-1][1] - whid) / np.linalg.norm(whid)
+                assert rel < 1e-2, (f, rel)
+                for i in range(m):
+                    assert_choice(int(got[i, 0]), wlog[i], 2e-2 * np.abs(wlog[i]).max())
+                    for g in range(1, G):
+                        assert_choice(int(got[i, g]), wplog[g - 1][i], 2e-2 * np.abs(wplog[g - 1][i]).max())
+            prev = got
+        runs.append(seq)
+        fr.close()
+    for (c1, h1, l1), (c2, h2, l2) in zip(*runs):
+        assert np.array_equal(c1, c2) and np.array_equal(h1, h2) and np.array_equal(l1, l2)

@@ -89,7 +89,10 @@ DP = dict(hidden=256, heads=4, kv=2, head_dim=64, inter=512, t_layers=2, p_layer
           groups=4, eps=1e-6, theta=1.0e4, penalty=1.2)
 
 
-def tiny_decoder_package(O, tmp_path, t_hidden=None):
+TEXT_HIDDEN, TEXT_VOCAB = 256, 120
+
+
+def tiny_decoder_package(O, tmp_path, t_hidden=None, text=False):
     """A package with the talker (attention norms, final norm, codec head) and the code predictor (layers, norm,
     per-group tables and heads), named and keyed as the reference's catalog and loader expect.  t_hidden: a talker
     wider than the predictor, which then reads its input through small_to_mtp_projection."""
@@ -157,6 +160,17 @@ def tiny_decoder_package(O, tmp_path, t_hidden=None):
         proj = (q8(H, HT), (0.1 * O.normal(seed[0] + 1, H)).astype(np.float32))
         tensors += [("talker.code_predictor.small_to_mtp_projection.weight", proj[0], None, Q8),
                     ("talker.code_predictor.small_to_mtp_projection.bias", proj[1], None, None)]
+    if text:  # the talker's text side (catalog.cpp:271-275)
+        kv.update({t + "text_hidden_size": ("uint32", TEXT_HIDDEN), t + "text_vocab_size": ("uint32", TEXT_VOCAB)})
+        tp = dict(embedding=q8(TEXT_VOCAB, TEXT_HIDDEN, 0.5), fc1=q8(TEXT_HIDDEN, TEXT_HIDDEN),
+                  fc1_bias=(0.1 * O.normal(seed[0] + 2, TEXT_HIDDEN)).astype(np.float32), fc2=q8(HT, TEXT_HIDDEN),
+                  fc2_bias=(0.1 * O.normal(seed[0] + 3, HT)).astype(np.float32))
+        tensors += [("talker.model.text_embedding.weight", tp["embedding"], None, Q8),
+                    ("talker.text_projection.linear_fc1.weight", tp["fc1"], None, Q8),
+                    ("talker.text_projection.linear_fc1.bias", tp["fc1_bias"], None, None),
+                    ("talker.text_projection.linear_fc2.weight", tp["fc2"], None, Q8),
+                    ("talker.text_projection.linear_fc2.bias", tp["fc2_bias"], None, None)]
+        proj = (proj, tp)
     path = tmp_path / "tiny_decoder.gguf"
     write_package(path, kv, tensors)
     return path, stacks, (ttable, thead, tnorm), (ptables, pheads, pnorm), proj
@@ -206,3 +220,61 @@ def test_package_decoder_matches_direct_frame(pkg, O, chain_mod, frame_mod, dev,
         assert torch.equal(c1, c2) and torch.equal(h1, h2) and torch.equal(l1, l2)
     from_pkg.close()
     direct.close()
+
+
+def test_cpp_driver_runs_a_package_like_the_python_path(pkg, O, dev, tmp_path):
+    """The C++ host driver (synth_b200_frames over b200q8h_decoder_load / b200q8h_decoder_run) loads a package with
+    the talker's text projection and decodes frames from text token ids, reading each frame's codes back before
+    the next; its codes equal those of the same package driven from Python (b200q8_gguf_decoder + frame runs from
+    the same ids), and its stop code ends a stream where the codes say so."""
+    import json
+    import os
+    import subprocess
+
+    from synthesize_cpp_b200 import build
+    from synthesize_cpp_b200 import gguf as G
+
+    path, *_ = tiny_decoder_package(O, tmp_path, text=True)
+    m, F, start = 3, 6, 2
+    rng = np.random.default_rng(44)
+    ids = rng.integers(0, TEXT_VOCAB, (F, m)).astype(np.int32)
+    prev = np.stack([rng.integers(0, DP["t_vocab"], m)] +
+                    [rng.integers(0, DP["p_vocab"], m) for _ in range(DP["groups"] - 1)], 1).astype(np.int32)
+    ids.tofile(tmp_path / "ids.i32")
+    prev.tofile(tmp_path / "prev.i32")
+
+    def drive(stop_code):
+        out = tmp_path / f"codes_{stop_code}.i32"
+        r = subprocess.run([build.CLI, str(path), "--streams", str(m), "--frames", str(F), "--out", str(out),
+                            "--text-ids", str(tmp_path / "ids.i32"), "--prev", str(tmp_path / "prev.i32"),
+                            "--start-pos", str(start), "--stop-code", str(stop_code),
+                            "--device", str(dev.index or 0)], capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr
+        return np.fromfile(out, np.int32).reshape(F, m, DP["groups"]), json.loads(r.stdout.strip().splitlines()[-1])
+
+    cpp, rep = drive(-1)
+    assert rep["frames"] == [F] * m
+    # the Python path over the same package and inputs
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    with G.Package(path) as p:
+        talker, pred, fr = p.decoder(device=dev.index or 0, max_m=m, n_ctx=start + F, n_slots=m)
+    codes = torch.empty((m, DP["groups"]), dtype=torch.int32, device=dev)
+    pv = t(prev)
+    py = []
+    for f in range(F):
+        fr.run(codes, text_ids=t(ids[f]), prev=pv, pos=t(np.full(m, start + f, np.int32)))
+        torch.cuda.synchronize(dev)
+        py.append(codes.cpu().numpy().copy())
+        pv = codes.clone()
+    fr.close()
+    talker.close()
+    pred.close()
+    assert np.array_equal(cpp, np.stack(py))
+    # a stop code: each stream ends at its first frame whose code 0 is it (the stop frame not counted)
+    stop = int(cpp[2, 1, 0])
+    cpp2, rep2 = drive(stop)
+    want = [next((f for f in range(F) if cpp[f, s, 0] == stop), F) for s in range(m)]
+    assert rep2["frames"] == want
+    last = max(want) + 1 if max(want) < F else F
+    assert np.array_equal(cpp2[:last], cpp[:last])
+    assert os.path.exists(build.CLI)
