@@ -44,7 +44,7 @@ def parse():
     ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b", "gemv", "gemv-large", "mul-mat",
                              "frame"],
                     help="talker: BASELINE config 2 (config 3 with --batch 16/64/256); talker-1.7b: config 4 shapes; "
-                         "dp-sweep: config 5, 512 streams split over the ranks in M=64 batches; "
+                         "dp-sweep: config 5, 512 streams split over the ranks in M=64 batches (one launch per op); "
                          "pack-1.7b: config 4 packing of all 1.4 B weights (synthesize-quantize); "
                          "gemv / gemv-large: config 1 GEMV (and a 142 MB one) as an HBM bandwidth measurement; "
                          "mul-mat: one MUL_MAT of --n x --k at M = --batch")
@@ -205,8 +205,11 @@ def talker_shape(args):
 def talker_sizes(args, world: int, rank: int):
     """(first stream, [batch sizes]) this rank runs per step."""
     if args.workload == "dp-sweep":
-        # BASELINE config 5: 512 independent streams split evenly over the ranks, run as M=64 batches
-        return load_shapes().partition_streams(512, world, rank, 64)
+        # BASELINE config 5: 512 independent streams split evenly over the ranks, run as M=64 batches.  One
+        # launch per op serves all of a rank's batches: the tensor-core GEMM takes the tokens in chunks of at
+        # most 64 (the batches), so every weight tile is read once per step and applied to each batch's records
+        first, batches = load_shapes().partition_streams(512, world, rank, 64)
+        return first, [sum(batches)]
     return rank * args.batch, [args.batch]
 
 
@@ -214,8 +217,9 @@ def talker_config(args, shape, sizes, world: int) -> dict:
     """The workload's config dict; both arms print exactly this."""
     dp = args.workload == "dp-sweep"
     if dp:
-        workload = (f"{shape.name} decode, BASELINE config 5: 512 streams over {world} GPU(s), "
-                    f"batches {sizes} per GPU per step")
+        n = sum(sizes)
+        workload = (f"{shape.name} decode, BASELINE config 5: 512 streams over {world} GPU(s), {n} per GPU per "
+                    f"step as {(n + 63) // 64} M<=64 batches, one launch per op for all of them")
     else:
         cfg = "4" if args.workload == "talker-1.7b" else ("2" if args.batch == 1 else "3")
         workload = f"{shape.name} decode step (BASELINE config {cfg}), M={args.batch} per GPU"
