@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=1, help="tokens (streams) per step per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chain", default="auto", choices=["auto", "per-op"],
-                    help="auto: single-launch persistent step for M <= 2; per-op: CUDA graph of per-op kernels")
+                    help="auto: single-launch persistent step for M <= 8; per-op: CUDA graph of per-op kernels")
     return ap.parse_args()
 
 
@@ -948,7 +948,7 @@ def main():
     step_bytes = config["algorithmic_bytes_per_step"]
     step_flops = config["int8_ops_per_step"]
     achieved = step_bytes / step_s / 1e9
-    persistent = args.chain == "auto" and m_max <= 2
+    persistent = args.chain == "auto" and m_max <= 8
     per_batch = lambda m: 1 if persistent else (2 + 8 * shape.n_layers if m > 8 else 1 + 4 * shape.n_layers)
     launches_per_step = sum(per_batch(m) for m in sizes)
     if persistent:

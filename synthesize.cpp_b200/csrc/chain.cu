@@ -89,12 +89,14 @@ struct b200q8_chain {
     float *                      h0           = nullptr;
     cudaStream_t                 cap_stream   = nullptr;
     int                          sms          = 148;
-    // persistent single-launch step (M <= 2)
+    // persistent single-launch step (M <= 8; M <= 2 with attention)
     StepLayerDev *               step_layers  = nullptr;  // device array
     unsigned long long *         ll           = nullptr;
     size_t                       ll_layer     = 0;
     unsigned *                   sync         = nullptr;
     bool                         persistent   = false;
+    int                          persistent_max_m = 0;  // largest M the persistent step takes
+    int                          ll_m         = 2;      // token stride of the hand-off words
     bool                         persistent_in_graph = true;  // cleared if a graph cannot hold its launch
     void *                       timeline     = nullptr;  // B200Q8_TIMELINE analysis builds only
     void *                       planes       = nullptr;  // batched path (M > 8): GEMM code/scale planes
@@ -204,7 +206,7 @@ const uint8_t * contiguous(b200q8_chain * c, const void * a, size_t a_bytes, con
 // The persistent single-launch step's arguments for io; false when the step
 // cannot run it (M > 2, a shape or head it does not support, or disabled).
 bool persistent_args(b200q8_chain * c, const StepIO & io, StepArgs & a) {
-    if (!c->persistent || io.M > 2) {
+    if (!c->persistent || io.M > c->persistent_max_m) {
         return false;
     }
     const b200q8_chain_desc & d = c->d;
@@ -217,7 +219,7 @@ bool persistent_args(b200q8_chain * c, const StepIO & io, StepArgs & a) {
     a.rb_h = c->rb_h; a.rb_q = c->rb_q; a.rb_i = c->rb_i;
     a.table = io.table; a.table_rows = io.table_rows;
     a.ids = io.ids; a.x_in = io.x_in; a.h_out = io.h_out; a.M = (int) io.M; a.mode = d.mode;
-    a.ll = c->ll; a.ll_layer = c->ll_layer; a.ll_m = 2;
+    a.ll = c->ll; a.ll_layer = c->ll_layer; a.ll_m = c->ll_m;
     a.trace = c->act; a.trace_layer = c->layer_floats;
     for (int i = 0; i < kNumBufs; ++i) a.trace_off[i] = c->buf_off[i];
     a.sync = c->sync;
@@ -622,7 +624,7 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
             c->attn_count   = static_cast<unsigned *>(p4);
         }
     }
-    // persistent step (M <= 2): per-layer weight table, LL hand-off words,
+    // persistent step (M <= 8, or 2 with attention): per-layer weight table, LL hand-off words,
     // sync words
     const char * per_op = getenv("B200Q8_CHAIN_PER_OP");
     if (e == cudaSuccess && !(per_op && per_op[0] == '1')) {
@@ -632,7 +634,9 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
                                c->layers[l].norm_in, c->layers[l].norm_post,
                                c->attn ? c->q_norm[l] : nullptr, c->attn ? c->k_norm[l] : nullptr };
         }
-        c->ll_layer  = (size_t) 2 * (c->qkv_dim + Q + H + I + H);
+        // hand-off words for up to 8 tokens (2 with attention)
+        c->ll_m      = c->attn ? 2 : (int) std::min<int64_t>(8, std::max<int64_t>(2, d.max_m));
+        c->ll_layer  = (size_t) c->ll_m * (c->qkv_dim + Q + H + I + H);
         void * p1 = nullptr, * p2 = nullptr, * p3 = nullptr;
         e = cudaMalloc(&p1, sizeof(StepLayerDev) * d.n_layers);
         if (e == cudaSuccess) { c->owned.push_back(p1); e = cudaMalloc(&p2, sizeof(unsigned long long) * c->ll_layer * d.n_layers); }
@@ -649,7 +653,9 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
         StepArgs probe = {};
         probe.H = (int) H; probe.Q = (int) (d.n_head * d.head_dim); probe.KV = (int) KV; probe.I = (int) I;
         probe.mode = d.mode; probe.attn = c->attn ? 1 : 0; probe.head_dim = (int) d.head_dim;
-        c->persistent = e == cudaSuccess && decode_step_fits(probe);
+        probe.ll_m = c->ll_m;
+        c->persistent_max_m = e == cudaSuccess ? std::min(decode_step_max_m(probe), c->ll_m) : 0;
+        c->persistent       = c->persistent_max_m > 0;
 #ifdef B200Q8_TIMELINE
         // analysis builds: the stamp buffer exists before any graph capture
         if (e == cudaSuccess && cudaMalloc(&c->timeline, sizeof(unsigned long long) * 8 * 4 * d.n_layers * c->sms) ==

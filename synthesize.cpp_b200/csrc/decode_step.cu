@@ -1,5 +1,5 @@
 // decode_step.cu -- the whole talker-shaped decode step as ONE persistent
-// kernel launch (sm_100a), for M <= 2 tokens.
+// kernel launch (sm_100a), for M <= 8 tokens (M <= 2 with attention).
 //
 // Why: at M = 1 the step is 4 * n_layers dependent MUL_MATs of 1-7 MB each.
 // Launched one by one (the reference's GraphRun per step, or a CUDA graph of
@@ -127,7 +127,7 @@ struct Smem {
     uint64_t * empty;
     unsigned * epoch;
     int *      abort_local;
-    double *   rms_part;   // [kStepConsumerWarps][2] (header room for 16 warps)
+    double *   rms_part;   // [kStepConsumerWarps][M_T] (header room for 12 warps x 8 tokens)
     float *    rms_scale;  // unused slot kept for the header layout
     float *    hbuf;       // [M_T][H]
     float *    h1buf;      // [M_T][H]
@@ -364,57 +364,73 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
     for (int m = 0; m < M_T; ++m) {
         ss[m] = 0.0;
     }
-    constexpr int kPer = 4;  // elements in flight per thread per pass
+    // The M tokens' H values are one flat range of M * H elements (element
+    // i = m * H + e), taken kPer per thread per pass.  (Token by token
+    // measured slower at M = 1; issuing a pass's reads before the previous
+    // pass settles measured slower too: the extra registers spill in the
+    // several-token kernels.)
+    constexpr int kPer   = 4;  // elements in flight per thread per pass
+    const int     total  = M * H;
+    const int     lg_h   = (H & (H - 1)) == 0 ? __ffs(H) - 1 : -1;
+    const int     stride = kStepConsumers * kPer;
+    // a pass's words: the first one's address (the others follow at the
+    // consumer-count stride) and the kPer words read so far
+    auto load = [&](int base, const unsigned long long *& p0, unsigned long long (&w)[kPer], int & n) {
+        n  = 0;
+        p0 = delta != nullptr ? delta + base + t : nullptr;
 #pragma unroll
-    for (int m = 0; m < M_T; ++m) {
-        if (m >= M) {
-            break;
+        for (int i = 0; i < kPer; ++i) {
+            const int e = base + i * kStepConsumers + t;
+            w[i]        = 0;
+            if (e < total) {
+                n = i + 1;
+                if (delta != nullptr) {
+                    w[i] = ld_ll(p0 + i * kStepConsumers);
+                }
+            }
         }
-        const unsigned long long * dm  = delta != nullptr ? delta + (size_t) m * H : nullptr;
-        float *                    hd  = h_dst + (size_t) m * H;
-        const float *              hs  = h_src + (size_t) m * H;
-        for (int base = 0; base < H; base += kStepConsumers * kPer) {
+    };
+    const unsigned long long * p0 = nullptr;
+    unsigned long long         w[kPer];
+    int                        n = 0;
+    load(0, p0, w, n);
+    for (int base = 0; base < total; base += stride) {
+        if (delta != nullptr && !fail) {
             const unsigned long long * src[kPer];
-            unsigned long long         w[kPer];
-            int                        n = 0;
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
-                const int e = base + i * kStepConsumers + t;
-                src[i]      = dm != nullptr ? dm + (e < H ? e : 0) : nullptr;
-                w[i]        = 0;
-                if (e < H) {
-                    n = i + 1;
-                }
+                src[i] = p0 + (i < n ? i * kStepConsumers : 0);
             }
-            if (dm != nullptr) {
+            if (!ll_settle<kPer>(a, s, src, w, n, epoch)) {
+                raise_abort(a, s);  // records the timeout; other CTAs stop at their next check
+                fail = true;
+            }
+        }
 #pragma unroll
-                for (int i = 0; i < kPer; ++i) {
-                    if (i < n) {
-                        w[i] = ld_ll(src[i]);
+        for (int i = 0; i < kPer; ++i) {
+            const int e = base + i * kStepConsumers + t;
+            if (e < total) {
+                const int m = M_T == 1 ? 0 : lg_h >= 0 ? e >> lg_h : e / H;
+                float     v;
+                if (delta != nullptr) {
+                    v = __fadd_rn(h_src[e], __uint_as_float((unsigned) (w[i] & 0xffffffffu)));
+                    h_dst[e] = v;
+                    if (trace_h != nullptr) {
+                        trace_h[e] = v;
+                    }
+                } else {
+                    v = h_dst[e];
+                }
+#pragma unroll
+                for (int mm = 0; mm < M_T; ++mm) {
+                    if (mm == m) {
+                        ss[mm] += (double) __fmul_rn(v, v);
                     }
                 }
-                if (!fail && !ll_settle<kPer>(a, s, src, w, n, epoch)) {
-                    raise_abort(a, s);  // records the timeout; other CTAs stop at their next check
-                    fail = true;
-                }
             }
-#pragma unroll
-            for (int i = 0; i < kPer; ++i) {
-                const int e = base + i * kStepConsumers + t;
-                if (e < H) {
-                    float v;
-                    if (dm != nullptr) {
-                        v     = __fadd_rn(hs[e], __uint_as_float((unsigned) (w[i] & 0xffffffffu)));
-                        hd[e] = v;
-                        if (trace_h != nullptr) {
-                            trace_h[(size_t) m * H + e] = v;
-                        }
-                    } else {
-                        v = hd[e];
-                    }
-                    ss[m] += (double) __fmul_rn(v, v);
-                }
-            }
+        }
+        if (base + stride < total) {  // the next pass's reads go out once this one is done
+            load(base + stride, p0, w, n);
         }
     }
 #pragma unroll
@@ -433,7 +449,7 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
             ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], off);
         }
         if (lane == 0) {
-            s.rms_part[warp * 2 + m] = ss[m];
+            s.rms_part[warp * M_T + m] = ss[m];
         }
     }
     named_barrier_sync(1, kStepConsumers);
@@ -443,7 +459,7 @@ __device__ void residual_and_rms(const StepArgs & a, const Smem & s, const unsig
     for (int m = 0; m < M_T; ++m) {
         double tot = 0.0;
         for (int w = 0; w < kStepConsumerWarps; ++w) {
-            tot += s.rms_part[w * 2 + m];
+            tot += s.rms_part[w * M_T + m];
         }
         // dividing by a power of two is multiplying by its exact reciprocal
         const float mean = (float) (s.inv_h != 0.0 ? tot * s.inv_h : tot / (double) H);
@@ -469,12 +485,20 @@ __device__ bool stage_activations_t(const StepArgs & a, const Smem & s, int K, i
     const int     NSB  = K >> 8;
     const int     gb   = lane / LPB;  // block within the warp's BPW
     const int     eb   = lane % LPB;  // values E*eb .. E*eb+E-1 of the block
-    for (int m = 0; m < M; ++m)
-    for (int base = warp * BPW; base < NB; base += kStepConsumerWarps * BPW) {
-        const int   b     = base + gb;
-        const bool  valid = b < NB;
-        const int   i0    = (valid ? b : 0) * kQK + eb * E;
-        const float sc    = scale[m < M_T ? m : 0];
+    // the M tokens' blocks are one flat range (token m's block b is m * NB + b),
+    // so the tokens share the rounds
+    const int     MNB  = M * NB;
+    for (int base = warp * BPW; base < MNB; base += kStepConsumerWarps * BPW) {
+        const int   bf    = base + gb;
+        const bool  valid = bf < MNB;
+        const int   m     = M_T == 1 || !valid ? 0 : bf / NB;
+        const int   b     = valid ? bf - m * NB : 0;
+        const int   i0    = b * kQK + eb * E;
+        float       sc    = scale[0];
+#pragma unroll
+        for (int mm = 1; mm < M_T; ++mm) {
+            sc = m == mm ? scale[mm] : sc;
+        }
         float       v[E];
         // 128-bit loads (both buffers and i0 are 16-byte aligned): a lane's
         // values are 16 bytes apart from its neighbour's, and scalar loads at
@@ -604,16 +628,21 @@ __device__ bool stage_ll_t(const StepArgs & a, const Smem & s, int K, int M, con
     return consumers_any(fail || local_stop(s));
 }
 
-// One round per token whatever K is: 8 lanes per block up to 32*kStepConsumerWarps/8
-// blocks, then 4, then 2.  src_kind 0 stages the normed shared buffer
-// (stage_activations_t), 1 LL words (stage_ll_t; map_gqa: the source holds
-// the kv heads of the GQA expansion).
+// Lanes per block by one token's blocks: 8 up to 4 * kStepConsumerWarps
+// blocks, then 4, then 2; the M tokens' blocks form one flat range taken in
+// as many rounds as it needs (one lane group per block keeps the per-lane
+// chains short: one round of all tokens with fewer lanes per block measured
+// slower).  src_kind 0 stages the normed shared buffer (stage_activations_t),
+// 1 LL words (stage_ll_t; map_gqa: the source holds the kv heads of the GQA
+// expansion).
 template <int M_T, int MODE>
 __device__ bool stage_activations(const StepArgs & a, const Smem & s, int K, int M, int src_kind, const float * hsrc,
                                   const float * norm, const float (&scale)[M_T], const unsigned long long * ll,
                                   size_t ll_stride, bool map_gqa, unsigned epoch, float * trace_x, size_t trace_stride,
                                   uint8_t * xc, float * xd, bool & fail) {
     if (src_kind == 1) {
+        // lanes per block by one token's source blocks: a lane keeps at most 8
+        // words (4 where they fit) pending, further tokens take further rounds
         const int lg_rep = map_gqa ? a.lg_group : 0;
         const int NBs    = (K >> 5) >> lg_rep;
         if (NBs <= kStepConsumerWarps * 4) {
@@ -626,7 +655,7 @@ __device__ bool stage_activations(const StepArgs & a, const Smem & s, int K, int
         }
         return stage_ll_t<M_T, MODE, 2>(a, s, K, M, ll, ll_stride, lg_rep, epoch, trace_x, trace_stride, xc, xd, fail);
     }
-    const int NB = K >> 5;
+    const int NB = K >> 5;  // one token's blocks (further tokens take further rounds)
     if (NB <= kStepConsumerWarps * 4) {
         return stage_activations_t<M_T, MODE, 8>(a, s, K, M, hsrc, norm, scale, trace_x, trace_stride, xc, xd, fail);
     }
@@ -1188,8 +1217,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     s.epoch       = reinterpret_cast<unsigned *>(smem + 256);
     s.abort_local = reinterpret_cast<int *>(smem + 260);
     s.rms_scale   = reinterpret_cast<float *>(smem + 264);
-    s.rms_part    = reinterpret_cast<double *>(smem + 512);
-    s.tok         = reinterpret_cast<AttTok *>(smem + 1024);
+    s.rms_part    = reinterpret_cast<double *>(smem + 1024);
+    s.tok         = reinterpret_cast<AttTok *>(smem + 1024 + 8 * kStepConsumerWarps * 8);
     size_t off    = kStepHeader;
     s.hbuf        = reinterpret_cast<float *>(smem + off);
     off += (size_t) M_T * H * 4;
@@ -1640,8 +1669,13 @@ size_t decode_step_smem_bytes(const StepArgs & a, int mt, int & n_slots) {
     return off + (size_t) n_slots * kStepSlotBytes;
 }
 
+// Token slots of the kernel instance that runs M tokens: 1, 2, 4 or 8.
+int step_mt(int M) {
+    return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
+}
+
 bool decode_step_supported(const StepArgs & a, int G) {
-    if (a.M < 1 || a.M > 2 || a.H % 256 || a.Q % 256 || a.I % 256 || a.KV % 32) {
+    if (a.M < 1 || a.M > (a.attn ? 2 : 8) || a.M > a.ll_m || a.H % 256 || a.Q % 256 || a.I % 256 || a.KV % 32) {
         return false;
     }
     if ((1 << a.lg_head_dim) != a.head_dim || (1 << a.lg_group) != a.group) {
@@ -1667,7 +1701,7 @@ bool decode_step_supported(const StepArgs & a, int G) {
         return false;
     }
     int slots = 0;
-    if (decode_step_smem_bytes(a, a.M <= 1 ? 1 : 2, slots) == 0 || slots < 2) {
+    if (decode_step_smem_bytes(a, step_mt(a.M), slots) == 0 || slots < 2) {
         return false;
     }
     // consume_op holds all tiles of one op at once: they must fit the ring
@@ -1687,47 +1721,54 @@ bool decode_step_supported(const StepArgs & a, int G) {
 namespace {
 using StepFn = void (*)(const StepArgs);
 
-template <bool ATTN>
-StepFn pick_step_kernel_t(int mode, int mt) {
-    switch (mode) {
-        case B200Q8_QUANT_CPU_X86:
-            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_X86, ATTN>
-                           : decode_step_kernel<2, B200Q8_QUANT_CPU_X86, ATTN>;
-        case B200Q8_QUANT_CPU_ARM:
-            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_CPU_ARM, ATTN>
-                           : decode_step_kernel<2, B200Q8_QUANT_CPU_ARM, ATTN>;
-        default:
-            return mt == 1 ? decode_step_kernel<1, B200Q8_QUANT_REF, ATTN> : decode_step_kernel<2, B200Q8_QUANT_REF, ATTN>;
+template <int MODE>
+StepFn pick_step_kernel_m(int mt, bool attn) {
+    if (attn) {  // attention steps take at most 2 tokens
+        return mt == 1 ? decode_step_kernel<1, MODE, true> : decode_step_kernel<2, MODE, true>;
+    }
+    switch (mt) {
+        case 1: return decode_step_kernel<1, MODE, false>;
+        case 2: return decode_step_kernel<2, MODE, false>;
+        case 4: return decode_step_kernel<4, MODE, false>;
+        default: return decode_step_kernel<8, MODE, false>;
     }
 }
 
 StepFn pick_step_kernel(int mode, int mt, bool attn) {
-    return attn ? pick_step_kernel_t<true>(mode, mt) : pick_step_kernel_t<false>(mode, mt);
+    switch (mode) {
+        case B200Q8_QUANT_CPU_X86: return pick_step_kernel_m<B200Q8_QUANT_CPU_X86>(mt, attn);
+        case B200Q8_QUANT_CPU_ARM: return pick_step_kernel_m<B200Q8_QUANT_CPU_ARM>(mt, attn);
+        default: return pick_step_kernel_m<B200Q8_QUANT_REF>(mt, attn);
+    }
 }
 }  // namespace
 
-// True when one CTA of the step kernel fits on an SM with its shared memory
-// (the cooperative launch needs every CTA resident at once).
-bool decode_step_fits(const StepArgs & a) {
-    for (int mt = 1; mt <= 2; ++mt) {
+// The largest M (0, 1, 2, 4 or 8) up to which one CTA of the step kernel fits
+// on an SM with its shared memory (the cooperative launch needs every CTA
+// resident at once); attention steps stop at 2.
+int decode_step_max_m(const StepArgs & a) {
+    int best = 0;
+    for (int mt = 1; mt <= (a.attn ? 2 : 8); mt *= 2) {
         int          slots = 0;
         const size_t smem  = decode_step_smem_bytes(a, mt, slots);
         StepFn       fn    = pick_step_kernel(a.mode, mt, a.attn != 0);
-        if (smem == 0 || cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess) {
+        if (smem == 0 || slots < 2 ||
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess) {
             cudaGetLastError();
-            return false;
+            break;
         }
         int blocks = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, kStepThreads, smem) != cudaSuccess || blocks < 1) {
             cudaGetLastError();
-            return false;
+            break;
         }
+        best = mt;
     }
-    return true;
+    return best;
 }
 
 cudaError_t launch_decode_step(StepArgs a, int G, cudaStream_t stream) {
-    const int mt   = a.M <= 1 ? 1 : 2;
+    const int mt   = step_mt(a.M);
     int       slots = 0;
     const size_t smem = decode_step_smem_bytes(a, mt, slots);
     a.n_slots         = slots;

@@ -184,7 +184,7 @@ struct StepArgs {
 };
 
 bool        decode_step_supported(const StepArgs & a, int grid);
-bool        decode_step_fits(const StepArgs & a);
+int         decode_step_max_m(const StepArgs & a);
 size_t      decode_step_smem_bytes(const StepArgs & a, int mt, int & n_slots);
 cudaError_t launch_decode_step(StepArgs a, int grid, cudaStream_t stream);
 

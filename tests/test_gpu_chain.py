@@ -58,7 +58,7 @@ def check_mm(O, wq, k, x, y):
 
 
 def make_chain(chain_mod, layers, t_table, path, **kw):
-    """path 'persistent': the single-launch step (M <= 2); 'per_op': the graph of per-op GEMVs."""
+    """path 'persistent': the single-launch step (M <= 8); 'per_op': the graph of per-op GEMVs."""
     import os
 
     old = os.environ.get("B200Q8_CHAIN_PER_OP")
@@ -73,7 +73,8 @@ def make_chain(chain_mod, layers, t_table, path, **kw):
             os.environ["B200Q8_CHAIN_PER_OP"] = old
 
 
-@pytest.mark.parametrize("m,path", [(1, "persistent"), (2, "persistent"), (1, "per_op"), (2, "per_op"),
+@pytest.mark.parametrize("m,path", [(1, "persistent"), (2, "persistent"), (3, "persistent"), (4, "persistent"),
+                                    (5, "persistent"), (8, "persistent"), (1, "per_op"), (2, "per_op"),
                                     (8, "per_op"), (9, "per_op"), (64, "per_op")])
 def test_chain_per_op(chain_mod, O, dev, m, path):
     n_layers = 2

@@ -1,6 +1,6 @@
 """The decode step at the BASELINE configurations' own sizes, against the oracle.
 
-* config 2: the 28-layer 0.6B talker step at M = 1 and M = 2 through the single-launch persistent kernel;
+* config 2: the 28-layer 0.6B talker step at M = 1, 2 and 8 through the single-launch persistent kernel;
 * config 3: the same 28 layers at M = 16, 64 and 256 through the tensor-core chain;
 * config 4: the 28-layer 1.7B-shaped step at M = 1 (persistent) and M = 32 (tensor-core chain).
 
@@ -124,7 +124,7 @@ def run_and_check(O, chain_mod, q8, dev, model, d: Dims, m, path, outliers=False
     ch.close()
 
 
-@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("m", [1, 2, 8])
 def test_config2_persistent_28_layers(O, chain_mod, q8, dev, model06, m):
     run_and_check(O, chain_mod, q8, dev, model06, D06, m, "persistent")
 
