@@ -41,7 +41,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b", "gemv", "gemv-large", "mul-mat",
+    ap.add_argument("--workload", default="talker", choices=["talker", "talker-1.7b", "dp-sweep", "pack-1.7b", "gemv", "gemv-large", "mul-mat", "int8-peaks",
                              "frame"],
                     help="talker: BASELINE config 2 (config 3 with --batch 16/64/256); talker-1.7b: config 4 shapes; "
                          "dp-sweep: config 5, 512 streams split over the ranks in M=64 batches (one launch per op); "
@@ -810,6 +810,70 @@ def run_mul_mat(args, rank, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_int8_peaks(args, rank, local_rank):
+    """Measured int8 ceilings of this B200 (libb200q8_peaks.so): tcgen05.mma kind::i8 (128 x 256 x 32 per MMA,
+    one issuing thread per SM, TMEM accumulators), mma.sync m16n8k32 s8 (the legacy tensor path the Q8_0 GEMM
+    uses) and the per-block fp32 rescale a Q8_0 GEMM does on the CUDA cores after every K = 32 block, as
+    int8-op-equivalent rates.  The tcgen05 MMA is first checked on known operands against exact int32 products."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    import __graft_entry__ as g
+
+    g.load_package()
+    from synthesize_cpp_b200 import build
+
+    if rank != 0:
+        return
+    torch.cuda.set_device(local_rank)
+    L = ctypes.CDLL(build.PEAKS_LIB)
+    L.b200q8p_tcgen05_check.argtypes = [ctypes.c_void_p]
+    L.b200q8p_run.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]
+    out = np.empty((128, 256), np.int32)
+    rc = L.b200q8p_tcgen05_check(out.ctypes.data)
+    a = (np.arange(128)[:, None] % 7 - 3) * np.ones((1, 32), np.int64)
+    b = (np.arange(256)[:, None] + 2 * np.arange(32)[None, :]) % 5 - 2
+    want = (a @ b.T).astype(np.int32)
+    if rc != 0 or not np.array_equal(out, want):
+        raise RuntimeError(f"tcgen05 kind::i8 check failed (rc {rc}, {int((out != want).sum())} of 32768 differ)")
+    sms = torch.cuda.get_device_properties(local_rank).multi_processor_count
+    peaks, peak_kind = measured_peaks()
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    time.sleep(0.3)
+    res = {}
+    # (kind, iters per launch, int8 ops per launch)
+    plan = {"tcgen05_kind_i8": (0, 8192, lambda it: sms * it * 2 * 128 * 256 * 32),
+            "mma_sync_m16n8k32_s8": (1, 8192, lambda it: sms * 8 * it * 8 * 2 * 16 * 8 * 32),
+            "q8_0_block_rescale_fp32": (2, 8192, lambda it: sms * 256 * it * 16 * 64)}
+    for name, (kind, iters, ops) in plan.items():
+        ms = ctypes.c_float()
+        rc = L.b200q8p_run(kind, sms, iters, max(3, args.steps), ctypes.byref(ms))
+        if rc != 0:
+            raise RuntimeError(f"{name}: rc {rc}")
+        res[name] = {"tops": ops(iters) / (ms.value * 1e-3) / 1e12, "ms_per_launch": ms.value, "iters": iters}
+    clocks = sampler.stop()
+    t = res["tcgen05_kind_i8"]["tops"]
+    line = {
+        "metric": "int8 tensor ceilings and the Q8_0 per-block rescale bound (TOPS)", "value": t, "unit": "TOPS",
+        "n_gpus": 1, "steps": max(3, args.steps), "warmup": 1,
+        "ms_per_step": res["tcgen05_kind_i8"]["ms_per_launch"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "s8 x s8 -> s32; fp32 rescale", "data": "synthetic register/shared operands",
+        "config": {"workload": f"int8 peaks, one CTA per SM ({sms} SMs)",
+                   "tcgen05": "M=128 N=256 K=32 kind::i8, one elected thread, two TMEM accumulators",
+                   "mma_sync": "8 warps x 8 independent m16n8k32 s8 chains",
+                   "rescale": "per 2 block-outputs: fadd2 (bias) + fmul2 (dw*dx) + ffma2; 64 int8 ops each"},
+        "peaks": res,
+        "tcgen05_check": "one MMA on known operands equals the exact int32 products",
+        "bf16_tflops_measured": peaks.get("bf16_tflops"), "peak_source": peak_kind,
+        "gpu_launches": 3 * (max(3, args.steps) + 1) + 1,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -820,6 +884,9 @@ def main():
         return
     if args.workload == "pack-1.7b":
         run_pack(args, rank, local_rank)
+        return
+    if args.workload == "int8-peaks":
+        run_int8_peaks(args, rank, local_rank)
         return
     if args.workload in ("gemv", "gemv-large", "mul-mat"):
         run_mul_mat(args, rank, local_rank)

@@ -6,6 +6,9 @@
                        (include/b200q8_host.h) over that ABI (host/*.cpp)
     synth_b200_frames  the command-line frame driver (host/cli/), over
                        libb200q8_host.so
+    libb200q8_peaks.so measured int8 ceilings (peaks/): tcgen05 kind::i8,
+                       mma.sync s8 and the per-block fp32 rescale (bench.py
+                       --workload int8-peaks); not on the product path
 
 Both are written next to this file so they travel with the source tree.
 """
@@ -22,6 +25,7 @@ HOST = os.path.join(PKG, "host")
 LIB = os.path.join(PKG, "libb200q8.so")
 HOST_LIB = os.path.join(PKG, "libb200q8_host.so")
 CLI = os.path.join(PKG, "synth_b200_frames")
+PEAKS_LIB = os.path.join(PKG, "libb200q8_peaks.so")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -63,6 +67,11 @@ def build(force: bool = False, verbose: bool = False) -> list[str]:
             cmd.insert(1, "-Xptxas=-v")
         subprocess.run(cmd, check=True)
     out = [LIB]
+    peaks_src = os.path.join(PKG, "peaks", "int8_peaks.cu")
+    if os.path.exists(peaks_src):
+        if force or _stale(PEAKS_LIB, [peaks_src] + _sources(CSRC, (".cuh",)) + _sources(include, (".h",))):
+            subprocess.run([_nvcc(), *NVCC_FLAGS, "-o", PEAKS_LIB, peaks_src], check=True)
+        out.append(PEAKS_LIB)
     host_srcs = _sources(HOST, (".cpp",))
     cuda = _cuda_home()
     cuda_flags = [f"-I{os.path.join(cuda, 'include')}"]
