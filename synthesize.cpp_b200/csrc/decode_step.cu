@@ -805,6 +805,7 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
     const int      gpw    = 32 >> o.lgs;  // groups per warp
     const int      ngroup = kStepConsumerWarps * gpw;
     const int      gl     = lane & (GS - 1);
+    const bool     split  = pair_units && o.lgs <= 4;  // two groups of a pair unit fit one warp
     const uint32_t xc_s   = smem_addr(xc);
     const uint32_t xd_s   = smem_addr(xd);
     const uint32_t ring_s = smem_addr(s.ring);
@@ -839,35 +840,81 @@ __device__ __forceinline__ void consume_op(const StepArgs & a, const Smem & s, i
             }
             return ring_s + (uint32_t) (tile_slot(o.sl0, S, ti) * kStepSlotBytes) + (uint32_t) (r * segs[g].rb);
         };
-        for (int ub = u_lo + warp * gpw; ub < u_hi; ub += ngroup) {  // warp-uniform
-            const int  u      = ub + (lane >> o.lgs);
-            const bool active = u < u_hi;
-            float      acc0[M_T], acc1[M_T];
+        if (split) {
+            // a pair op's two rows of a unit go to two neighbouring lane groups
+            // (gate row: even group, up row: odd group): twice the lanes of one
+            // group per unit, half the work per lane; the up row's sum joins
+            // the gate row's by a shuffle before the publish
+            for (int ub = u_lo + warp * (gpw >> 1); ub < u_hi; ub += ngroup >> 1) {  // warp-uniform
+                const int  u      = ub + (lane >> (o.lgs + 1));
+                const int  seg    = (lane >> o.lgs) & 1;
+                const bool active = u < u_hi;
+                float      acc0[M_T], acc1[M_T];
 #pragma unroll
-            for (int m = 0; m < M_T; ++m) {
-                acc0[m] = 0.0f;
-                acc1[m] = 0.0f;
-            }
-            if (active) {
-                dot_row_half<M_T>(row_addr(0, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc0);
-                if (pair_units) {
-                    dot_row_half<M_T>(row_addr(1, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc1);
+                for (int m = 0; m < M_T; ++m) {
+                    acc0[m] = 0.0f;
                 }
-            }
-            group_reduce<M_T>(acc0, GS);
-            if (pair_units) {
-                group_reduce<M_T>(acc1, GS);
-            }
+                if (active) {
+                    // the segment's fields by select (a runtime index into segs would put it in local memory)
+                    const int    sr = seg ? segs[1].sr : segs[0].sr;
+                    const size_t rb = seg ? segs[1].rb : segs[0].rb;
+                    int          ti = seg ? o.seg1 : 0;
+                    int          r  = u;
+                    while (r >= sr) {
+                        r -= sr;
+                        ++ti;
+                    }
+                    const uint32_t addr =
+                        ring_s + (uint32_t) (tile_slot(o.sl0, S, ti) * kStepSlotBytes) + (uint32_t) (r * rb);
+                    dot_row_half<M_T>(addr, NSB, NB, K, gl, GS, xc_s, xd_s, M, acc0);
+                }
+                group_reduce<M_T>(acc0, GS);
+#pragma unroll
+                for (int m = 0; m < M_T; ++m) {
+                    acc1[m] = __shfl_down_sync(0xffffffffu, acc0[m], GS);
+                }
 #ifdef B200Q8_TIMELINE
-            const long long tp0 = clock64();
+                const long long tp0 = clock64();
 #endif
-            if (active && gl == 0) {
-                publish(u, acc0, acc1);
-            }
+                if (active && seg == 0 && gl == 0) {
+                    publish(u, acc0, acc1);
+                }
 #ifdef B200Q8_TIMELINE
-            __syncwarp();
-            tc_pub += clock64() - tp0;
+                __syncwarp();
+                tc_pub += clock64() - tp0;
 #endif
+            }
+        } else {
+            for (int ub = u_lo + warp * gpw; ub < u_hi; ub += ngroup) {  // warp-uniform
+                const int  u      = ub + (lane >> o.lgs);
+                const bool active = u < u_hi;
+                float      acc0[M_T], acc1[M_T];
+#pragma unroll
+                for (int m = 0; m < M_T; ++m) {
+                    acc0[m] = 0.0f;
+                    acc1[m] = 0.0f;
+                }
+                if (active) {
+                    dot_row_half<M_T>(row_addr(0, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc0);
+                    if (pair_units) {
+                        dot_row_half<M_T>(row_addr(1, u), NSB, NB, K, gl, GS, xc_s, xd_s, M, acc1);
+                    }
+                }
+                group_reduce<M_T>(acc0, GS);
+                if (pair_units) {
+                    group_reduce<M_T>(acc1, GS);
+                }
+#ifdef B200Q8_TIMELINE
+                const long long tp0 = clock64();
+#endif
+                if (active && gl == 0) {
+                    publish(u, acc0, acc1);
+                }
+#ifdef B200Q8_TIMELINE
+                __syncwarp();
+                tc_pub += clock64() - tp0;
+#endif
+            }
         }
         if (k1 >= o.n_r) {
             break;  // the last round: its tiles stay held for release_tiles
