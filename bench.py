@@ -53,7 +53,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=1, help="tokens (streams) per step per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chain", default="auto", choices=["auto", "per-op"],
-                    help="auto: single-launch persistent step for M <= 8; per-op: CUDA graph of per-op kernels")
+                    help="auto: single-launch persistent step for M <= 2, tensor-core GEMM chain from M = 3; "
+                         "per-op: CUDA graph of per-op GEMVs up to M = 8")
     return ap.parse_args()
 
 
@@ -494,7 +495,9 @@ def run_frame(args, rank, local_rank):
     achieved = fbytes / frame_s / 1e9
 
     def chain_launches(layers, mm):
-        return 1 + (6 * layers + 1 if mm <= 8 else 10 * layers + 3)
+        # the persistent step is one launch up to 2 tokens; from 3 on, per layer a stage and a GEMM for each of
+        # qkv, o, gate|up and down plus the attention kernel, then the output stage and head
+        return 1 + (1 if mm <= 2 else 9 * layers + 3)
 
     per_frame = (2 + chain_launches(fs.talker.n_layers, m) + 2 + chain_launches(fs.predictor.n_layers, 2 * m) + 1 +
                  (G - 2) * (chain_launches(fs.predictor.n_layers, m) + 1))
@@ -1015,12 +1018,13 @@ def main():
     step_bytes = config["algorithmic_bytes_per_step"]
     step_flops = config["int8_ops_per_step"]
     achieved = step_bytes / step_s / 1e9
-    persistent = args.chain == "auto" and m_max <= 8
-    per_batch = lambda m: 1 if persistent else (2 + 8 * shape.n_layers if m > 8 else 1 + 4 * shape.n_layers)
+    persistent = args.chain == "auto" and m_max <= 2
+    per_batch = lambda m: (1 if persistent else
+                           2 + 8 * shape.n_layers if m >= 3 and args.chain == "auto" or m > 8 else 1 + 4 * shape.n_layers)
     launches_per_step = sum(per_batch(m) for m in sizes)
     if persistent:
         kernel_name = "decode_step_kernel (the whole step in one persistent launch)"
-    elif m_max > 8:
+    elif m_max > 8 or args.chain == "auto":
         kernel_name = "gemm_q8_0_kernel + stage_rows_kernel (int8 mma.sync GEMM per op, CUDA graph + PDL)"
     else:
         kernel_name = "gemv_q8_0_kernel (every launch of the step; 1 + 4*layers launches)"

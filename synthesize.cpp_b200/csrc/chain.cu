@@ -37,6 +37,13 @@ int             current_sm_count();
 
 namespace {
 
+// From this many tokens on a step runs as the per-op int8 tensor-core GEMM
+// chain: its MMAs take 8 tokens at once, so 3 to 8 tokens cost about what 8
+// do (0.755 ms per 28-layer step at M = 4 and at M = 8 on B200, against
+// 0.566 ms for the persistent step at M = 2 and 0.97 / 1.88 ms for a
+// persistent step of 4 / 8 tokens).
+constexpr int64_t kBatchedMinM = 3;
+
 // h = x_in + get_rows(table, ids); a NULL ids or x_in drops that term (the
 // other is copied exactly).
 __global__ void embed_add_kernel(const uint8_t * __restrict__ table, size_t table_stride, int64_t table_rows,
@@ -89,7 +96,7 @@ struct b200q8_chain {
     float *                      h0           = nullptr;
     cudaStream_t                 cap_stream   = nullptr;
     int                          sms          = 148;
-    // persistent single-launch step (M <= 8; M <= 2 with attention)
+    // persistent single-launch step (M <= 2)
     StepLayerDev *               step_layers  = nullptr;  // device array
     unsigned long long *         ll           = nullptr;
     size_t                       ll_layer     = 0;
@@ -206,7 +213,7 @@ const uint8_t * contiguous(b200q8_chain * c, const void * a, size_t a_bytes, con
 // The persistent single-launch step's arguments for io; false when the step
 // cannot run it (M > 2, a shape or head it does not support, or disabled).
 bool persistent_args(b200q8_chain * c, const StepIO & io, StepArgs & a) {
-    if (!c->persistent || io.M > c->persistent_max_m) {
+    if (!c->persistent || io.M > c->persistent_max_m || (io.M >= kBatchedMinM && c->planes != nullptr)) {
         return false;
     }
     const b200q8_chain_desc & d = c->d;
@@ -240,7 +247,7 @@ bool persistent_args(b200q8_chain * c, const StepIO & io, StepArgs & a) {
     return decode_step_supported(a, c->sms);
 }
 
-// M > 8: per op, a per-token prologue kernel (norm / GQA / SwiGLU + residual,
+// M >= kBatchedMinM: per op, a per-token prologue kernel (norm / GQA / SwiGLU + residual,
 // quantized into code and scale planes) then the int8 tensor-core GEMM;
 // 2 launches per op with programmatic dependent launch between them.
 cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, const StepIO & io) {
@@ -331,7 +338,7 @@ cudaError_t enqueue_step(b200q8_chain * c, cudaStream_t st, const StepIO & io) {
             return e;
         }
     }
-    if (M > 8 && c->planes != nullptr) {
+    if (M >= kBatchedMinM && c->planes != nullptr) {
         return enqueue_step_batched(c, st, io);
     }
     for (int64_t m0 = 0; m0 < M; m0 += 8) {
@@ -587,7 +594,7 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
             e         = cudaMemset(p, 0, (2 * hm + vm) * sizeof(float));
         }
     }
-    bool batched_ok = d.max_m > 8 && d.head_dim % 4 == 0;
+    bool batched_ok = d.max_m >= kBatchedMinM && d.head_dim % 4 == 0;
     for (int i = 0; i < c->n_heads && batched_ok; ++i) {
         batched_ok = gemm_supported(c->heads[i], c->rb_h, H, c->vocab, d.max_m);
     }
@@ -624,7 +631,7 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
             c->attn_count   = static_cast<unsigned *>(p4);
         }
     }
-    // persistent step (M <= 8, or 2 with attention): per-layer weight table, LL hand-off words,
+    // persistent step (M <= 2): per-layer weight table, LL hand-off words,
     // sync words
     const char * per_op = getenv("B200Q8_CHAIN_PER_OP");
     if (e == cudaSuccess && !(per_op && per_op[0] == '1')) {
@@ -634,8 +641,8 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
                                c->layers[l].norm_in, c->layers[l].norm_post,
                                c->attn ? c->q_norm[l] : nullptr, c->attn ? c->k_norm[l] : nullptr };
         }
-        // hand-off words for up to 8 tokens (2 with attention)
-        c->ll_m      = c->attn ? 2 : (int) std::min<int64_t>(8, std::max<int64_t>(2, d.max_m));
+        // hand-off words for the persistent step's 2 tokens
+        c->ll_m      = 2;
         c->ll_layer  = (size_t) c->ll_m * (c->qkv_dim + Q + H + I + H);
         void * p1 = nullptr, * p2 = nullptr, * p3 = nullptr;
         e = cudaMalloc(&p1, sizeof(StepLayerDev) * d.n_layers);

@@ -1,5 +1,5 @@
 // decode_step.cu -- the whole talker-shaped decode step as ONE persistent
-// kernel launch (sm_100a), for M <= 8 tokens (M <= 2 with attention).
+// kernel launch (sm_100a), for M <= 2 tokens.
 //
 // Why: at M = 1 the step is 4 * n_layers dependent MUL_MATs of 1-7 MB each.
 // Launched one by one (the reference's GraphRun per step, or a CUDA graph of
@@ -50,6 +50,12 @@ constexpr int kStepSlotBytes     = 16384;
 constexpr int kStepMaxSlots      = 16;
 constexpr int kStepYMax          = 64;  // rows one CTA produces in one op (per token)
 constexpr int kStepHeader        = 2048;
+// Tokens per launch.  The kernel's token loops are written for any M_T (the
+// tokens' elements and blocks are flat ranges), and it was measured with 4
+// and 8 token slots: 0.968 / 1.880 ms per step at M = 4 / 8, against 0.755 /
+// 0.757 ms for the per-op tensor-core GEMM chain, whose MMAs take 8 tokens at
+// once.  From M = 3 on the chain runs that path, and the step keeps 1 and 2.
+constexpr int kStepMaxM          = 2;
 
 __device__ __forceinline__ unsigned long long ld_ll(const unsigned long long * p) {
     unsigned long long v;
@@ -1716,13 +1722,13 @@ size_t decode_step_smem_bytes(const StepArgs & a, int mt, int & n_slots) {
     return off + (size_t) n_slots * kStepSlotBytes;
 }
 
-// Token slots of the kernel instance that runs M tokens: 1, 2, 4 or 8.
+// Token slots of the kernel instance that runs M tokens (1 or 2).
 int step_mt(int M) {
-    return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
+    return M <= 1 ? 1 : 2;
 }
 
 bool decode_step_supported(const StepArgs & a, int G) {
-    if (a.M < 1 || a.M > (a.attn ? 2 : 8) || a.M > a.ll_m || a.H % 256 || a.Q % 256 || a.I % 256 || a.KV % 32) {
+    if (a.M < 1 || a.M > kStepMaxM || a.M > a.ll_m || a.H % 256 || a.Q % 256 || a.I % 256 || a.KV % 32) {
         return false;
     }
     if ((1 << a.lg_head_dim) != a.head_dim || (1 << a.lg_group) != a.group) {
@@ -1770,15 +1776,10 @@ using StepFn = void (*)(const StepArgs);
 
 template <int MODE>
 StepFn pick_step_kernel_m(int mt, bool attn) {
-    if (attn) {  // attention steps take at most 2 tokens
+    if (attn) {
         return mt == 1 ? decode_step_kernel<1, MODE, true> : decode_step_kernel<2, MODE, true>;
     }
-    switch (mt) {
-        case 1: return decode_step_kernel<1, MODE, false>;
-        case 2: return decode_step_kernel<2, MODE, false>;
-        case 4: return decode_step_kernel<4, MODE, false>;
-        default: return decode_step_kernel<8, MODE, false>;
-    }
+    return mt == 1 ? decode_step_kernel<1, MODE, false> : decode_step_kernel<2, MODE, false>;
 }
 
 StepFn pick_step_kernel(int mode, int mt, bool attn) {
@@ -1790,12 +1791,12 @@ StepFn pick_step_kernel(int mode, int mt, bool attn) {
 }
 }  // namespace
 
-// The largest M (0, 1, 2, 4 or 8) up to which one CTA of the step kernel fits
-// on an SM with its shared memory (the cooperative launch needs every CTA
-// resident at once); attention steps stop at 2.
+// The largest M (0, 1 or 2) up to which one CTA of the step kernel fits on an
+// SM with its shared memory (the cooperative launch needs every CTA resident
+// at once).
 int decode_step_max_m(const StepArgs & a) {
     int best = 0;
-    for (int mt = 1; mt <= (a.attn ? 2 : 8); mt *= 2) {
+    for (int mt = 1; mt <= kStepMaxM; mt *= 2) {
         int          slots = 0;
         const size_t smem  = decode_step_smem_bytes(a, mt, slots);
         StepFn       fn    = pick_step_kernel(a.mode, mt, a.attn != 0);

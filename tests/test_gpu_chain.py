@@ -58,7 +58,8 @@ def check_mm(O, wq, k, x, y):
 
 
 def make_chain(chain_mod, layers, t_table, path, **kw):
-    """path 'persistent': the single-launch step (M <= 8); 'per_op': the graph of per-op GEMVs."""
+    """path 'persistent' / 'auto': the chain's own choice (the single-launch step for M <= 2, the tensor-core GEMM
+    chain from M = 3); 'per_op': the graph of per-op GEMVs (M <= 8) or GEMMs."""
     import os
 
     old = os.environ.get("B200Q8_CHAIN_PER_OP")
@@ -73,9 +74,9 @@ def make_chain(chain_mod, layers, t_table, path, **kw):
             os.environ["B200Q8_CHAIN_PER_OP"] = old
 
 
-@pytest.mark.parametrize("m,path", [(1, "persistent"), (2, "persistent"), (3, "persistent"), (4, "persistent"),
-                                    (5, "persistent"), (8, "persistent"), (1, "per_op"), (2, "per_op"),
-                                    (8, "per_op"), (9, "per_op"), (64, "per_op")])
+@pytest.mark.parametrize("m,path", [(1, "persistent"), (2, "persistent"), (3, "auto"), (4, "auto"), (5, "auto"),
+                                    (8, "auto"), (1, "per_op"), (2, "per_op"), (8, "per_op"), (9, "per_op"),
+                                    (64, "per_op")])
 def test_chain_per_op(chain_mod, O, dev, m, path):
     n_layers = 2
     mats, norms, table = make_model(O, n_layers)

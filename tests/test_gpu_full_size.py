@@ -1,6 +1,7 @@
 """The decode step at the BASELINE configurations' own sizes, against the oracle.
 
-* config 2: the 28-layer 0.6B talker step at M = 1, 2 and 8 through the single-launch persistent kernel;
+* config 2: the 28-layer 0.6B talker step at M = 1 and 2 (single-launch persistent kernel) and 8 (tensor-core
+  chain, the chain's own choice from M = 3);
 * config 3: the same 28 layers at M = 16, 64 and 256 through the tensor-core chain;
 * config 4: the 28-layer 1.7B-shaped step at M = 1 (persistent) and M = 32 (tensor-core chain).
 
@@ -125,8 +126,8 @@ def run_and_check(O, chain_mod, q8, dev, model, d: Dims, m, path, outliers=False
 
 
 @pytest.mark.parametrize("m", [1, 2, 8])
-def test_config2_persistent_28_layers(O, chain_mod, q8, dev, model06, m):
-    run_and_check(O, chain_mod, q8, dev, model06, D06, m, "persistent")
+def test_config2_28_layers(O, chain_mod, q8, dev, model06, m):
+    run_and_check(O, chain_mod, q8, dev, model06, D06, m, "auto")
 
 
 @pytest.mark.parametrize("m", [16, 64, 256])
