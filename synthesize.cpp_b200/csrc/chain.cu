@@ -106,7 +106,8 @@ struct b200q8_chain {
     int                          ll_m         = 2;      // token stride of the hand-off words
     bool                         persistent_in_graph = true;  // cleared if a graph cannot hold its launch
     void *                       timeline     = nullptr;  // B200Q8_TIMELINE analysis builds only
-    void *                       planes       = nullptr;  // batched path (M > 8): GEMM code/scale planes
+    void *                       planes       = nullptr;  // batched path (M >= kBatchedMinM): GEMM code/scale planes
+    GemmSplit                    split        = {};       // batched path: split-K partials and counters
     // attention with a KV cache (desc.attention != nullptr)
     bool                         attn         = false;
     b200q8_attention_desc        ad           = {};
@@ -286,7 +287,8 @@ cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, const StepIO
                                   (int) Q, hd, grp, B(l, kAttn), (size_t) Q, M, d.mode, xrec, st, true);
         }
         if (e == cudaSuccess)
-            e = launch_gemm_staged(c->w_o[l], c->rb_q, Q, H, xrec, M, B(l, kO), (size_t) H, st, c->sms, true);
+            e = launch_gemm_staged(c->w_o[l], c->rb_q, Q, H, xrec, M, B(l, kO), (size_t) H, st, c->sms, true,
+                                   &c->split);
         // gate|up: n2 = rms_norm(h1) * norm_post with h1 = h + o
         if (e == cudaSuccess)
             e = launch_stage_rows(0, h_in, B(l, kO), (size_t) H, B(l, kH1), (size_t) H, c->layers[l].norm_post, d.eps,
@@ -300,7 +302,7 @@ cudaError_t enqueue_step_batched(b200q8_chain * c, cudaStream_t st, const StepIO
                                   grp, B(l, kS), (size_t) I, M, d.mode, xrec, st, true);
         if (e == cudaSuccess)
             e = launch_gemm_staged(c->w_d[l], c->rb_i, I, H, xrec, M, B(l, kDown), (size_t) H, st, c->sms,
-                                   true);
+                                   true, &c->split);
     }
     if (e == cudaSuccess) {
         const int L = d.n_layers - 1;
@@ -610,6 +612,17 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
         if (e == cudaSuccess) {
             c->owned.push_back(p);
             c->planes = p;
+        }
+        // split-K room for the ops whose row blocks leave SMs idle (o and
+        // down: N = hidden); up to 4 splits of any op of this width
+        const size_t part = 4 * (size_t) d.max_m * (size_t) std::max(H, Q);
+        void *       q    = nullptr;
+        if (e == cudaSuccess) e = cudaMalloc(&q, part * sizeof(float) + (size_t) c->sms * sizeof(unsigned));
+        if (e == cudaSuccess) {
+            c->owned.push_back(q);
+            e = cudaMemset(q, 0, part * sizeof(float) + (size_t) c->sms * sizeof(unsigned));
+            c->split = { static_cast<float *>(q), part, reinterpret_cast<unsigned *>(static_cast<float *>(q) + part),
+                         (size_t) c->sms };
         }
     }
     if (e == cudaSuccess && c->attn) {

@@ -21,7 +21,11 @@
 // and every byte is loaded once per unit.  Eight consumer warps
 // split the unit into 16-row tiles x block subsets of the chunk; partial sums
 // over K are combined through shared memory in a fixed order, so results are
-// deterministic.  Copies are never multicast.
+// deterministic.  When the units of a small-M call leave SMs idle, and the
+// caller gives room for it, a unit takes only a range of the K chunks
+// (split-K): its partial sums go through L2 and the last of a block's splits
+// to finish adds them in split order, again independent of arrival order.
+// Copies are never multicast.
 #include "common.cuh"
 #include "kernels.h"
 #include "mma_tile.cuh"
@@ -43,6 +47,7 @@ constexpr int   kChunkRowBytes     = kChunkBlocks * kBlockBytes;  // 272: one we
 constexpr int   kRecTokenBytes     = kChunkBlocks * kQK + kChunkBlocks * 4;  // 288: codes + scales
 constexpr int   kMaxTokenChunk     = 64;
 constexpr int   kGemmMaxM          = 65536;  // tokens per call (chunks of <= 64)
+constexpr int   kGemmSplitMaxTG    = 2;      // split-K only for token chunks of <= 16
 
 // 2-D tiled TMA load of the box at (x, y) of `map` into this CTA's shared
 // memory (128-byte aligned), completing on `bar`.  x counts 2-byte elements
@@ -104,13 +109,24 @@ struct GemmArgs {
     int             n_tc;      // token chunks
     int             rb;        // weight rows per unit (16, 32, 64 or 128)
     int             n_rb;      // row blocks = ceil(N / rb)
-    int             n_units;   // n_tc * n_rb
+    int             n_units;   // n_tc * n_rb * ksplit
     int             n_slots;
     int             tl_slot;   // timeline builds only
+    // split-K (ksplit > 1): unit u takes K chunks [kz * kc_n, (kz + 1) * kc_n)
+    // of its rows and tokens; partial sums go to part [ksplit][M][N], and the
+    // last of a (tokens, rows) block's ksplit units to finish (counted in
+    // cnt[tc * n_rb + rb], which it sets back to 0) adds the partials in split
+    // order 0, 1, ... and writes y, so results do not depend on arrival order.
+    int             ksplit;
+    int             kc_n;      // K chunks per unit
+    float *         part;
+    unsigned *      cnt;
 };
 
-// TG: token groups of 8 in a token chunk (tm = 8 * TG).
-template <int TG>
+// TG: token groups of 8 in a token chunk (tm = 8 * TG); SPLITK: the
+// instance can split K (it does when a.ksplit > 1).  Only the small token
+// chunks that use split-K carry its code.
+template <int TG, bool SPLITK>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_q8_0_kernel(const GemmArgs a, const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -149,14 +165,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint64_t wpol     = a.n_tc == 1 ? l2_evict_first_policy() : l2_evict_last_policy();
         const uint64_t xpol     = l2_evict_last_policy();
         const int      my_units = (a.n_units - (int) blockIdx.x + G - 1) / G;
-        const int      total    = my_units * n_kc;
-        // fill i = chunk kc of the CTA's unit i / n_kc; it uses slot i % S
+        const int      kc_n     = SPLITK ? a.kc_n : n_kc;
+        const int      total    = my_units * kc_n;
+        // fill i = the (i % kc_n)-th chunk of the CTA's unit i / kc_n; it uses slot i % S
         auto issue_w = [&](int i, int si) {
-            const int ui = i / n_kc;
-            const int kc = i - ui * n_kc;
+            const int ui = i / kc_n;
             const int u  = (int) blockIdx.x + ui * G;
-            const int tc = u / a.n_rb;
-            const int r0 = (u - tc * a.n_rb) * a.rb;
+            const int kz = SPLITK ? u / (a.n_tc * a.n_rb) : 0;
+            const int ut = u - kz * (a.n_tc * a.n_rb);
+            const int kc = kz * kc_n + (i - ui * kc_n);
+            const int tc = ut / a.n_rb;
+            const int r0 = (ut - tc * a.n_rb) * a.rb;
             if (lane == 0) {
                 // the box counts in full, rows past N included (they read as 0)
                 mbar_arrive_expect_tx(&full[si], (uint32_t) (w_bytes + rec_bytes));
@@ -164,9 +183,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
         };
         auto issue_x = [&](int i, int si) {
-            const int ui = i / n_kc;
-            const int kc = i - ui * n_kc;
-            const int tc = ((int) blockIdx.x + ui * G) / a.n_rb;
+            const int ui = i / kc_n;
+            const int u  = (int) blockIdx.x + ui * G;
+            const int kz = SPLITK ? u / (a.n_tc * a.n_rb) : 0;
+            const int kc = kz * kc_n + (i - ui * kc_n);
+            const int tc = (u - kz * (a.n_tc * a.n_rb)) / a.n_rb;
             if (lane == 0) {
                 bulk_copy_g2s(ring + (size_t) si * slot + w_bytes, a.xrec + ((size_t) tc * n_kc + kc) * rec_bytes,
                               (uint32_t) rec_bytes, &full[si], xpol);
@@ -244,9 +265,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     bool     fail = false;
     // Every consumer warp runs the same trip counts and reaches the same
     // barriers whatever happens; a failed wait only skips work.
+    // split-K: set when this CTA finished a block's last split
+    volatile unsigned * last_s = reinterpret_cast<volatile unsigned *>(smem + 2 * kGemmMaxSlots * 8 + 4);
+    const int           kc_n   = SPLITK ? a.kc_n : n_kc;
+    const bool          split  = SPLITK && a.ksplit > 1;
     for (int u = blockIdx.x; u < a.n_units; u += G) {
-        const int tc   = u / a.n_rb;
-        const int r0   = (u - tc * a.n_rb) * a.rb;
+        const int kz   = SPLITK ? u / (a.n_tc * a.n_rb) : 0;
+        const int ut   = u - kz * (a.n_tc * a.n_rb);
+        const int tc   = ut / a.n_rb;
+        const int r0   = (ut - tc * a.n_rb) * a.rb;
         const int rows = min(a.rb, a.N - r0);
         const int tok0 = tc * a.tm;
         float2    acc[TG][2];
@@ -255,7 +282,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             acc[i][0] = make_float2(0.0f, 0.0f);
             acc[i][1] = make_float2(0.0f, 0.0f);
         }
-        for (int kc = 0; kc < n_kc; ++kc) {
+        for (int kc = 0; kc < kc_n; ++kc) {
             if (!fail && !mbar_wait_bounded(&full[s], ph)) {
                 record_device_error((unsigned) B200Q8_ERR_DEVICE_TIMEOUT);
                 *abort_flag = 1;
@@ -329,7 +356,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int q = 0; q < 2; ++q) {
                 const int tok = tok0 + c0 + q;
                 if (tok < a.M) {
-                    float * dst = a.y + (size_t) tok * a.y_stride + r0;
+                    // split-K: this unit's partial sums, added up by the block's last split
+                    float * dst = split ? a.part + ((size_t) kz * a.M + tok) * a.N + r0
+                                               : a.y + (size_t) tok * a.y_stride + r0;
                     if (ra < rows) {
                         dst[ra] = q ? v.y : v.x;
                     }
@@ -368,6 +397,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int tg = 0; tg < TG; ++tg) {
                 store(tg, make_float4(acc[tg][0].x, acc[tg][0].y, acc[tg][1].x, acc[tg][1].y));
             }
+        }
+        if (split) {
+            // every consumer's partial stores reach the device before the count
+            __threadfence();
+            named_barrier_sync(1, kGemmConsumerWarps * 32);
+            unsigned * const cnt = a.cnt + (size_t) tc * a.n_rb + (ut - tc * a.n_rb);
+            if (threadIdx.x == 0) {
+                *last_s = atomicAdd(cnt, 1u) == (unsigned) (a.ksplit - 1) ? 1u : 0u;
+                __threadfence();
+            }
+            named_barrier_sync(1, kGemmConsumerWarps * 32);
+            if (*last_s) {
+                // all splits of this (tokens, rows) block have landed: add them in split order
+                // kU elements per thread per pass, their loads issued together
+                constexpr int kU     = 4;
+                constexpr int kT     = kGemmConsumerWarps * 32;
+                const bool    ok     = !fail && *abort_flag == 0;
+                const size_t  plane  = (size_t) a.M * a.N;
+                const int     n_elem = a.tm * a.rb;
+                for (int i0 = threadIdx.x; i0 < n_elem; i0 += kU * kT) {
+                    float  v[kU];
+                    size_t off[kU], yoff[kU];
+                    bool   in[kU];
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) {
+                        const int i   = i0 + q * kT;
+                        const int t   = i / a.rb;
+                        const int r   = i - t * a.rb;
+                        const int tok = tok0 + t;
+                        in[q]         = i < n_elem && tok < a.M && r < rows;
+                        off[q]        = (size_t) tok * a.N + r0 + r;
+                        yoff[q]       = (size_t) tok * a.y_stride + r0 + r;
+                        v[q]          = in[q] ? __ldcg(a.part + off[q]) : 0.0f;
+                    }
+                    for (int k2 = 1; k2 < a.ksplit; ++k2) {
+#pragma unroll
+                        for (int q = 0; q < kU; ++q) {
+                            if (in[q]) {
+                                v[q] += __ldcg(a.part + off[q] + (size_t) k2 * plane);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) {
+                        if (in[q] && ok) {
+                            a.y[yoff[q]] = v[q];
+                        }
+                    }
+                }
+                if (threadIdx.x == 0) {
+                    *cnt = 0u;  // ready for the next launch
+                }
+            }
+            named_barrier_sync(1, kGemmConsumerWarps * 32);
         }
     }
     if (threadIdx.x == 0) GTL(5);
@@ -631,13 +714,13 @@ int gemm_tg(int tm) {
     return tm / 8;
 }
 
-template <int TG>
+template <int TG, bool SPLITK>
 cudaError_t launch_gemm_tg(const GemmArgs & a, const CUtensorMap & wmap, int grid, size_t smem, cudaStream_t stream,
                            bool pdl) {
     const cudaError_t e =
-        cudaFuncSetAttribute(gemm_q8_0_kernel<TG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        cudaFuncSetAttribute(gemm_q8_0_kernel<TG, SPLITK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     return e != cudaSuccess ? e
-                            : launch_pdl(gemm_q8_0_kernel<TG>, dim3((unsigned) grid), dim3(kGemmThreads), smem, stream,
+                            : launch_pdl(gemm_q8_0_kernel<TG, SPLITK>, dim3((unsigned) grid), dim3(kGemmThreads), smem, stream,
                                          pdl, a, wmap);
 }
 
@@ -705,7 +788,8 @@ bool gemm_supported(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, i
 }
 
 cudaError_t launch_gemm_staged(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const uint8_t * xrec,
-                               int64_t M, float * y, size_t y_stride, cudaStream_t stream, int sm_count, bool pdl) {
+                               int64_t M, float * y, size_t y_stride, cudaStream_t stream, int sm_count, bool pdl,
+                               const GemmSplit * split) {
     const GemmChunking c = gemm_chunking(M);
     GemmArgs           a = {};
     a.w                  = w;
@@ -745,6 +829,24 @@ cudaError_t launch_gemm_staged(const uint8_t * w, size_t row_bytes, int64_t K, i
     a.rb             = best_rb;
     a.n_rb           = (int) ((N + a.rb - 1) / a.rb);
     a.n_units        = a.n_tc * a.n_rb;
+    // split-K when the units leave SMs idle: the largest split of the K chunks
+    // (a divisor of them) whose units still fit in one wave, given room for
+    // the partials and the counters.  Only for token chunks of <= 16: on
+    // larger chunks (M = 32 and 64 measured) the partials' round trip through
+    // L2 and the serial combine cost more than the idle SMs.
+    const int n_kc = (int) (K >> 8);
+    a.ksplit       = 1;
+    for (int d = 2; split != nullptr && tg <= kGemmSplitMaxTG && d <= n_kc; ++d) {
+        if (n_kc % d == 0 && (int64_t) a.n_units * d <= sm_count &&
+            (size_t) d * (size_t) M * (size_t) N <= split->part_floats &&
+            (size_t) a.n_units <= split->n_cnt) {
+            a.ksplit = d;
+        }
+    }
+    a.kc_n    = n_kc / a.ksplit;
+    a.part    = a.ksplit > 1 ? split->part : nullptr;
+    a.cnt     = a.ksplit > 1 ? split->cnt : nullptr;
+    a.n_units = a.n_tc * a.n_rb * a.ksplit;
     const size_t slot = gemm_slot_bytes(a.rb, c.tm);
     a.n_slots        = (int) std::min<size_t>(kGemmMaxSlots, ((size_t) kGemmSmemLimit - fixed) / slot);
     if (a.n_slots < 2) {
@@ -756,15 +858,18 @@ cudaError_t launch_gemm_staged(const uint8_t * w, size_t row_bytes, int64_t K, i
     if (!encode_weight_map(&wmap, w, row_bytes, N, a.rb)) {
         return cudaErrorInvalidValue;
     }
+    // TG 1 and 2 run the split-capable instances whether or not this call
+    // splits: measured faster at M <= 16 than the plain ones, for every op
+    static_assert(kGemmSplitMaxTG == 2, "split-capable instances: TG 1 and 2");
     switch (tg) {
-        case 1: return launch_gemm_tg<1>(a, wmap, grid, smem, stream, pdl);
-        case 2: return launch_gemm_tg<2>(a, wmap, grid, smem, stream, pdl);
-        case 3: return launch_gemm_tg<3>(a, wmap, grid, smem, stream, pdl);
-        case 4: return launch_gemm_tg<4>(a, wmap, grid, smem, stream, pdl);
-        case 5: return launch_gemm_tg<5>(a, wmap, grid, smem, stream, pdl);
-        case 6: return launch_gemm_tg<6>(a, wmap, grid, smem, stream, pdl);
-        case 7: return launch_gemm_tg<7>(a, wmap, grid, smem, stream, pdl);
-        case 8: return launch_gemm_tg<8>(a, wmap, grid, smem, stream, pdl);
+        case 1: return launch_gemm_tg<1, true>(a, wmap, grid, smem, stream, pdl);
+        case 2: return launch_gemm_tg<2, true>(a, wmap, grid, smem, stream, pdl);
+        case 3: return launch_gemm_tg<3, false>(a, wmap, grid, smem, stream, pdl);
+        case 4: return launch_gemm_tg<4, false>(a, wmap, grid, smem, stream, pdl);
+        case 5: return launch_gemm_tg<5, false>(a, wmap, grid, smem, stream, pdl);
+        case 6: return launch_gemm_tg<6, false>(a, wmap, grid, smem, stream, pdl);
+        case 7: return launch_gemm_tg<7, false>(a, wmap, grid, smem, stream, pdl);
+        case 8: return launch_gemm_tg<8, false>(a, wmap, grid, smem, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

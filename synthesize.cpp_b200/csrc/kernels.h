@@ -87,8 +87,18 @@ cudaError_t  launch_gemm(const uint8_t * w, size_t row_bytes, int64_t K, int64_t
                          int64_t M, float * y, size_t y_stride, int mode, void * workspace, cudaStream_t stream,
                          int sm_count);
 // The GEMM on activations already staged by launch_stage_rows.
+// Room for split-K partial sums (part, part_floats floats) and per-block
+// arrival counters (cnt, n_cnt words, zero when no launch is running; each
+// launch leaves them zero).  Launches on one split area must be ordered.
+struct GemmSplit {
+    float *    part;
+    size_t     part_floats;
+    unsigned * cnt;
+    size_t     n_cnt;
+};
 cudaError_t  launch_gemm_staged(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const uint8_t * xrec,
-                                int64_t M, float * y, size_t y_stride, cudaStream_t stream, int sm_count, bool pdl);
+                                int64_t M, float * y, size_t y_stride, cudaStream_t stream, int sm_count, bool pdl,
+                                const GemmSplit * split = nullptr);
 // Per-token prologue (one CTA per token): kind 0 = rms_norm(a [+ b]) * norm
 // (a + b also written to sum_out), 1 = GQA expansion of a, 2 = silu(a) * b,
 // 3 = a; the result is quantized into the staged records xrec.
