@@ -243,15 +243,27 @@ static bool small_m_via_gemm(int64_t K, int64_t N, int64_t M) {
     return M >= 1 && M <= 8 && (size_t) N * (size_t) (K / kQK) * kBlockBytes >= gemv_via_gemm_min_bytes();
 }
 
+// Workspace every path but the tcgen05 GEMM can run in: the larger of the
+// general path's quantized activations (M rows of K/32 blocks) and the
+// mma.sync GEMM's staged activation records.
+static size_t base_workspace_size(int64_t K, int64_t N, int64_t M) {
+    const size_t general = align_up((size_t) M * (size_t) (K / kQK) * kBlockBytes, 256);
+    const size_t staged  = K % 256 == 0 ? align_up(gemm_workspace_bytes(K, M), 256) : 0;
+    return M > 8 || small_m_via_gemm(K, N, M) ? std::max(general, staged) : general;
+}
+
+// Shapes the tcgen05 GEMM takes (given aligned pointers), when it is on.
+static bool tc_shape(int64_t K, int64_t N, int64_t M) {
+    const int64_t min_m = gemm_tc_min_m();
+    return min_m > 0 && M >= min_m && M > 8 && K % 256 == 0 && N >= 1;
+}
+
 size_t b200q8_mul_mat_workspace_size(int64_t K, int64_t N, int64_t M) {
     if (K <= 0 || M <= 0 || K % kQK != 0) {
         return 0;
     }
-    // the larger of: quantized activations for the general path (M rows of
-    // K/32 blocks) and the tensor-core path's staged activation records
-    const size_t general = align_up((size_t) M * (size_t) (K / kQK) * kBlockBytes, 256);
-    const size_t staged  = K % 256 == 0 ? align_up(gemm_workspace_bytes(K, M), 256) : 0;
-    return M > 8 || small_m_via_gemm(K, N, M) ? std::max(general, staged) : general;
+    const size_t base = base_workspace_size(K, N, M);
+    return tc_shape(K, N, M) ? std::max(base, align_up(gemm_tc_workspace_bytes(K, N, M), 256)) : base;
 }
 
 b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_row_bytes, const float * x, int64_t M,
@@ -293,8 +305,16 @@ b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_ro
     p.y          = y;
     p.y_stride   = ys;
     p.mode       = mode;
+    // large M, when switched on: the tcgen05 GEMM if the workspace holds its
+    // planes (the workspace size query then asks for them); else the mma.sync
+    // GEMM below
+    if (tc_shape(K, N, M) && gemm_tc_supported(p.w, w_row_bytes, K, N, M, x, xs) && workspace != nullptr &&
+        aligned(workspace, 16) && workspace_bytes >= gemm_tc_workspace_bytes(K, N, M)) {
+        cudaError_t e = launch_gemm_tc(p.w, w_row_bytes, K, N, x, xs, M, y, ys, mode, workspace, st, sms);
+        return e == cudaSuccess ? B200Q8_OK : cuda_error(e, "mul_mat: tcgen05 GEMM launch");
+    }
     if (M > 8 && gemm_supported(p.w, w_row_bytes, K, N, M)) {
-        const size_t need = b200q8_mul_mat_workspace_size(K, N, M);
+        const size_t need = base_workspace_size(K, N, M);
         if (workspace == nullptr || workspace_bytes < need) {
             return set_error(B200Q8_ERR_INVALID_ARG, "mul_mat: M > 8 needs %zu bytes of workspace (got %zu)", need,
                              workspace_bytes);
@@ -320,7 +340,7 @@ b200q8_status_t b200q8_mul_mat(const void * w, int64_t K, int64_t N, size_t w_ro
         return B200Q8_OK;
     }
     // General shapes: quantize x into the workspace, then a plain kernel.
-    const size_t need = b200q8_mul_mat_workspace_size(K, N, M);
+    const size_t need = base_workspace_size(K, N, M);
     if (workspace == nullptr || workspace_bytes < need) {
         return set_error(B200Q8_ERR_INVALID_ARG, "mul_mat: this shape needs %zu bytes of workspace (got %zu)", need,
                          workspace_bytes);

@@ -99,6 +99,17 @@ struct GemmSplit {
 cudaError_t  launch_gemm_staged(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const uint8_t * xrec,
                                 int64_t M, float * y, size_t y_stride, cudaStream_t stream, int sm_count, bool pdl,
                                 const GemmSplit * split = nullptr);
+// Large-M MUL_MAT on the tcgen05 tensor cores (gemm_tc.cu): the weights and
+// the quantized activations as code / scale planes in the workspace, then one
+// persistent kernel over 128-row x 128-token tiles.  gemm_tc_min_m() is 0
+// (off) unless B200Q8_TC_MIN_M sets it.
+int64_t      gemm_tc_min_m();
+bool         gemm_tc_supported(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, int64_t M, const float * x,
+                               size_t x_stride);
+size_t       gemm_tc_workspace_bytes(int64_t K, int64_t N, int64_t M);
+cudaError_t  launch_gemm_tc(const uint8_t * w, size_t row_bytes, int64_t K, int64_t N, const float * x,
+                            size_t x_stride, int64_t M, float * y, size_t y_stride, int mode, void * workspace,
+                            cudaStream_t stream, int sm_count);
 // Per-token prologue (one CTA per token): kind 0 = rms_norm(a [+ b]) * norm
 // (a + b also written to sum_out), 1 = GQA expansion of a, 2 = silu(a) * b,
 // 3 = a; the result is quantized into the staged records xrec.

@@ -3,6 +3,7 @@
 #include "quantize.cu"
 #include "gemv.cu"
 #include "gemm.cu"
+#include "gemm_tc.cu"
 #include "decode_step.cu"
 #include "attention.cu"
 #include "abi.cu"
