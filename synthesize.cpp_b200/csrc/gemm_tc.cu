@@ -5,7 +5,9 @@
 //
 // Two byte passes lay both operands out as planes: int8 codes [rows][K] and
 // fp32 scales [K/32][rows] (the weights' from their Q8_0 rows, the
-// activations' from the same quantizer as every other path).  A persistent
+// activations' from the same quantizer as every other path), and for the
+// activations also -1.5 * 2^23 * dx, which is exact in fp32 (dx is an fp16
+// value: 3 * dx needs 13 significant bits).  A persistent
 // kernel then works on tiles of 128 weight rows x 128 tokens:
 //  * one producer thread loads, per stage of four Q8_0 blocks (128 bytes of
 //    K), each operand's codes as one 2-D TMA box of 128 bytes x 128 rows with
@@ -17,9 +19,11 @@
 //    of the float 1.5 * 2^23 (0x4B400000) before each MMA and the MMA adds
 //    the block's int32 sums to it, so each word reads as 1.5 * 2^23 + sum
 //    exactly (|sum| <= 32 * 128 * 128 < 2^22);
-//  * sixteen epilogue warps read each block's accumulator with tcgen05.ld,
-//    rescale in fp32 on the CUDA cores -- acc += (v - 1.5 * 2^23) * (dw * dx),
-//    three packed f32x2 instructions per pair of outputs, in block order --
+//  * sixteen epilogue warps read each block's accumulator with tcgen05.ld and
+//    rescale in fp32 on the CUDA cores, in block order:
+//    u = fma(v, dx, -1.5 * 2^23 * dx) is (v - 1.5 * 2^23) * dx = sum * dx with
+//    one rounding, then acc = fma(u, dw, acc) -- two packed f32x2
+//    instructions per pair of outputs --
 //    and write the bias back with tcgen05.st, handing the accumulator back to
 //    the MMA thread when the next block starts.
 // The scales change every 32 values of K, so every block's sums are rescaled
@@ -53,7 +57,7 @@ constexpr int kTcEpiCols    = kTcToks * 4 / kTcEpiWarps;
 constexpr int kTcThreads    = (2 + kTcEpiWarps) * 32;
 constexpr int kTcCodeBytes  = 128 * kTcKB * 32;                      // 16 KiB per operand per stage
 constexpr int kTcScaleBytes = kTcKB * 128 * 4;                       // 2 KiB per operand per stage
-constexpr int kTcStageBytes = 2 * kTcCodeBytes + 2 * kTcScaleBytes;  // 36 KiB
+constexpr int kTcStageBytes = 2 * kTcCodeBytes + 3 * kTcScaleBytes;  // 38 KiB: codes, dw, dx, -B * dx
 constexpr int kTcHeader     = 1024;
 constexpr int kTcSmem       = kTcHeader + 1024 + kTcStages * kTcStageBytes;  // + slack to a 1 KiB boundary
 constexpr int kTcMaxK       = 65536;
@@ -176,7 +180,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t * bar, uint32_t parity, const i
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap wc_map,
                    const __grid_constant__ CUtensorMap xc_map, const __grid_constant__ CUtensorMap wd_map,
-                   const __grid_constant__ CUtensorMap xd_map) {
+                   const __grid_constant__ CUtensorMap xd_map, const __grid_constant__ CUtensorMap xn_map) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t * full      = reinterpret_cast<uint64_t *>(smem);  // stage landed (TMA)
     uint64_t * empty     = full + kTcStages;                     // stage read (MMA commit + epilogue warps)
@@ -245,6 +249,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tc_tma_2d(st + kTcCodeBytes, &xc_map, kb0 * 32, t0, &full[s], pol);
                     tc_tma_2d(st + 2 * kTcCodeBytes, &wd_map, n0, kb0, &full[s], pol);
                     tc_tma_2d(st + 2 * kTcCodeBytes + kTcScaleBytes, &xd_map, t0, kb0, &full[s], pol);
+                    tc_tma_2d(st + 2 * kTcCodeBytes + 2 * kTcScaleBytes, &xn_map, t0, kb0, &full[s], pol);
                 }
             }
             // copies still in flight land before the CTA leaves: the last fill of each slot
@@ -309,7 +314,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 mbar_arrive(&tempty[b]);
             }
         }
-        const float2 nbias = make_float2(-12582912.0f, -12582912.0f);  // -(1.5 * 2^23)
         int          ci = 0, bi = 0;
         int          held = -1;  // accumulator re-biased (tcgen05.st issued) but not yet handed back
         bool         ok   = true;
@@ -344,6 +348,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint8_t * st = stages + (size_t) s * kTcStageBytes;
                 const float *   wd = reinterpret_cast<const float *>(st + 2 * kTcCodeBytes);
                 const float *   xd = wd + kTcKB * 128;
+                const float *   xn = xd + kTcKB * 128;
 #pragma unroll 1
                 for (int j = 0; j < kTcKB; ++j, ++bi) {
                     const int b = bi % kTcBufs;
@@ -360,26 +365,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const float    dw  = wd[j * 128 + r];
                     const float2   dw2 = make_float2(dw, dw);
                     const float4 * dx  = reinterpret_cast<const float4 *>(xd + j * 128 + cg * kTcEpiCols);
+                    const float4 * dn  = reinterpret_cast<const float4 *>(xn + j * 128 + cg * kTcEpiCols);
                     // two halves of 16 columns: the scales first, then the accumulator words
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        float4 d[4];
+                        float4 d[4], e[4];
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             d[i] = dx[4 * h + i];
+                            e[i] = dn[4 * h + i];
                         }
                         uint32_t v[16];
                         tc_ld16(tl + b * kTcToks + 16 * h, v);
                         tc_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            const float2 s0 = __fadd2_rn(
-                                make_float2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), nbias);
-                            const float2 s1 = __fadd2_rn(
-                                make_float2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])), nbias);
+                            const float2 u0 = __ffma2_rn(make_float2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
+                                                         make_float2(d[i].x, d[i].y), make_float2(e[i].x, e[i].y));
+                            const float2 u1 =
+                                __ffma2_rn(make_float2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
+                                           make_float2(d[i].z, d[i].w), make_float2(e[i].z, e[i].w));
                             const int    a0 = 8 * h + 2 * i;
-                            acc[a0]     = __ffma2_rn(s0, __fmul2_rn(dw2, make_float2(d[i].x, d[i].y)), acc[a0]);
-                            acc[a0 + 1] = __ffma2_rn(s1, __fmul2_rn(dw2, make_float2(d[i].z, d[i].w)), acc[a0 + 1]);
+                            acc[a0]     = __ffma2_rn(u0, dw2, acc[a0]);
+                            acc[a0 + 1] = __ffma2_rn(u1, dw2, acc[a0 + 1]);
                         }
                     }
                     // back to the bias; handed back at the next block (or below)
@@ -463,7 +471,8 @@ __global__ void __launch_bounds__(256) tc_repack_weights_kernel(const uint8_t * 
 template <int MODE>
 __global__ void __launch_bounds__(256) tc_stage_acts_kernel(const float * __restrict__ x, size_t x_stride, int K,
                                                             int M, uint8_t * __restrict__ codes,
-                                                            float * __restrict__ scales, int pitch) {
+                                                            float * __restrict__ scales, float * __restrict__ nbscales,
+                                                            int pitch) {
     const int     warp  = threadIdx.x >> 5;
     const int     lane  = threadIdx.x & 31;
     const int     g     = lane & 7;
@@ -490,7 +499,8 @@ __global__ void __launch_bounds__(256) tc_stage_acts_kernel(const float * __rest
             const int blk = half * 4 + (lane >> 3);
             *reinterpret_cast<uint32_t *>(codes + (size_t) m * K + (size_t) c * 256 + half * 128 + 4 * lane) = wv;
             if (g == 0) {
-                scales[(size_t) (c * 8 + blk) * pitch + m] = p.d;
+                scales[(size_t) (c * 8 + blk) * pitch + m]   = p.d;
+                nbscales[(size_t) (c * 8 + blk) * pitch + m] = -12582912.0f * p.d;  // exact: see the top
             }
         }
     }
@@ -501,6 +511,7 @@ struct TcPlanes {
     float *   wd;
     uint8_t * xc;
     float *   xd;
+    float *   xn;  // -1.5 * 2^23 * xd
     int       pitch_n, pitch_m;
     size_t    bytes;
 };
@@ -522,6 +533,8 @@ TcPlanes tc_planes(void * ws, int64_t K, int64_t N, int64_t M) {
     p.xc = base + off;
     off += tc_align((size_t) M * (size_t) K);
     p.xd = reinterpret_cast<float *>(base + off);
+    off += tc_align((size_t) (K / 32) * (size_t) p.pitch_m * 4);
+    p.xn = reinterpret_cast<float *>(base + off);
     off += tc_align((size_t) (K / 32) * (size_t) p.pitch_m * 4);
     p.bytes = off;
     return p;
@@ -597,24 +610,25 @@ cudaError_t launch_gemm_tc(const uint8_t * w, size_t row_bytes, int64_t K, int64
     switch (mode) {
         case B200Q8_QUANT_REF:
             tc_stage_acts_kernel<B200Q8_QUANT_REF>
-                <<<ga, 256, 0, stream>>>(x, x_stride, (int) K, (int) M, p.xc, p.xd, p.pitch_m);
+                <<<ga, 256, 0, stream>>>(x, x_stride, (int) K, (int) M, p.xc, p.xd, p.xn, p.pitch_m);
             break;
         case B200Q8_QUANT_CPU_X86:
             tc_stage_acts_kernel<B200Q8_QUANT_CPU_X86>
-                <<<ga, 256, 0, stream>>>(x, x_stride, (int) K, (int) M, p.xc, p.xd, p.pitch_m);
+                <<<ga, 256, 0, stream>>>(x, x_stride, (int) K, (int) M, p.xc, p.xd, p.xn, p.pitch_m);
             break;
         default:
             tc_stage_acts_kernel<B200Q8_QUANT_CPU_ARM>
-                <<<ga, 256, 0, stream>>>(x, x_stride, (int) K, (int) M, p.xc, p.xd, p.pitch_m);
+                <<<ga, 256, 0, stream>>>(x, x_stride, (int) K, (int) M, p.xc, p.xd, p.xn, p.pitch_m);
             break;
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         return e;
     }
-    CUtensorMap wc_map, xc_map, wd_map, xd_map;
+    CUtensorMap wc_map, xc_map, wd_map, xd_map, xn_map;
     if (!tc_encode_codes(&wc_map, p.wc, K, N) || !tc_encode_codes(&xc_map, p.xc, K, M) ||
-        !tc_encode_scales(&wd_map, p.wd, K, N, p.pitch_n) || !tc_encode_scales(&xd_map, p.xd, K, M, p.pitch_m)) {
+        !tc_encode_scales(&wd_map, p.wd, K, N, p.pitch_n) || !tc_encode_scales(&xd_map, p.xd, K, M, p.pitch_m) ||
+        !tc_encode_scales(&xn_map, p.xn, K, M, p.pitch_m)) {
         return cudaErrorInvalidValue;
     }
     TcArgs a   = {};
@@ -630,7 +644,7 @@ cudaError_t launch_gemm_tc(const uint8_t * w, size_t row_bytes, int64_t K, int64
         return e;
     }
     const int grid = std::max(1, std::min(a.n_tiles, sm_count));
-    gemm_tc_kernel<<<grid, kTcThreads, kTcSmem, stream>>>(a, wc_map, xc_map, wd_map, xd_map);
+    gemm_tc_kernel<<<grid, kTcThreads, kTcSmem, stream>>>(a, wc_map, xc_map, wd_map, xd_map, xn_map);
     return cudaGetLastError();
 }
 
