@@ -24,8 +24,9 @@
 //    u = fma(v, dx, -1.5 * 2^23 * dx) is (v - 1.5 * 2^23) * dx = sum * dx with
 //    one rounding, then acc = fma(u, dw, acc) -- two packed f32x2
 //    instructions per pair of outputs --
-//    and write the bias back with tcgen05.st, handing the accumulator back to
-//    the MMA thread when the next block starts.
+//    and write the bias back with tcgen05.st.  Accumulators pass between the
+//    MMA thread and the epilogue two blocks at a time (one barrier wait and
+//    one hand-back per pair), the pair going back when the next pair starts.
 // The scales change every 32 values of K, so every block's sums are rescaled
 // on the CUDA cores: the tensor pipe takes over the MMA issue and the operand
 // loads, the fp32 rescale stays where the mma.sync path has it.
@@ -50,7 +51,8 @@ constexpr int kTcRows       = 128;  // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kTcToks       = 128;  // tokens per tile (MMA N, TMEM columns per accumulator)
 constexpr int kTcKB         = 4;    // Q8_0 blocks per pipeline stage: 128 bytes of K, one swizzle row
 constexpr int kTcStages     = 5;
-constexpr int kTcBufs       = 4;    // TMEM accumulators
+constexpr int kTcBufs       = 4;    // TMEM accumulators, handed over in pairs (two blocks per hand-off)
+constexpr int kTcPairs      = kTcBufs / 2;
 constexpr int kTcTmemCols   = kTcBufs * kTcToks;  // 512: all of an SM's TMEM
 constexpr int kTcEpiWarps   = 16;   // 4 per TMEM lane quarter, 32 accumulator columns each
 constexpr int kTcEpiCols    = kTcToks * 4 / kTcEpiWarps;
@@ -184,9 +186,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t * full      = reinterpret_cast<uint64_t *>(smem);  // stage landed (TMA)
     uint64_t * empty     = full + kTcStages;                     // stage read (MMA commit + epilogue warps)
-    uint64_t * tfull     = empty + kTcStages;                    // accumulator written (MMA commit)
-    uint64_t * tempty    = tfull + kTcBufs;                      // accumulator re-biased (epilogue warps)
-    uint64_t * mma_done  = tempty + kTcBufs;                     // every MMA issued has completed
+    uint64_t * tfull     = empty + kTcStages;                    // accumulator pair written (MMA commit)
+    uint64_t * tempty    = tfull + kTcPairs;                     // accumulator pair re-biased (epilogue warps)
+    uint64_t * mma_done  = tempty + kTcPairs;                    // every MMA issued has completed
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
     int *      stop      = reinterpret_cast<int *>(tmem_slot + 1);
     // stages start on the first 1 KiB boundary after the header (swizzle atoms)
@@ -204,9 +206,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1 + kTcEpiWarps);
         }
-        for (int b = 0; b < kTcBufs; ++b) {
-            mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], kTcEpiWarps);
+        for (int p = 0; p < kTcPairs; ++p) {
+            mbar_init(&tfull[p], 1);
+            mbar_init(&tempty[p], kTcEpiWarps);
         }
         mbar_init(mma_done, 1);
         *stop = 0;
@@ -260,7 +262,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // MMA issuer: one MMA per Q8_0 block into accumulator bi % 4
+            // MMA issuer: one MMA per Q8_0 block into accumulator bi % 4; pair (bi / 2) % 2
+            // is waited for before its first block and committed after its second
             int  ci = 0, bi = 0;
             bool ok = true;
             for (int it = 0; it < my_tiles && ok; ++it) {
@@ -276,15 +279,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll 1
                     for (int j = 0; j < kTcKB; ++j, ++bi) {
                         const int b = bi % kTcBufs;
-                        if (!tc_wait(&tempty[b], (uint32_t) ((bi / kTcBufs) & 1), stop)) {
-                            if (*(volatile int *) stop == 0) fail();
-                            ok = false;
-                            break;
+                        const int p = b >> 1;
+                        if ((bi & 1) == 0) {
+                            if (!tc_wait(&tempty[p], (uint32_t) ((bi / kTcBufs) & 1), stop)) {
+                                if (*(volatile int *) stop == 0) fail();
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
                         }
-                        tc_fence_after();
                         tc_mma(tbase + (uint32_t) (b * kTcToks), tc_desc_sw128(sa + 32 * j),
                                tc_desc_sw128(sa + kTcCodeBytes + 32 * j));
-                        tc_commit(&tfull[b]);
+                        if (bi & 1) {
+                            tc_commit(&tfull[p]);
+                        }
                     }
                     if (ok) {
                         tc_commit(&empty[s]);
@@ -310,14 +318,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-            for (int b = 0; b < kTcBufs; ++b) {
-                mbar_arrive(&tempty[b]);
+            for (int p = 0; p < kTcPairs; ++p) {
+                mbar_arrive(&tempty[p]);
             }
         }
         int          ci = 0, bi = 0;
-        int          held = -1;  // accumulator re-biased (tcgen05.st issued) but not yet handed back
+        int          held = -1;  // accumulator pair re-biased (tcgen05.st issued) but not yet handed back
         bool         ok   = true;
-        // hand the held accumulator back to the MMA thread once its bias store completed
+        // hand the held pair back to the MMA thread once its bias stores completed
         auto release = [&]() {
             if (held >= 0) {
                 tc_wait_st();
@@ -350,9 +358,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const float *   xd = wd + kTcKB * 128;
                 const float *   xn = xd + kTcKB * 128;
 #pragma unroll 1
-                for (int j = 0; j < kTcKB; ++j, ++bi) {
-                    const int b = bi % kTcBufs;
-                    if (ok && !tc_wait(&tfull[b], (uint32_t) ((bi / kTcBufs) & 1), stop)) {
+                for (int j = 0; j < kTcKB; j += 2, bi += 2) {
+                    const int p = (bi % kTcBufs) >> 1;
+                    if (ok && !tc_wait(&tfull[p], (uint32_t) ((bi / kTcBufs) & 1), stop)) {
                         if (*(volatile int *) stop == 0) fail();
                         ok = false;
                     }
@@ -361,38 +369,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         continue;
                     }
                     tc_fence_after();
-                    release();  // the previous block's accumulator
-                    const float    dw  = wd[j * 128 + r];
-                    const float2   dw2 = make_float2(dw, dw);
-                    const float4 * dx  = reinterpret_cast<const float4 *>(xd + j * 128 + cg * kTcEpiCols);
-                    const float4 * dn  = reinterpret_cast<const float4 *>(xn + j * 128 + cg * kTcEpiCols);
-                    // two halves of 16 columns: the scales first, then the accumulator words
+                    release();  // the previous pair
+#pragma unroll 1
+                    for (int q2 = 0; q2 < 2; ++q2) {
+                        const int      jb  = j + q2;
+                        const int      b   = 2 * p + q2;
+                        const float    dw  = wd[jb * 128 + r];
+                        const float2   dw2 = make_float2(dw, dw);
+                        const float4 * dx  = reinterpret_cast<const float4 *>(xd + jb * 128 + cg * kTcEpiCols);
+                        const float4 * dn  = reinterpret_cast<const float4 *>(xn + jb * 128 + cg * kTcEpiCols);
+                        // two halves of 16 columns: the scales first, then the accumulator words
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float4 d[4], e[4];
+                        for (int h = 0; h < 2; ++h) {
+                            float4 d[4], e[4];
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            d[i] = dx[4 * h + i];
-                            e[i] = dn[4 * h + i];
+                            for (int i = 0; i < 4; ++i) {
+                                d[i] = dx[4 * h + i];
+                                e[i] = dn[4 * h + i];
+                            }
+                            uint32_t v[16];
+                            tc_ld16(tl + b * kTcToks + 16 * h, v);
+                            tc_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const float2 u0 = __ffma2_rn(
+                                    make_float2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
+                                    make_float2(d[i].x, d[i].y), make_float2(e[i].x, e[i].y));
+                                const float2 u1 = __ffma2_rn(
+                                    make_float2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
+                                    make_float2(d[i].z, d[i].w), make_float2(e[i].z, e[i].w));
+                                const int a0 = 8 * h + 2 * i;
+                                acc[a0]      = __ffma2_rn(u0, dw2, acc[a0]);
+                                acc[a0 + 1]  = __ffma2_rn(u1, dw2, acc[a0 + 1]);
+                            }
                         }
-                        uint32_t v[16];
-                        tc_ld16(tl + b * kTcToks + 16 * h, v);
-                        tc_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float2 u0 = __ffma2_rn(make_float2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])),
-                                                         make_float2(d[i].x, d[i].y), make_float2(e[i].x, e[i].y));
-                            const float2 u1 =
-                                __ffma2_rn(make_float2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])),
-                                           make_float2(d[i].z, d[i].w), make_float2(e[i].z, e[i].w));
-                            const int    a0 = 8 * h + 2 * i;
-                            acc[a0]     = __ffma2_rn(u0, dw2, acc[a0]);
-                            acc[a0 + 1] = __ffma2_rn(u1, dw2, acc[a0 + 1]);
-                        }
+                        // back to the bias; the pair is handed back when the next one starts (or below)
+                        tc_st32_bias(tl + b * kTcToks);
                     }
-                    // back to the bias; handed back at the next block (or below)
-                    tc_st32_bias(tl + b * kTcToks);
-                    held = b;
+                    held = p;
                 }
                 __syncwarp();
                 if (ok && lane == 0) {
