@@ -153,7 +153,10 @@ b200q8_status_t b200q8_get_rows(const void * table, int64_t K, int64_t rows, siz
 /* ---- MUL_MAT ------------------------------------------------------------ */
 
 /* Bytes of caller-provided scratch b200q8_mul_mat needs for these sizes
- * (0 when the fused decode path needs none). */
+ * (0 when the fused decode path needs none).  With B200Q8_TC_MIN_M=<M> set in
+ * the environment (read once), M >= that many tokens also count the tcgen05
+ * GEMM's planes; b200q8_mul_mat uses that GEMM only when the workspace holds
+ * them, and otherwise needs only the smaller size. */
 size_t b200q8_mul_mat_workspace_size(int64_t K, int64_t N, int64_t M);
 
 /* y = W * quantize(x): y[m][n] = sum_b fp32(dw[n,b]) * fp32(dx[m,b]) * sum_i qw*qx,
