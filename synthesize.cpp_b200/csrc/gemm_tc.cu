@@ -281,7 +281,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const int b = bi % kTcBufs;
                         const int p = b >> 1;
                         if ((bi & 1) == 0) {
-                            if (!tc_wait(&tempty[p], (uint32_t) ((bi / kTcBufs) & 1), stop)) {
+                            // the MMA thread runs ahead of the epilogue and mostly waits here: a
+                            // suspending wait leaves its SMSP's issue slots to the epilogue warps
+                            if (!mbar_wait_bounded_or_flag(&tempty[p], (uint32_t) ((bi / kTcBufs) & 1), stop)) {
                                 if (*(volatile int *) stop == 0) fail();
                                 ok = false;
                                 break;
