@@ -653,10 +653,16 @@ def run_pack(args, rank, local_rank):
     for a, d, (n, k) in zip(f32, dst_host, mats):
         q8.quantize_chunk_host(a, d, 0, n, k, device=local_rank)
     t_e2e = time.perf_counter() - t0
-    # spot parity on the largest tensor, and the CPU reference tool's rate (one thread, as ggml_quantize_chunk)
+    # parity: every tensor's bytes, from the device buffers and from the host call, against the oracle's
+    # restatement of quantize_row_q8_0_ref (OpenMP over rows); the reference tool's own entry point
+    # (ggml_quantize_chunk) on the largest tensor; then that tool's rate (one thread, as ggml_quantize_chunk)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
+    for i, (a, (n, k)) in enumerate(zip(f32, mats)):
+        ref = O.quantize_rows_mt(a.reshape(n, k)).ravel()
+        if not (np.array_equal(ref, dst_host[i]) and np.array_equal(ref, dst_dev[i].cpu().numpy().ravel())):
+            raise AssertionError(f"pack-1.7b: tensor {i} ({n} x {k}) differs from the oracle")
     n0, k0 = mats[4]
     ref, _ = O.quantize_chunk(f32[4], 0, n0, k0)
     assert np.array_equal(ref, dst_host[4]) and np.array_equal(ref, dst_dev[4].cpu().numpy().ravel())
@@ -682,6 +688,8 @@ def run_pack(args, rank, local_rank):
                 "d2h_bytes_per_step": weights * 34 // 32},
         "gpu_launches": len(mats) * args.steps,
         "clocks": clocks,
+        "parity": {"tensors_byte_equal": len(mats), "weights_checked": weights,
+                   "against": "oracle quantize_row_q8_0_ref (device buffers and host-call output)"},
         "cpu_baseline": {"value": cpu_w / cpu_t / 1e9, "unit": "Gweight/s", "cores": 1, "kind": "port",
                          "sample": f"{cpu_w} weights (first 2 layers) through the oracle's quantize_row_q8_0_ref, "
                                    "one thread like ggml_quantize_chunk"},
