@@ -614,8 +614,9 @@ b200q8_status_t b200q8_chain_create(const b200q8_chain_desc * desc, int32_t devi
             c->planes = p;
         }
         // split-K room for the ops whose row blocks leave SMs idle (o and
-        // down: N = hidden); up to 4 splits of any op of this width
-        const size_t part = 4 * (size_t) d.max_m * (size_t) std::max(H, Q);
+        // down: N = hidden); up to 4 splits of any op of this width, for the
+        // token chunks of <= 16 that split (the launcher checks the room)
+        const size_t part = 4 * (size_t) std::min<int64_t>(d.max_m, 16) * (size_t) std::max(H, Q);
         void *       q    = nullptr;
         if (e == cudaSuccess) e = cudaMalloc(&q, part * sizeof(float) + (size_t) c->sms * sizeof(unsigned));
         if (e == cudaSuccess) {
