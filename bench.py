@@ -842,6 +842,7 @@ def run_int8_peaks(args, rank, local_rank):
     L = ctypes.CDLL(build.PEAKS_LIB)
     L.b200q8p_tcgen05_check.argtypes = [ctypes.c_void_p]
     L.b200q8p_run.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]
+    L.b200q8p_tcgen05_latency.argtypes = [ctypes.c_void_p]
     out = np.empty((128, 256), np.int32)
     rc = L.b200q8p_tcgen05_check(out.ctypes.data)
     a = (np.arange(128)[:, None] % 7 - 3) * np.ones((1, 32), np.int64)
@@ -849,6 +850,15 @@ def run_int8_peaks(args, rank, local_rank):
     want = (a @ b.T).astype(np.int32)
     if rc != 0 or not np.array_equal(out, want):
         raise RuntimeError(f"tcgen05 kind::i8 check failed (rc {rc}, {int((out != want).sum())} of 32768 differ)")
+    # the round trips the tcgen05 GEMM's pipeline is built from (one CTA, SM clock cycles)
+    lat = np.zeros(6, np.int64)
+    rc = L.b200q8p_tcgen05_latency(lat.ctypes.data)
+    if rc != 0:
+        raise RuntimeError(f"tcgen05 latency probe: rc {rc}")
+    latency = {"tcgen05_ld_16_columns_and_wait": {"best": int(lat[0]), "mean": int(lat[1])},
+               "tcgen05_st_32_columns_and_wait": {"best": int(lat[2]), "mean": int(lat[3])},
+               "mma_128x128x32_issue_to_commit": int(lat[4]),
+               "mma_128x128x32_back_to_back_each": round((int(lat[5]) - int(lat[4])) / 31, 1)}
     sms = torch.cuda.get_device_properties(local_rank).multi_processor_count
     peaks, peak_kind = measured_peaks()
     sampler = ClockSampler(physical_gpu_index(local_rank))
@@ -878,8 +888,9 @@ def run_int8_peaks(args, rank, local_rank):
                    "rescale": "per 2 block-outputs: fadd2 (bias) + fmul2 (dw*dx) + ffma2; 64 int8 ops each"},
         "peaks": res,
         "tcgen05_check": "one MMA on known operands equals the exact int32 products",
+        "tcgen05_latency_cycles": latency,
         "bf16_tflops_measured": peaks.get("bf16_tflops"), "peak_source": peak_kind,
-        "gpu_launches": 3 * (max(3, args.steps) + 1) + 1,
+        "gpu_launches": 3 * (max(3, args.steps) + 1) + 3,
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

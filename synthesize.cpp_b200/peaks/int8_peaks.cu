@@ -13,6 +13,11 @@
 //    K = 32 block (bias-subtract, dw*dx, fma into the accumulator: one packed
 //    f32x2 instruction each per pair of outputs) -- the CUDA-core bound every
 //    tensor path shares, since Q8_0 scales change every 32 values of K.
+//  * tcgen05_latency_kernel (one CTA): the round trips the tcgen05 Q8_0 GEMM's
+//    pipeline is built from -- a 16-column tcgen05.ld plus its wait, a
+//    32-column tcgen05.st plus its wait, one M = 128, N = 128, K = 32 MMA from
+//    issue to its commit arriving on an mbarrier, and 32 such MMAs back to
+//    back -- in SM clock cycles.
 // tcgen05_i8_kernel also has a check mode: one MMA on known operands, the
 // accumulator read back with tcgen05.ld and compared by the caller with the
 // exact int32 products, so a timed rate is only reported for an MMA whose
@@ -61,12 +66,13 @@ __host__ __device__ constexpr uint32_t idesc_i8() {
            | ((uint32_t) (kM >> 4) << 24);// m_dim
 }
 
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate,
+                                       uint32_t idesc = idesc_i8()) {
     const uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc_i8()), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2),
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2),
         "r"(mask3)
         : "memory");
 }
@@ -231,9 +237,139 @@ __global__ void __launch_bounds__(256, 1) rescale_kernel(int iters, float seed, 
     }
 }
 
+// One CTA of 128 threads: out[0..1] = best / mean cycles of a 16-column
+// tcgen05.ld + wait (16 tries), out[2..3] the same for a 32-column
+// tcgen05.st + wait, out[4] one 128 x 128 x 32 MMA from issue to its commit
+// arriving, out[5] 32 such MMAs back to back (issue to the last commit).
+// Operands are the zeroed tiles of tcgen05_i8_kernel's layout; every TMEM
+// address stays inside the 512 columns allocated.
+__global__ void __launch_bounds__(128, 1) tcgen05_latency_kernel(long long * out, unsigned * err) {
+    __shared__ __align__(1024) uint8_t tiles[kABytes + kBBytes];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t tmem_base;
+    const int warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < kABytes + kBBytes; i += blockDim.x) {
+        tiles[i] = 0;
+    }
+    if (threadIdx.x == 0) {
+        b200q8::mbar_init(&bar, 1);
+        b200q8::fence_mbar_init();
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         b200q8::smem_addr(&tmem_base)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tb = tmem_base;
+    const uint32_t tl = tb + ((uint32_t) (32 * warp) << 16);
+    long long      best = 1LL << 60, sum = 0;
+    for (int r = 0; r < 16; ++r) {
+        uint32_t        v[16];
+        const long long t0 = clock64();
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+            : "r"(tl + 16u * (uint32_t) (r & 7)));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        uint32_t x = 0;
+        for (int i = 0; i < 16; ++i) {
+            x ^= v[i];
+        }
+        const long long t1 = clock64();
+        if (x == 0xdeadbeefu) {
+            out[7] = x;  // keeps the loads live
+        }
+        best = min(best, t1 - t0);
+        sum += t1 - t0;
+    }
+    if (threadIdx.x == 0) {
+        out[0] = best;
+        out[1] = sum / 16;
+    }
+    best = 1LL << 60;
+    sum  = 0;
+    for (int r = 0; r < 16; ++r) {
+        const uint32_t  b  = 0u;
+        const long long t0 = clock64();
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+            "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(tl + 32u * (uint32_t) (r & 7)),
+            "r"(b)
+            : "memory");
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        const long long t1 = clock64();
+        best               = min(best, t1 - t0);
+        sum += t1 - t0;
+    }
+    if (threadIdx.x == 0) {
+        out[2] = best;
+        out[3] = sum / 16;
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (threadIdx.x == 0) {
+        constexpr uint32_t idesc128 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (128 >> 3) << 17) |
+                                      ((uint32_t) (kM >> 4) << 24);
+        const uint64_t a  = smem_desc(b200q8::smem_addr(tiles));
+        const uint64_t bd = smem_desc(b200q8::smem_addr(tiles + kABytes));
+        uint32_t       ph = 0;
+        const int      ns[2] = { 1, 32 };
+        for (int q = 0; q < 2; ++q) {
+            const long long t0 = clock64();
+            for (int i = 0; i < ns[q]; ++i) {
+                mma_i8(tb + 128u * (uint32_t) (i & 3), a, bd, 0u, idesc128);
+            }
+            mma_commit(&bar);
+            bool ok = b200q8::mbar_wait_bounded(&bar, ph);
+            if (!ok) {
+                atomicExch(err, 1u);
+                ok = b200q8::mbar_wait_bounded(&bar, ph);  // once more before the TMEM is freed
+            }
+            ph ^= 1u;
+            out[4 + q] = ok ? clock64() - t0 : -1;
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tb), "r"(512));
+    }
+}
+
 }  // namespace
 
 extern "C" {
+
+// tcgen05_latency_kernel's six figures (cycles) into out_host.  Returns 0, a
+// CUDA error code, or -1 when a wait timed out.
+int b200q8p_tcgen05_latency(long long * out_host) {
+    long long * out = nullptr;
+    unsigned *  err = nullptr;
+    cudaError_t e   = cudaMalloc(&out, sizeof(long long) * 8);
+    if (e == cudaSuccess) e = cudaMalloc(&err, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(err, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(out, 0, sizeof(long long) * 8);
+    for (int rep = 0; rep < 2 && e == cudaSuccess; ++rep) {  // the second run is reported
+        tcgen05_latency_kernel<<<1, 128>>>(out, err);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    }
+    unsigned herr = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(out_host, out, sizeof(long long) * 6, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&herr, err, sizeof(unsigned), cudaMemcpyDeviceToHost);
+    cudaFree(out);
+    cudaFree(err);
+    return e != cudaSuccess ? (int) e : herr != 0 ? -1 : 0;
+}
 
 // One tcgen05 MMA on known operands; out (host, int32 [128][256]) receives
 // the accumulator.  Returns 0, or a CUDA error code, or -1 when a wait timed
