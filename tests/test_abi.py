@@ -100,6 +100,34 @@ def test_version_and_workspace(pkg):
     assert L.b200q8_mul_mat_workspace_size(33, 1, 1) == 0
 
 
+def test_workspace_counts_the_tcgen05_planes_only_when_switched_on(pkg):
+    """B200Q8_TC_MIN_M (read once per process, so checked in a fresh one) makes the workspace query add the
+    tcgen05 GEMM's planes from that M on: int8 codes of W and x, fp32 scales of both and -1.5*2^23*dx for x
+    (rows padded to 4), each plane 256-aligned.  Below that M, and without the variable, the sizes stay the mma.sync path's."""
+    import os
+    import sys
+
+    code = (
+        "import sys; sys.path.insert(0, %r); import __graft_entry__ as g; g.load_package();"
+        "from synthesize_cpp_b200 import _abi; L = _abi.lib();"
+        "print(L.b200q8_mul_mat_workspace_size(1024, 3072, 2048), L.b200q8_mul_mat_workspace_size(1024, 3072, 1023),"
+        " L.b200q8_mul_mat_workspace_size(2048, 33, 1030))"
+    ) % os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    al = lambda v: (v + 255) // 256 * 256
+    planes = lambda k, n, m: (al(n * k) + al(k // 32 * ((n + 3) // 4 * 4) * 4) + al(m * k)
+                              + 2 * al(k // 32 * ((m + 3) // 4 * 4) * 4))
+    on = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                        env=dict(os.environ, B200Q8_TC_MIN_M="1024"), check=True).stdout.split()
+    off = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         env={k: v for k, v in os.environ.items() if k != "B200Q8_TC_MIN_M"},
+                         check=True).stdout.split()
+    on, off = [int(v) for v in on], [int(v) for v in off]
+    assert on[0] == max(off[0], planes(1024, 3072, 2048))
+    assert on[0] > off[0]
+    assert on[1] == off[1]  # M below the threshold
+    assert on[2] == max(off[2], planes(2048, 33, 1030))
+
+
 def test_invalid_arguments_report_status_and_message(pkg):
     from synthesize_cpp_b200 import _abi
 
